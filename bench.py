@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Benchmark: frames/s of the B200 temporal block-sparse stem engine at 1080p with ~5%
+changed blocks, plus the tile-conv roofline fraction.
+
+Workload (one "step" = one frame of every stream on the GPU): S independent 1920x1088
+camera streams per GPU (default 16, the reference's own 16-camera M1 benchmark,
+bench/bench_m1.py:148-151), seeded synthetic content (blurred-noise background, N(0,2)
+sensor noise, moving filled rectangles tuned to ~5% changed 32 px blocks per frame),
+Sarbon-S stem widths (32/64/128) with random-init weights, fp16 caches, change threshold
+8 grey levels of mean abs diff.  Frames are pre-staged in HBM (normalised fp16, as the
+engine input); every step reads S x 12.5 MB of new frames plus the image cache, far more
+than the 126 MB L2, so no L2 flush is needed.
+
+Arms:
+  --impl b200 (default)  the CUDA engine; `value` is device-timed frames/s with inputs in
+                         HBM; `e2e` runs the same steps through the public API from pinned
+                         host uint8 BGR frames (H2D copy of every frame and a D2H read of
+                         every step's {mode, count} inside the timed region).
+  --impl reference       the reference algorithm on the host CPU (the numpy oracle that
+                         restates sarbon/sparse's engine), one stream-frame per step.
+
+Multi-GPU (torchrun): streams are independent; each rank runs its own S streams (weak
+scaling) with no collective inside the timed region; the time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "frames/s/GPU at 1080p, 5% changed blocks; stem tile-conv % of tensor/HBM roofline"
+UNIT = "frames/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--streams", type=int, default=16, help="camera streams per GPU")
+    p.add_argument("--height", type=int, default=1088)
+    p.add_argument("--width", type=int, default=1920)
+    p.add_argument("--rects", type=int, default=0, help="moving rectangles per stream (0 = auto for ~5%%)")
+    p.add_argument("--frames", type=int, default=16, help="distinct frames staged per stream")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--e2e-steps", type=int, default=200)
+    p.add_argument("--profile-steps", type=int, default=24)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=20.0)
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def auto_rects(h, w):
+    """Rectangles per stream for ~5% changed 32 px blocks (calibrated on the generator:
+    each moving 40-120 px rectangle touches ~13 blocks per frame at 8 grey levels)."""
+    return max(1, round(0.05 * (h // 32) * (w // 32) / 13))
+
+
+def pingpong(n):
+    return list(range(n)) + list(range(n - 2, 0, -1))
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return FALLBACK_PEAKS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms in the background."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def layer_flops(eng, counts, mode):
+    """Algorithmic conv FLOPs of one step: 2*cin*cout*9*t^2 per active tile per layer,
+    counted on the real active counts k_d (dense: every block)."""
+    total = 0
+    for l in eng.layers:
+        t = eng.block // l.out_stride
+        k = eng.n_blocks if mode == "dense" else counts[eng.ds.index(eng.dilation(l.radius))]
+        total += 2 * l.w_tile.shape[2] * l.w_tile.shape[3] * 9 * t * t * k
+    return total
+
+
+def gate_bytes(eng, n_changed):
+    """Gate kernel bytes: read frames and image cache (fp16), copy the changed blocks'
+    frames into the cache (re-read + write), write the change mask."""
+    px = eng.n * eng.h * eng.w * 3
+    blk = eng.block * eng.block * 3 * 2
+    return 2 * px * 2 + n_changed * 2 * blk + eng.n_blocks
+
+
+def build_net(seed):
+    from sarbon_b200 import LocalBackbone
+    torch.manual_seed(seed)
+    return LocalBackbone().eval()
+
+
+def make_frames(args, rank, dev):
+    from sarbon_b200 import scenes
+    rects = args.rects or auto_rects(args.height, args.width)
+    src = scenes.Streams(args.streams, args.height, args.width, seed=1000 * rank + args.seed + 1,
+                         n_rects=rects, device=dev)
+    u8 = torch.stack([src.next() for _ in range(args.frames)])  # [F, S, H, W, 3] RGB
+    return u8, rects
+
+
+# ----------------------------------------------------------------------------- CPU (reference algorithm)
+def oracle_for(net, n, h, w, tau):
+    from oracle import sparse_oracle as so
+    nodes = []
+    for nd in net.program()[0]:
+        d = {"kind": nd.kind, "src": list(nd.src), "dst": nd.dst, "stride": nd.stride, "radius": nd.radius,
+             "act": bool(nd.act)}
+        if nd.kind == "conv":
+            d["w"] = nd.conv.weight.detach().float().cpu().numpy()
+            d["b"] = nd.conv.bias.detach().float().cpu().numpy()
+            d["conv_stride"] = nd.conv.stride[0]
+        nodes.append(d)
+    return so.OracleEngine(so.fuse_program(nodes), n, h, w, dtype=np.float16, tau=tau)
+
+
+def cpu_run(net, frames_seq, tau, max_steps, seconds):
+    """Time the CPU oracle (the reference's algorithm) on 1 stream: reset, then one
+    stream-frame per step.  Returns (frames/s, steps, threads)."""
+    h, w = frames_seq[0].shape[1:3]
+    ora = oracle_for(net, 1, h, w, tau)
+    ora.reset(frames_seq[0])
+    ora.step(frames_seq[1 % len(frames_seq)])  # warm-up step (BLAS threads, page faults)
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_steps:
+        ora.step(frames_seq[(n + 2) % len(frames_seq)])
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return n / dt, n, os.cpu_count()
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from sarbon_b200 import scenes
+    net = build_net(args.seed)
+    u8, rects = make_frames(args, 0, "cpu")
+    seq = [scenes.normalise(u8[i, :1]).numpy() for i in pingpong(min(args.frames, 8))]
+    tau = 8 / float(scenes.STD.mean())
+    budget = max(10.0, min(150.0, 0.5 * args.steps))
+    fps, n, cores = cpu_run(net, seq, tau, args.steps, budget)
+    line = {"metric": METRIC, "value": fps, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": n,
+            "warmup": 1, "ms_per_step": 1e3 / fps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 in / f32 accumulate (numpy fp32)", "data": "synthetic",
+            "config": {"workload": f"1080p, {args.streams} streams/GPU, ~5% changed blocks",
+                       "height": args.height, "width": args.width, "streams_per_gpu": args.streams,
+                       "rects_per_stream": rects, "sample": "1 stream-frame per step"},
+            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{n} steps of 1 stream x {args.width}x{args.height} after reset "
+                                       f"(numpy oracle restating sarbon/sparse, BLAS threads = host cores)"},
+            "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU
+def run_b200(args):
+    import torch.distributed as dist
+    from sarbon_b200 import FusedSparseEngine, scenes
+    rank, world, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    tau = 8 / float(scenes.STD.mean())
+    net = build_net(args.seed).to(dev)
+    S, H, W = args.streams, args.height, args.width
+    eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev)
+    u8, rects = make_frames(args, rank, dev)
+    staged = torch.stack([scenes.normalise(u8[i]) for i in range(u8.shape[0])])  # [F,S,H,W,3] fp16
+    order = pingpong(args.frames)
+    seq = [staged[i] for i in order]
+
+    # --- statistics pass (untimed): modes, changed and active counts over one cycle
+    eng.reset(seq[0])
+    modes, changed, act = {"skip": 0, "sparse": 0, "dense": 0}, [], []
+    for f in seq[1:] + seq[:1]:
+        mode, k = eng.step(f)
+        modes[mode] += 1
+        changed.append(int(eng.changed.sum().item()))
+        act.append(list(eng.device_stats().counts)[:len(eng.ds)])
+    nb = eng.n_blocks
+    changed_frac = statistics.mean(changed) / nb
+    act_frac = [statistics.mean(a[i] for a in act) / nb for i in range(len(eng.ds))]
+
+    # --- timed region: K steps, no host sync, frames already in HBM
+    eng.reset(seq[0])
+    for i in range(args.warmup):
+        eng.step_async(seq[(1 + i) % len(seq)])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    start.record()
+    base = 1 + args.warmup
+    for i in range(args.steps):
+        eng.step_async(seq[(base + i) % len(seq)])
+    end.record()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    launches = eng.launch_count() * args.steps
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = t.item()
+    st = eng.device_stats()
+    if st.error:
+        raise RuntimeError(f"device error flags {st.error} after the timed region")
+
+    # --- per-kernel roofline pass (events around every launch; separate from the timing)
+    prof = {"gate": 0.0, "lists": 0.0, "copy": 0.0, "conv": 0.0, "finalize": 0.0}
+    conv_flops, gbytes, nprof = 0, 0, 0
+    eng.reset(seq[0])
+    for i in range(args.profile_steps):
+        f = seq[1 + i % (len(seq) - 1)]
+        mode, k, kms = eng.step_profiled(f)
+        counts = list(eng.device_stats().counts)[:len(eng.ds)]
+        prof["gate"] += kms[0]
+        prof["lists"] += kms[1]
+        prof["copy"] += kms[2]
+        prof["conv"] += sum(kms[3:3 + len(eng.layers)])
+        prof["finalize"] += kms[3 + len(eng.layers)]
+        conv_flops += layer_flops(eng, counts, mode) if mode != "skip" else 0
+        gbytes += gate_bytes(eng, int(eng.changed.sum().item()))
+        nprof += 1
+    peaks, src = load_peaks()
+    n_conv = nprof * len(eng.layers)
+    conv_tflops = conv_flops / (prof["conv"] * 1e-3) / 1e12
+    gate_gbs = gbytes / (prof["gate"] * 1e-3) / 1e9
+    roof = {"bound": "tensor", "kernel": "sb::conv_tc_kernel (tile conv, all 11 layers)",
+            "achieved": conv_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+            "frac": conv_tflops / peaks["bf16_tflops_sustained"],
+            "traffic": None, "peak_source": f"{src} bf16_tflops_sustained (fp16 dense = bf16 rate)",
+            "flops_per_launch": conv_flops / n_conv, "ms_per_launch": prof["conv"] / n_conv}
+    roof_gate = {"bound": "hbm", "kernel": "sb::gate_kernel<0>", "achieved": gate_gbs, "peak": peaks["hbm_gbs"],
+                 "unit": "GB/s", "frac": gate_gbs / peaks["hbm_gbs"], "bytes_per_launch": gbytes / nprof,
+                 "ms_per_launch": prof["gate"] / nprof}
+    share = {k: v / sum(prof.values()) for k, v in prof.items()}
+
+    # --- e2e through the public API from pinned host uint8 BGR frames
+    e2e = None
+    if not args.no_e2e:
+        ne = min(args.frames, 8)
+        host = [u8[i].flip(-1).contiguous().cpu().pin_memory() for i in range(ne)]
+        eorder = [host[i] for i in pingpong(ne)]
+        dbuf = [torch.empty_like(host[0], device=dev) for _ in range(2)]
+        res_dev = eng.result_view()
+        ring = torch.zeros(args.e2e_steps, 2, dtype=torch.int64).pin_memory()
+        copy_s = torch.cuda.Stream(dev)
+        up = [torch.cuda.Event() for _ in range(2)]
+        done = [torch.cuda.Event() for _ in range(2)]
+        eng.reset(scenes.normalise(u8[0]))
+        for i in range(3):
+            eng.step_u8(dbuf[0].copy_(eorder[(1 + i) % len(eorder)]), scenes.MEAN, scenes.STD, sync=True)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream(dev)
+        e0.record()
+        for i in range(args.e2e_steps):
+            b = i % 2
+            with torch.cuda.stream(copy_s):
+                if i >= 2:
+                    copy_s.wait_event(done[b])
+                dbuf[b].copy_(eorder[(4 + i) % len(eorder)], non_blocking=True)
+                up[b].record(copy_s)
+            cur.wait_event(up[b])
+            eng.step_u8(dbuf[b], scenes.MEAN, scenes.STD, sync=False)
+            done[b].record(cur)
+            ring[i].copy_(res_dev, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1)
+        te = torch.tensor([ems], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * S * args.e2e_steps / (te.item() * 1e-3), "unit": UNIT,
+               "h2d_bytes_per_step": int(host[0].numel()), "d2h_bytes_per_step": 16,
+               "steps": args.e2e_steps, "input": "pinned host uint8 BGR, normalisation fused into the gate",
+               "modes_seen": sorted({int(m) for m in ring[:, 0].tolist()})}
+
+    # --- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cseq = [scenes.normalise(u8[i, :1]).cpu().numpy() for i in pingpong(min(args.frames, 8))]
+        fps, n, cores = cpu_run(net.cpu(), cseq, tau, 64, args.cpu_seconds)
+        cpu = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{n} steps of 1 stream x {W}x{H} (numpy oracle restating sarbon/sparse; "
+                         f"BLAS threads = host cores)"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = world * S * args.steps / (ms_max * 1e-3)
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+            "data": "synthetic (seeded moving-rectangle camera streams, random-init Sarbon-S stem)",
+            "config": {"workload": f"1080p x {S} streams/GPU, ~5% changed blocks",
+                       "height": H, "width": W, "block": 32, "streams_per_gpu": S, "rects_per_stream": rects,
+                       "tau_grey_levels": 8, "frames_staged": args.frames,
+                       "changed_block_frac": changed_frac,
+                       "active_block_frac": {f"d{d}": a for d, a in zip(eng.ds, act_frac)},
+                       "modes_cycle": modes, "per_gpu_fps": S * args.steps / (ms_max * 1e-3),
+                       "l2": f"no flush: each step reads {S * H * W * 6 / 1e6:.0f} MB of new frames + "
+                             f"the image cache (> 126 MB L2)"},
+            "roofline": roof, "roofline_gate": roof_gate, "kernel_time_share": share,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clock_info}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

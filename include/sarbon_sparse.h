@@ -1,0 +1,179 @@
+/*
+ * sarbon_sparse.h -- C ABI of the B200 temporal block-sparse stem engine.
+ *
+ * One engine serves N camera streams of H x W pixels on one GPU.  Per step it
+ *   1. gates every block x block tile of the new frames against the cached image
+ *      (exact per-block sum of |fp16 diff|, threshold, OR extra mask, refresh phase),
+ *   2. dilates the change mask per receptive-field dilation and compacts the active
+ *      blocks into ordered (cam, by, bx) lists,
+ *   3. recomputes only the active tiles of the 3x3 conv stem (tcgen05 tensor cores
+ *      for fp16, CUDA cores for fp32), fused with bias, residual add and ReLU,
+ *      writing straight into the NHWC feature caches,
+ *   4. falls back to a dense pass above a calibrated active-block count.
+ *
+ * Conventions: plain C types only, an opaque engine handle, int status codes,
+ * no exceptions.  Device pointers are raw CUDA device addresses on the engine's
+ * GPU; `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * Caches and block lists are engine-owned device memory, valid until
+ * sb_destroy().  Calls on one engine are serial (one host thread at a time).
+ *
+ * Reference interface replaced (Bahrombekk/Sarbon, sarbon/sparse/fused_engine.py):
+ * the functions below mirror FusedSparseEngine, see each declaration.
+ */
+#ifndef SARBON_SPARSE_H
+#define SARBON_SPARSE_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SB_API __attribute__((visibility("default")))
+#else
+#define SB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define SB_OK         0
+#define SB_EINVAL     1   /* bad argument (shape, id, dtype, topology) */
+#define SB_EOVERFLOW  2   /* active count above capacity: dense refresh needed */
+#define SB_ETIMEOUT   3   /* a bounded device-side wait gave up */
+#define SB_ECUDA      4   /* a CUDA runtime/driver call failed */
+#define SB_ENOMEM     5   /* device or pinned allocation failed */
+
+/* cache element types (fused_engine.py:55-56 `dtype`) */
+#define SB_F16 0
+#define SB_F32 1
+
+/* step modes (fused_engine.py:230-237) */
+#define SB_MODE_SKIP   0
+#define SB_MODE_SPARSE 1
+#define SB_MODE_DENSE  2
+
+#define SB_MAX_LAYERS 32
+#define SB_MAX_DILATIONS 4
+
+typedef struct sb_engine sb_engine;
+
+/* One fused conv(+add) of the stem (fused_engine.py:29-41, built by _fuse :99-119).
+ * Cache ids: 0 is the image cache; cache id i+1 is the output of layer i. */
+typedef struct sb_layer_desc {
+    int32_t src;         /* input cache id */
+    int32_t res;         /* residual cache id, or -1 */
+    int32_t cin, cout;   /* channels */
+    int32_t stride;      /* conv stride (1 or 2), kernel 3x3, padding 1 */
+    int32_t out_stride;  /* output feature stride w.r.t. the image */
+    int32_t radius;      /* receptive radius in image pixels (dilation = ceil(radius/block)) */
+    int32_t act;         /* 1 = ReLU */
+} sb_layer_desc;
+
+typedef struct sb_stats_t {
+    int64_t skip, sparse, dense;   /* fused_engine.py:92 `stats` */
+    int64_t last_count;            /* k of the last step (-1: hysteresis dense) */
+    int32_t last_mode;
+    int32_t error;                 /* sticky device error flags (0 = none) */
+    int32_t counts[SB_MAX_DILATIONS]; /* active blocks per dilation of the last gated step */
+    int32_t n_dilations;
+    int32_t dilations[SB_MAX_DILATIONS];
+} sb_stats_t;
+
+/* FusedSparseEngine.__init__ (fused_engine.py:55-92).  `tau` is in frame units
+ * per pixel-channel (threshold = float32(tau*block*block*3), :144); `refresh` 0
+ * disables the round-robin refresh (:145-147).  Allocates the NHWC caches
+ * (zeroed), lists, masks and device state on the current CUDA device. */
+SB_API int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width,
+              int block, int dtype, double tau, int refresh, int dense_check_every,
+              sb_engine** out);
+
+/* Layer weights from host memory: w float32 [3][3][cin][cout] (the Triton kernel's
+ * w_tile layout, fused_engine.py:114) and bias float32 [cout] (:116). */
+SB_API int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias);
+
+/* FusedSparseEngine.reset (fused_engine.py:207-212): dense pass from fp16/fp32
+ * frames [N][H][W][3] (engine dtype, device memory); clears hysteresis. */
+SB_API int sb_reset(sb_engine* e, const void* frames_dev, void* stream);
+
+/* Dense pass without touching the hysteresis state (the reference's
+ * `dense_graph.replay()`, fused_engine.py:88,172-185). */
+SB_API int sb_dense(sb_engine* e, const void* frames_dev, void* stream);
+
+/* FusedSparseEngine.step (fused_engine.py:214-240) on frames [N][H][W][3] in the
+ * engine dtype.  Skip/sparse/dense and hysteresis are decided on the device, so
+ * the call is asynchronous; when mode_out or count_out is non-NULL it synchronises
+ * `stream` and returns the mode (SB_MODE_*) and the active count (-1 for a
+ * hysteresis dense step). */
+SB_API int sb_step(sb_engine* e, const void* frames_dev, void* stream, int* mode_out, int64_t* count_out);
+
+/* The same step on uint8 BGR frames [N][H][W][3] with the caller's normalisation
+ * fused into the gate (sarbon/inference/video.py:74-99, `_prep`: BGR->RGB,
+ * (x - mean[c]) / std[c] in fp32, rounded to fp16).  fp16 engines only. */
+SB_API int sb_step_u8(sb_engine* e, const uint8_t* frames_dev, const float mean[3], const float std_[3],
+               void* stream, int* mode_out, int64_t* count_out);
+
+/* sb_step with a CUDA event before and after every kernel it launches (gate, lists,
+ * dense copy, one conv per layer, finalize); synchronises `stream` and writes the
+ * duration of each launch in ms to kernel_ms[0..*n_kernels).  Measurement aid with
+ * no counterpart in the reference (which has no per-kernel timing). */
+SB_API int sb_step_profiled(sb_engine* e, const void* frames_dev, void* stream, float* kernel_ms, int capacity,
+                            int* n_kernels);
+
+/* Device address of two int64 {mode, count} the last step's finalize kernel wrote;
+ * lets a caller copy each step's result to the host asynchronously.  No counterpart
+ * in the reference (its step returns them after a host sync, fused_engine.py:228-240). */
+SB_API int sb_result_ptr(sb_engine* e, const int64_t** dev_ptr);
+
+/* Mode and count of the last step (synchronises `stream`). */
+SB_API int sb_query(sb_engine* e, void* stream, int* mode_out, int64_t* count_out);
+
+/* FusedSparseEngine.set_extra (fused_engine.py:201-205): uint8 [N][Hb][Wb] device
+ * mask of blocks recomputed regardless of pixel change (copied on `stream`). */
+SB_API int sb_set_extra(sb_engine* e, const uint8_t* mask_dev, void* stream);
+
+/* Set the dense-fallback crossover (fused_engine.py:89, written by calibrate
+ * :242-275) and the hysteresis period (:91). */
+SB_API int sb_set_fallback(sb_engine* e, int64_t fallback, void* stream);
+SB_API int sb_set_dense_check_every(sb_engine* e, int n, void* stream);
+
+/* Calibration support (fused_engine.py:261-264): run the conv sequence over
+ * exactly `n_tiles` entries of the current block lists (entries past the active
+ * count recompute block 0, like nonzero_static's fill_value=0), updating the
+ * image cache from `frames_dev` where `changed` is set. */
+SB_API int sb_run_sparse_forced(sb_engine* e, const void* frames_dev, int64_t n_tiles, void* stream);
+
+/* Cache views (fused_engine.py:67-71,124-125): device pointer and NHWC shape of
+ * cache id (0 = image, i+1 = layer i output). */
+SB_API int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]);
+
+/* Gate buffers (uint8 device pointers, engine-owned): `changed` [N][Hb][Wb], masks
+ * [n_dil][N][Hb][Wb] (fused_engine.py:74-77) and the `extra` mask [N][Hb][Wb] the
+ * next step ORs into the change mask (writing it directly equals sb_set_extra). */
+SB_API int sb_gate_buffers(sb_engine* e, uint8_t** changed, uint8_t** masks, uint8_t** extra, int* n_dilations,
+                    int dilations[SB_MAX_DILATIONS]);
+
+/* Per-dilation block lists of the last gated step (fused_engine.py:161-165): int32
+ * device pointers to cam, by, bx (capacity N*Hb*Wb, ascending flat block order) and,
+ * when `count` is non-NULL, the number of valid entries (synchronises `stream`). */
+SB_API int sb_debug_lists(sb_engine* e, int d_index, int32_t** cam, int32_t** by, int32_t** bx,
+                   int64_t* count, void* stream);
+
+/* Counters (fused_engine.py:92,239) and sticky device errors (synchronises). */
+SB_API int sb_stats(sb_engine* e, void* stream, sb_stats_t* out);
+
+/* Number of CUDA kernels the last sb_step / sb_step_u8 / sb_reset launched. */
+SB_API int sb_last_launch_count(sb_engine* e);
+
+SB_API int sb_destroy(sb_engine* e);
+
+/* Human-readable text of the last error on this thread (never NULL). */
+SB_API const char* sb_last_error(void);
+
+/* Library build tag, e.g. "sarbon_b200 sm_100a". */
+SB_API const char* sb_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SARBON_SPARSE_H */

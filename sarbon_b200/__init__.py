@@ -1,0 +1,17 @@
+"""sarbon_b200: B200-native temporal block-sparse stem engine for Sarbon.
+
+Public API (mirrors ``sarbon.sparse``):
+
+* :class:`FusedSparseEngine` -- the engine (CUDA library ``libsarbon_sparse.so``).
+* :class:`LocalBackbone`, :func:`stem_to_local`, :func:`fold` -- stem topology and BN folding.
+* :func:`budget_buckets` -- the reference's budget schedule.
+
+Importing the package does not load the CUDA library; constructing an engine does, and
+raises :class:`SarbonLibraryError` when it is missing.
+"""
+from ._lib import SarbonLibraryError
+from .fused_engine import FusedSparseEngine, budget_buckets, fuse_layers
+from .local import LocalBackbone, Node, fold, stem_to_local
+
+__all__ = ["FusedSparseEngine", "LocalBackbone", "Node", "SarbonLibraryError", "budget_buckets", "fold",
+           "fuse_layers", "stem_to_local"]

@@ -1,0 +1,100 @@
+"""ctypes binding of ``libsarbon_sparse.so`` (C ABI declared in ``include/sarbon_sparse.h``).
+
+There is no fallback: if the library is missing or cannot be loaded, every entry point
+raises ``SarbonLibraryError``.  Build it with ``python -m sarbon_b200.build_lib``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libsarbon_sparse.so"
+
+SB_OK, SB_EINVAL, SB_EOVERFLOW, SB_ETIMEOUT, SB_ECUDA, SB_ENOMEM = range(6)
+SB_F16, SB_F32 = 0, 1
+SB_MODE_SKIP, SB_MODE_SPARSE, SB_MODE_DENSE = 0, 1, 2
+MODE_NAMES = ("skip", "sparse", "dense")
+SB_MAX_LAYERS = 32
+SB_MAX_DILATIONS = 4
+
+STATUS_NAMES = {SB_OK: "SB_OK", SB_EINVAL: "SB_EINVAL", SB_EOVERFLOW: "SB_EOVERFLOW",
+                SB_ETIMEOUT: "SB_ETIMEOUT", SB_ECUDA: "SB_ECUDA", SB_ENOMEM: "SB_ENOMEM"}
+
+
+class SarbonLibraryError(RuntimeError):
+    """The CUDA library is missing, failed to load, or a call returned an error status."""
+
+    def __init__(self, msg, status=None):
+        super().__init__(msg)
+        self.status = status
+
+
+class LayerDesc(C.Structure):
+    _fields_ = [("src", C.c_int32), ("res", C.c_int32), ("cin", C.c_int32), ("cout", C.c_int32),
+                ("stride", C.c_int32), ("out_stride", C.c_int32), ("radius", C.c_int32),
+                ("act", C.c_int32)]
+
+
+class Stats(C.Structure):
+    _fields_ = [("skip", C.c_int64), ("sparse", C.c_int64), ("dense", C.c_int64),
+                ("last_count", C.c_int64), ("last_mode", C.c_int32), ("error", C.c_int32),
+                ("counts", C.c_int32 * SB_MAX_DILATIONS), ("n_dilations", C.c_int32),
+                ("dilations", C.c_int32 * SB_MAX_DILATIONS)]
+
+
+_P = C.c_void_p
+_I = C.c_int
+_I64 = C.c_int64
+# name -> (restype, argtypes); every symbol declared in include/sarbon_sparse.h
+PROTOTYPES = {
+    "sb_create": (_I, [C.POINTER(LayerDesc), _I, _I, _I, _I, _I, _I, C.c_double, _I, _I, C.POINTER(_P)]),
+    "sb_upload_weights": (_I, [_P, _I, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
+    "sb_reset": (_I, [_P, _P, _P]),
+    "sb_dense": (_I, [_P, _P, _P]),
+    "sb_step": (_I, [_P, _P, _P, C.POINTER(_I), C.POINTER(_I64)]),
+    "sb_step_u8": (_I, [_P, _P, C.POINTER(C.c_float), C.POINTER(C.c_float), _P, C.POINTER(_I),
+                        C.POINTER(_I64)]),
+    "sb_query": (_I, [_P, _P, C.POINTER(_I), C.POINTER(_I64)]),
+    "sb_step_profiled": (_I, [_P, _P, _P, C.POINTER(C.c_float), _I, C.POINTER(_I)]),
+    "sb_result_ptr": (_I, [_P, C.POINTER(_P)]),
+    "sb_set_extra": (_I, [_P, _P, _P]),
+    "sb_set_fallback": (_I, [_P, _I64, _P]),
+    "sb_set_dense_check_every": (_I, [_P, _I, _P]),
+    "sb_run_sparse_forced": (_I, [_P, _P, _I64, _P]),
+    "sb_cache_ptr": (_I, [_P, _I, C.POINTER(_P), C.POINTER(_I64)]),
+    "sb_gate_buffers": (_I, [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_I), C.POINTER(_I)]),
+    "sb_debug_lists": (_I, [_P, _I, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_I64), _P]),
+    "sb_stats": (_I, [_P, _P, C.POINTER(Stats)]),
+    "sb_last_launch_count": (_I, [_P]),
+    "sb_destroy": (_I, [_P]),
+    "sb_last_error": (C.c_char_p, []),
+    "sb_version": (C.c_char_p, []),
+}
+
+_lib = None
+
+
+def lib():
+    """Load the library once; raise SarbonLibraryError if it is absent or incomplete."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise SarbonLibraryError(f"{LIB_PATH} not found: build it with `python -m sarbon_b200.build_lib`")
+        try:
+            h = C.CDLL(str(LIB_PATH))
+        except OSError as e:
+            raise SarbonLibraryError(f"cannot load {LIB_PATH}: {e}") from e
+        for name, (res, args) in PROTOTYPES.items():
+            try:
+                fn = getattr(h, name)
+            except AttributeError as e:
+                raise SarbonLibraryError(f"{LIB_PATH} does not export {name}") from e
+            fn.restype, fn.argtypes = res, args
+        _lib = h
+    return _lib
+
+
+def check(status, what=""):
+    if status != SB_OK:
+        msg = lib().sb_last_error().decode(errors="replace")
+        raise SarbonLibraryError(f"{what}: {STATUS_NAMES.get(status, status)}: {msg}", status)

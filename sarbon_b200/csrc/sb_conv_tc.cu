@@ -1,0 +1,521 @@
+// sb_conv_tc.cu -- fused gather -> 3x3 conv -> bias -> (+residual) -> ReLU -> scatter on
+// the sm_100a tensor cores (tcgen05.mma, fp16 inputs, fp32 accumulators in TMEM).
+//
+// Reference: Bahrombekk/Sarbon sarbon/sparse/triton_conv.py:15-86 (`_tile_conv_kernel`,
+// `tile_conv`): one implicit GEMM per active tile list, M = tiles * t^2 output pixels,
+// N = C_out, K = 9 * C_in, input windows read straight from the NHWC cache with zero
+// padding only at the image border, epilogue writing straight into the output cache.
+//
+// B200 design (not a translation of the Triton kernel):
+//   * persistent CTAs (one per SM) loop over 128-pixel M-tiles of the active-tile list;
+//     the list length and the skip/sparse/dense mode are read from device memory, so the
+//     launch needs no host sync;
+//   * the whole weight matrix of the CTA's C_out slice stays resident in shared memory
+//     (one bulk copy of a pre-swizzled image per CTA);
+//   * the im2col A operand of each (tap, 64-channel chunk) is fetched by TMA: one
+//     4-D tiled box per tile, [chunk][t px][t rows][cam] with element strides = conv
+//     stride, so the hardware does the strided gather and the image-border zero fill;
+//   * one elected thread issues tcgen05.mma (M=128, N=C_out slice, K=16 steps) from the
+//     swizzled smem stages into a double-buffered TMEM accumulator;
+//   * four epilogue warps read TMEM (tcgen05.ld 32x32b), add bias and residual, apply
+//     ReLU and store 16-byte vectors into the destination cache while the next M-tile's
+//     MMAs run.
+//   * the 3-channel first layer cannot be fetched by TMA (6-byte pixels); its A rows
+//     (27 taps x channels, zero-padded to K=32) are gathered by four producer warps.
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "sb_internal.cuh"
+#include "sb_ptx.cuh"
+
+namespace sb {
+
+constexpr int kMaxSmem = 232448;  // 227 KB opt-in shared memory per CTA on sm_100
+
+template <int CIN, int NCTA, int T, int S>
+struct TcCfg {
+  static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
+  static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
+  static constexpr int CH = MANUAL ? KPAD : (CIN % 64 == 0 ? 64 : 32);  // K elements per K-block
+  static constexpr int NCH = MANUAL ? 1 : CIN / CH;
+  static constexpr int NKB = MANUAL ? 1 : 9 * NCH;    // K-blocks per M-tile
+  static constexpr int ROWB = CH * 2;                 // bytes per operand row
+  static constexpr int SWZ = ROWB == 128 ? 2 : 4;     // 128B / 64B swizzle
+  static constexpr int SBO = 8 * ROWB;
+  static constexpr int TT = T * T;
+  static constexpr int TPM = TT >= 128 ? 1 : 128 / TT;  // tiles per M-tile
+  static constexpr int MPT = TT >= 128 ? TT / 128 : 1;  // M-tiles per tile
+  static constexpr int BOX_ROWS = TT >= 128 ? 128 / T : T;
+  static constexpr int BOX_BYTES = T * BOX_ROWS * ROWB;
+  static constexpr int A_STAGE = 128 * ROWB;
+  static constexpr int B_KB = NCTA * ROWB;
+  static constexpr int W_BYTES = NKB * B_KB;
+  static constexpr int TMEM_COLS = (2 * NCTA) <= 32 ? 32 : (2 * NCTA) <= 64 ? 64 : (2 * NCTA) <= 128 ? 128 : (2 * NCTA) <= 256 ? 256 : 512;
+  static constexpr int W_OFF = 0;
+  static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
+  static constexpr int FIXED = 1024 /*align slack*/ + NCTA * 4 + 256 /*barriers*/;
+  static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int SMEM = FIXED + A_OFF + STAGES * A_STAGE;
+  static constexpr int THREADS = MANUAL ? 320 : 192;   // 4 epilogue + producer + MMA (+4 gather)
+  static constexpr uint32_t IDESC = idesc_f16(128, NCTA);
+  static_assert(STAGES >= 2, "shared memory too small for two stages");
+  static_assert(NCTA % 16 == 0 && NCTA >= 16 && NCTA <= 256, "UMMA N");
+  static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
+};
+
+struct TileXY {
+  int cam, by, bx;
+};
+
+// Active-tile i of this layer: dense -> every block in flat order; sparse -> the
+// block list (entries past the listed count are block 0, as nonzero_static pads).
+SB_DEV TileXY tile_at(const ConvArgs& a, int mode, int listed, int i) {
+  TileXY r{0, 0, 0};
+  if (mode == SB_MODE_DENSE) {
+    const int per = a.hb * a.wb;
+    r.cam = i / per;
+    const int q = i - r.cam * per;
+    r.by = q / a.wb;
+    r.bx = q - r.by * a.wb;
+  } else if (i < listed) {
+    r.cam = __ldg(a.lcam + i);
+    r.by = __ldg(a.lby + i);
+    r.bx = __ldg(a.lbx + i);
+  }
+  return r;
+}
+
+template <int CIN, int NCTA, int T, int S>
+__global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
+    conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmap) {
+  using C = TcCfg<CIN, NCTA, T, S>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sW = smem + C::W_OFF;
+  uint8_t* sA = smem + C::A_OFF;
+  float* sBias = reinterpret_cast<float*>(sA + C::STAGES * C::A_STAGE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sBias + NCTA);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + C::STAGES;
+  uint64_t* accf = bars + 2 * C::STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* wbar = acce + 2;
+  uint64_t* dbar = wbar + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(dbar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int n0 = blockIdx.y * NCTA;  // output-channel slice of this CTA
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::STAGES; ++i) {
+      mbar_init(&full[i], C::MANUAL ? 128 : 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], 128);
+    }
+    mbar_init(wbar, 1);
+    mbar_init(dbar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  for (int i = threadIdx.x; i < NCTA; i += blockDim.x) sBias[i] = a.bias[n0 + i];
+  if (!C::MANUAL && warp == 4 && lane == 0) prefetch_tmap(&tmap);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  // work of this launch, decided on the device (no host sync)
+  const int mode = a.st->mode_cur;
+  const int listed = a.st->counts[a.d_idx];
+  int n_tiles = 0;
+  if (mode == SB_MODE_DENSE) n_tiles = a.n_blocks;
+  else if (mode == SB_MODE_SPARSE) n_tiles = a.st->force_tiles > 0 ? a.st->force_tiles : listed;
+  if (n_tiles > a.n_blocks && mode != SB_MODE_DENSE) n_tiles = a.n_blocks;
+  const int n_mtiles = C::TT >= 128 ? n_tiles * C::MPT : (n_tiles + C::TPM - 1) / C::TPM;
+  const int my_tiles = (int)blockIdx.x < n_mtiles ? (n_mtiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+
+  if (my_tiles > 0) {
+    if (warp == 4 && lane == 0) {
+      // ------------------------------------------------ producer: weights, then A stages
+      const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)blockIdx.y * C::W_BYTES;
+      mbar_arrive_expect_tx(wbar, C::W_BYTES);
+      for (int off = 0; off < C::W_BYTES; off += 32768) {
+        const int len = C::W_BYTES - off < 32768 ? C::W_BYTES - off : 32768;
+        bulk_load(sW + off, wsrc + off, len, wbar);
+      }
+      if (!C::MANUAL) {
+        uint32_t g = 0;
+        for (int it = 0; it < my_tiles && !*abort_flag; ++it) {
+          const int m = blockIdx.x + it * gridDim.x;
+          int cam[C::TPM], y0[C::TPM], x0[C::TPM];
+#pragma unroll
+          for (int j = 0; j < C::TPM; ++j) {
+            int ti, sub;
+            if (C::TT >= 128) { ti = m / C::MPT; sub = m % C::MPT; }
+            else { ti = m * C::TPM + j; sub = 0; }
+            const TileXY p = tile_at(a, mode, listed, ti < n_tiles ? ti : 0);
+            cam[j] = p.cam;
+            y0[j] = (p.by * T + sub * C::BOX_ROWS) * S - 1;
+            x0[j] = p.bx * T * S - 1;
+          }
+          for (int kb = 0; kb < C::NKB; ++kb, ++g) {
+            const int tap = kb / C::NCH, ch = kb % C::NCH;
+            const int ky = tap / 3, kx = tap % 3;
+            const int s = g % C::STAGES;
+            const uint32_t ph = (g / C::STAGES) & 1u;
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+              atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], C::A_STAGE);
+            uint8_t* dst = sA + s * C::A_STAGE;
+#pragma unroll
+            for (int j = 0; j < C::TPM; ++j)
+              tma_load_4d(dst + j * C::BOX_BYTES, &tmap, &full[s], ch * C::CH, x0[j] + kx, y0[j] + ky, cam[j]);
+          }
+        }
+        // drain: every issued A load has landed before the CTA may exit
+        const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0u;
+        for (uint32_t q = first; q < g; ++q) {
+          volatile int never = 0;
+          mbar_wait(&full[q % C::STAGES], (q / C::STAGES) & 1u, &never);
+        }
+      }
+    } else if (C::MANUAL && warp >= 6) {
+      // ------------------------------------------------ gather producers (first layer)
+      const int r = threadIdx.x - 192;  // A row = output pixel slot, 0..127
+      const __half* x = static_cast<const __half*>(a.x);
+      uint32_t g = 0;
+      for (int it = 0; it < my_tiles && !*abort_flag; ++it, ++g) {
+        const int m = blockIdx.x + it * gridDim.x;
+        int ti, p;
+        if (C::TT >= 128) { ti = m / C::MPT; p = (m % C::MPT) * 128 + r; }
+        else { ti = m * C::TPM + r / C::TT; p = r % C::TT; }
+        const TileXY tc = tile_at(a, mode, listed, ti < n_tiles ? ti : 0);
+        const int gy = tc.by * T + p / T, gx = tc.bx * T + p % T;
+        const int s = g % C::STAGES;
+        const uint32_t ph = (g / C::STAGES) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+          atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
+          *abort_flag = 1;
+          break;
+        }
+        uint16_t v[C::KPAD > 0 ? C::KPAD : 16];
+#pragma unroll
+        for (int k = 0; k < C::KPAD; ++k) v[k] = 0;
+#pragma unroll
+        for (int ky = 0; ky < 3; ++ky) {
+          const int iy = gy * S + ky - 1;
+#pragma unroll
+          for (int kx = 0; kx < 3; ++kx) {
+            const int ix = gx * S + kx - 1;
+            if (iy >= 0 && iy < a.hx && ix >= 0 && ix < a.wx) {
+              const __half* px = x + (((size_t)tc.cam * a.hx + iy) * a.wx + ix) * CIN;
+#pragma unroll
+              for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = __half_as_ushort(__ldg(px + c));
+            }
+          }
+        }
+        uint8_t* row = sA + s * C::A_STAGE + r * C::ROWB;
+        constexpr int NQ = C::ROWB / 16;
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          const int pq = C::SWZ == 2 ? (q ^ (r & 7)) : (q ^ ((r >> 1) & 3));
+          uint4 w4;
+          w4.x = v[q * 8 + 0] | ((uint32_t)v[q * 8 + 1] << 16);
+          w4.y = v[q * 8 + 2] | ((uint32_t)v[q * 8 + 3] << 16);
+          w4.z = v[q * 8 + 4] | ((uint32_t)v[q * 8 + 5] << 16);
+          w4.w = v[q * 8 + 6] | ((uint32_t)v[q * 8 + 7] << 16);
+          *reinterpret_cast<uint4*>(row + pq * 16) = w4;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&full[s]);
+      }
+    } else if (warp == 5 && lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      bool ok = mbar_wait(wbar, 0, abort_flag);
+      if (!ok) {
+        atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
+        *abort_flag = 1;
+      }
+      uint32_t g = 0;
+      for (int it = 0; ok && it < my_tiles; ++it) {
+        const int ab = it & 1;
+        if (!mbar_wait(&acce[ab], ((it >> 1) & 1) ^ 1, abort_flag)) {
+          atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * NCTA;
+        for (int kb = 0; kb < C::NKB; ++kb, ++g) {
+          const int s = g % C::STAGES;
+          if (!mbar_wait(&full[s], (g / C::STAGES) & 1u, abort_flag)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * C::A_STAGE);
+          const uint32_t b_addr = smem_u32(sW + kb * C::B_KB);
+#pragma unroll
+          for (int kk = 0; kk < C::CH / 16; ++kk) {
+            const uint64_t ad = smem_desc(a_addr + kk * 32, C::SBO, C::SWZ);
+            const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
+            mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[s]);  // stage free once these MMAs have read it
+        }
+        if (!ok) break;
+        mma_commit(&accf[ab]);    // accumulator ready for the epilogue
+      }
+      // drain: all issued MMAs complete before TMEM is released
+      mma_commit(dbar);
+      volatile int never = 0;
+      mbar_wait(dbar, 0, &never);
+    } else if (warp < 4) {
+      // ------------------------------------------------ epilogue: TMEM -> bias/res/ReLU -> cache
+      const int r = warp * 32 + lane;  // accumulator row = TMEM lane
+      __half* y = static_cast<__half*>(a.y);
+      const __half* res = static_cast<const __half*>(a.res);
+      for (int it = 0; it < my_tiles; ++it) {
+        const int m = blockIdx.x + it * gridDim.x;
+        const int ab = it & 1;
+        const bool got = mbar_wait(&accf[ab], (it >> 1) & 1, abort_flag);
+        if (!got) {
+          atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
+          *abort_flag = 1;
+        }
+        // warp-uniform exit: tcgen05.ld below is .sync.aligned
+        if (__any_sync(0xFFFFFFFFu, !got || *abort_flag != 0)) break;
+        tc_fence_after();
+        int ti, p;
+        if (C::TT >= 128) { ti = m / C::MPT; p = (m % C::MPT) * 128 + r; }
+        else { ti = m * C::TPM + r / C::TT; p = r % C::TT; }
+        const bool valid = ti < n_tiles;
+        const TileXY tc = tile_at(a, mode, listed, valid ? ti : 0);
+        const int gy = tc.by * T + p / T, gx = tc.bx * T + p % T;
+        const bool inb = tc.cam < a.n && gy < a.ho && gx < a.wo;
+        if (valid && !inb) atomicOr(&a.st->error, SB_ERR_BAD_TILE);
+        const size_t pix = (((size_t)tc.cam * a.ho + gy) * a.wo + gx) * a.cout + n0;
+        const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16) + ab * NCTA;
+#pragma unroll 1
+        for (int c0 = 0; c0 < NCTA; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(taddr + c0, v);
+          tmem_ld_wait();
+          float f[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]) + sBias[c0 + j];
+          if (valid && inb) {
+            if (res != nullptr) {
+              const uint4* rp = reinterpret_cast<const uint4*>(res + pix + c0);
+              const uint4 r0 = __ldg(rp), r1 = __ldg(rp + 1);
+              const __half2* h0 = reinterpret_cast<const __half2*>(&r0);
+              const __half2* h1 = reinterpret_cast<const __half2*>(&r1);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 q0 = __half22float2(h0[j]), q1 = __half22float2(h1[j]);
+                f[2 * j] += q0.x;
+                f[2 * j + 1] += q0.y;
+                f[8 + 2 * j] += q1.x;
+                f[8 + 2 * j + 1] += q1.y;
+              }
+            }
+            if (a.act) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) f[j] = fmaxf(f[j], 0.0f);
+            }
+            uint4 o0, o1;
+            __half2* p0 = reinterpret_cast<__half2*>(&o0);
+            __half2* p1 = reinterpret_cast<__half2*>(&o1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              p0[j] = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+              p1[j] = __floats2half2_rn(f[8 + 2 * j], f[8 + 2 * j + 1]);
+            }
+            uint4* op = reinterpret_cast<uint4*>(y + pix + c0);
+            op[0] = o0;
+            op[1] = o1;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acce[ab]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+namespace {
+
+struct Variant {
+  int cin, cout, t, s, ncta;
+  void (*fn)(const ConvArgs, const CUtensorMap);
+  int smem, threads, w_bytes, ch, box_rows;
+};
+
+template <int CIN, int NCTA, int T, int S>
+Variant make_variant(int cout) {
+  using C = TcCfg<CIN, NCTA, T, S>;
+  return Variant{CIN, cout, T, S, NCTA, conv_tc_kernel<CIN, NCTA, T, S>, C::SMEM, C::THREADS, C::W_BYTES,
+                 C::CH, C::BOX_ROWS};
+}
+
+// Sarbon stem shapes (widths 32/64/128, Res blocks) at block 32 and block 64.
+const std::vector<Variant>& variants() {
+  static const std::vector<Variant> v = {
+      // block 32
+      make_variant<3, 32, 16, 2>(32),
+      make_variant<32, 64, 8, 2>(64),
+      make_variant<64, 64, 8, 1>(64),
+      make_variant<64, 128, 4, 2>(128),
+      make_variant<128, 64, 4, 1>(128),  // two C_out slices of 64 (weights fit smem)
+      // block 64
+      make_variant<3, 32, 32, 2>(32),
+      make_variant<32, 64, 16, 2>(64),
+      make_variant<64, 64, 16, 1>(64),
+      make_variant<64, 128, 8, 2>(128),
+      make_variant<128, 64, 8, 1>(128),
+  };
+  return v;
+}
+
+const Variant* find_variant(int cin, int cout, int t, int s) {
+  for (const auto& v : variants())
+    if (v.cin == cin && v.cout == cout && v.t == t && v.s == s) return &v;
+  return nullptr;
+}
+
+}  // namespace
+
+bool conv_tc_supported(int cin, int cout, int t, int s) { return find_variant(cin, cout, t, s) != nullptr; }
+
+int conv_tc_nsplit(int cin, int cout, int t, int s) {
+  const Variant* v = find_variant(cin, cout, t, s);
+  return v ? v->cout / v->ncta : 0;
+}
+
+size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s) {
+  const Variant* v = find_variant(cin, cout, t, s);
+  return v ? (size_t)v->w_bytes * (v->cout / v->ncta) : 0;
+}
+
+int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s) {
+  const Variant* v = find_variant(cin, cout, t, s);
+  if (!v) return 0;
+  return 1;
+}
+
+// Weight image for the tcgen05 B operand: per C_out slice, per K-block (tap-major,
+// then channel chunk), NCTA rows of ROWB bytes, K-major, with the 128B/64B swizzle
+// applied exactly as the MMA reads it from a 1024-byte-aligned shared buffer.
+void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_t* out) {
+  const Variant* v = find_variant(cin, cout, t, s);
+  if (!v) return;
+  const bool manual = cin < 16;
+  const int ch = v->ch, rowb = ch * 2, ncta = v->ncta, nsplit = cout / ncta;
+  const int nch = manual ? 1 : cin / ch, nkb = manual ? 1 : 9 * nch;
+  const size_t split_elems = (size_t)v->w_bytes / 2;
+  for (int sp = 0; sp < nsplit; ++sp) {
+    uint16_t* img = out + sp * split_elems;
+    std::memset(img, 0, (size_t)v->w_bytes);
+    for (int kb = 0; kb < nkb; ++kb) {
+      for (int n = 0; n < ncta; ++n) {
+        const int co = sp * ncta + n;
+        for (int k = 0; k < ch; ++k) {
+          float val = 0.f;
+          if (manual) {
+            if (k < 9 * cin) {
+              const int tap = k / cin, ci = k % cin;
+              val = w[((size_t)tap * cin + ci) * cout + co];
+            }
+          } else {
+            const int tap = kb / nch, ci = (kb % nch) * ch + k;
+            val = w[((size_t)tap * cin + ci) * cout + co];
+          }
+          const int q = (k * 2) / 16, within = (k * 2) % 16;
+          const int pq = rowb == 128 ? (q ^ (n & 7)) : (q ^ ((n >> 1) & 3));
+          const size_t byte = (size_t)kb * ncta * rowb + (size_t)n * rowb + pq * 16 + within;
+          __half h = __float2half_rn(val);
+          img[byte / 2] = *reinterpret_cast<uint16_t*>(&h);
+        }
+      }
+    }
+  }
+}
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+// 4-D tiled map over an NHWC fp16 cache: dims {C, W, H, N}; box {CH, T*S, rows*S, 1}
+// with element strides {1, S, S, 1} so that one box is the strided im2col slice of one
+// tap for one tile.
+cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s) {
+  const Variant* v = nullptr;
+  for (const auto& c : variants())
+    if (c.cin == cin && c.t == t && c.s == s) { v = &c; break; }
+  if (!v || cin < 16) return cudaErrorInvalidValue;
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) return cudaErrorNotSupported;
+  cuuint64_t dims[4] = {(cuuint64_t)cin, (cuuint64_t)wx, (cuuint64_t)hx, (cuuint64_t)n};
+  cuuint64_t strides[3] = {(cuuint64_t)cin * 2, (cuuint64_t)wx * cin * 2, (cuuint64_t)hx * wx * cin * 2};
+  cuuint32_t box[4] = {(cuuint32_t)v->ch, (cuuint32_t)(t * s), (cuuint32_t)(v->box_rows * s), 1};
+  cuuint32_t estr[4] = {1, (cuuint32_t)s, (cuuint32_t)s, 1};
+  const CUtensorMapSwizzle swz = v->ch * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(src), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_conv_tc(const ConvArgs& a, const CUtensorMap* map, int grid_x, cudaStream_t st) {
+  const Variant* v = find_variant(a.cin, a.cout, a.t, a.s);
+  if (!v) return cudaErrorInvalidValue;
+  static bool attr_done[16] = {};
+  const int idx = (int)(v - variants().data());
+  if (!attr_done[idx]) {
+    cudaError_t e = cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem);
+    if (e != cudaSuccess) return e;
+    attr_done[idx] = true;
+  }
+  dim3 grid(grid_x, a.cout / v->ncta);
+  CUtensorMap dummy;
+  std::memset(&dummy, 0, sizeof(dummy));
+  v->fn<<<grid, v->threads, v->smem, st>>>(a, map ? *map : dummy);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

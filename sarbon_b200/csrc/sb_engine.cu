@@ -1,0 +1,598 @@
+// sb_engine.cu -- the C ABI (include/sarbon_sparse.h): engine object, device memory,
+// tensor maps and the per-step launch sequence.
+//
+// Reference: Bahrombekk/Sarbon sarbon/sparse/fused_engine.py (FusedSparseEngine).  The
+// reference captures a gate graph, syncs once per step to read the active count, then
+// replays a sparse graph per budget bucket or a dense cuDNN graph.  Here the whole step
+// is one stream-ordered sequence with the dispatch decided on the device:
+//   gate -> lists (+ mode) -> dense img copy (no-op unless dense) -> conv x L -> finalize
+// Every conv kernel reads the mode and its list length from device memory and runs a
+// persistent grid, so there is no host sync inside a step.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "sb_internal.cuh"
+#include "sb_ptx.cuh"
+
+using namespace sb;
+
+namespace {
+
+thread_local std::string g_err = "no error";
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define SB_CUDA(call)                                                                  \
+  do {                                                                                 \
+    cudaError_t e_ = (call);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return fail(SB_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_));       \
+  } while (0)
+
+std::vector<int> budget_buckets(int n_blocks, int unit = 16, double ratio = 1.15) {
+  std::vector<int> out;
+  int b = unit;
+  while (b < n_blocks) {
+    out.push_back(b);
+    const int nb = (int)std::ceil(b * ratio / unit) * unit;
+    b = std::max(b + unit, nb);
+  }
+  out.push_back((int)std::ceil((double)n_blocks / unit) * unit);
+  return out;
+}
+
+__global__ void set_i64_kernel(int64_t* p, int64_t v) { *p = v; }
+__global__ void set_i32_kernel(int32_t* p, int32_t v) { *p = v; }
+
+}  // namespace
+
+struct sb_engine {
+  int dev = 0;
+  int n = 0, h = 0, w = 0, block = 0, hb = 0, wb = 0, n_blocks = 0, dtype = SB_F16, esz = 2;
+  double tau = 0.0;
+  int refresh = 0;
+  int64_t thr_fx = 0;
+  double thr = 0.0;
+  int n_layers = 0;
+  sb_layer_desc layers[SB_MAX_LAYERS];
+  int nd = 0;
+  int ds[SB_MAX_DILATIONS] = {};
+  int layer_di[SB_MAX_LAYERS] = {};
+  int layer_t[SB_MAX_LAYERS] = {};
+  void* cache[SB_MAX_LAYERS + 1] = {};
+  int64_t shape[SB_MAX_LAYERS + 1][4] = {};
+  uint8_t* changed = nullptr;
+  uint8_t* extra = nullptr;
+  uint8_t* masks = nullptr;
+  int32_t* lists = nullptr;
+  unsigned long long* status = nullptr;
+  int n_chunks = 0;
+  State* st = nullptr;
+  float* bias[SB_MAX_LAYERS] = {};
+  void* wdev[SB_MAX_LAYERS] = {};
+  bool wok[SB_MAX_LAYERS] = {};
+  CUtensorMap tmap[SB_MAX_LAYERS];
+  bool has_tmap[SB_MAX_LAYERS] = {};
+  int32_t* host_out = nullptr;      // mapped pinned: mode, count, error, written
+  int32_t* host_out_dev = nullptr;
+  int n_sms = 148;
+  int last_launches = 0;
+  std::vector<void*> allocs;
+  // optional per-launch timing (sb_step_profiled)
+  bool profiling = false;
+  std::vector<cudaEvent_t> events;
+  int n_events = 0;
+};
+
+namespace {
+
+// Record a timing event on `s` when profiling (one before the first launch and one
+// after every launch of the step).
+void mark(sb_engine* e, cudaStream_t s) {
+  if (!e->profiling) return;
+  if (e->n_events >= (int)e->events.size()) {
+    cudaEvent_t ev;
+    if (cudaEventCreate(&ev) != cudaSuccess) return;
+    e->events.push_back(ev);
+  }
+  cudaEventRecord(e->events[e->n_events++], s);
+}
+
+int alloc_dev(sb_engine* e, void** p, size_t bytes) {
+  if (cudaMalloc(p, bytes) != cudaSuccess) return fail(SB_ENOMEM, "cudaMalloc failed");
+  e->allocs.push_back(*p);
+  if (cudaMemset(*p, 0, bytes) != cudaSuccess) return fail(SB_ECUDA, "cudaMemset failed");
+  return SB_OK;
+}
+
+int launch_convs(sb_engine* e, cudaStream_t s) {
+  for (int i = 0; i < e->n_layers; ++i) {
+    const sb_layer_desc& L = e->layers[i];
+    if (!e->wok[i]) return fail(SB_EINVAL, "weights of layer " + std::to_string(i) + " not uploaded");
+    ConvArgs a{};
+    a.x = e->cache[L.src];
+    a.y = e->cache[i + 1];
+    a.res = L.res >= 0 ? e->cache[L.res] : nullptr;
+    a.bias = e->bias[i];
+    a.wimg = e->wdev[i];
+    const int di = e->layer_di[i];
+    a.lcam = e->lists + (size_t)di * 3 * e->n_blocks;
+    a.lby = a.lcam + e->n_blocks;
+    a.lbx = a.lby + e->n_blocks;
+    a.st = e->st;
+    a.d_idx = di;
+    a.n = e->n;
+    a.hx = (int)e->shape[L.src][1];
+    a.wx = (int)e->shape[L.src][2];
+    a.cin = L.cin;
+    a.ho = (int)e->shape[i + 1][1];
+    a.wo = (int)e->shape[i + 1][2];
+    a.cout = L.cout;
+    a.hb = e->hb;
+    a.wb = e->wb;
+    a.n_blocks = e->n_blocks;
+    a.t = e->layer_t[i];
+    a.s = L.stride;
+    a.act = L.act;
+    cudaError_t err;
+    if (e->dtype == SB_F16) {
+      err = launch_conv_tc(a, e->has_tmap[i] ? &e->tmap[i] : nullptr, e->n_sms, s);
+    } else {
+      err = launch_conv_simt(a, e->n_sms * 4, s);
+    }
+    if (err != cudaSuccess)
+      return fail(SB_ECUDA, "conv launch (layer " + std::to_string(i) + "): " + cudaGetErrorString(err));
+    e->last_launches += 1;
+    mark(e, s);
+  }
+  return SB_OK;
+}
+
+int check_frames(sb_engine* e, const void* p) {
+  if (!p) return fail(SB_EINVAL, "frames pointer is NULL");
+  if (reinterpret_cast<uintptr_t>(p) % 16) return fail(SB_EINVAL, "frames must be 16-byte aligned");
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
+    return fail(SB_EINVAL, "frames must be device memory");
+  return SB_OK;
+}
+
+int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, const float* stdv,
+              cudaStream_t s, int* mode_out, int64_t* count_out) {
+  int rc = check_frames(e, frames);
+  if (rc) return rc;
+  SB_CUDA(cudaSetDevice(e->dev));
+  e->last_launches = 0;
+  GateArgs g{};
+  g.frames = frames;
+  g.img = e->cache[0];
+  g.extra = e->extra;
+  g.changed = e->changed;
+  g.st = e->st;
+  g.n = e->n;
+  g.h = e->h;
+  g.w = e->w;
+  g.hb = e->hb;
+  g.wb = e->wb;
+  g.block = e->block;
+  g.thr_fx = e->thr_fx;
+  g.thr = e->thr;
+  g.refresh = e->refresh;
+  for (int c = 0; c < 3; ++c) {
+    g.mean[c] = mean ? mean[c] : 0.f;
+    g.stdv[c] = stdv ? stdv[c] : 1.f;
+  }
+  mark(e, s);
+  SB_CUDA(launch_gate(g, kind, s));
+  mark(e, s);
+  ListArgs l{};
+  l.changed = e->changed;
+  l.masks = e->masks;
+  l.lists = e->lists;
+  l.status = e->status;
+  l.st = e->st;
+  l.n_blocks = e->n_blocks;
+  l.hb = e->hb;
+  l.wb = e->wb;
+  l.n_dil = e->nd;
+  for (int i = 0; i < e->nd; ++i) l.ds[i] = e->ds[i];
+  SB_CUDA(launch_lists(l, e->n_chunks, s));
+  mark(e, s);
+  CopyArgs c{};
+  c.frames = frames;
+  c.img = e->cache[0];
+  c.changed = nullptr;
+  c.st = e->st;
+  c.n = e->n;
+  c.h = e->h;
+  c.w = e->w;
+  c.hb = e->hb;
+  c.wb = e->wb;
+  c.block = e->block;
+  c.elem_bytes = e->esz;
+  c.u8 = kind == 2;
+  for (int k = 0; k < 3; ++k) {
+    c.mean[k] = g.mean[k];
+    c.stdv[k] = g.stdv[k];
+  }
+  SB_CUDA(launch_copy(c, s));
+  mark(e, s);
+  e->last_launches = 3;
+  rc = launch_convs(e, s);
+  if (rc) return rc;
+  SB_CUDA(launch_finalize(e->st, e->refresh, e->host_out_dev, s));
+  mark(e, s);
+  e->last_launches += 1;
+  if (mode_out || count_out) {
+    SB_CUDA(cudaStreamSynchronize(s));
+    volatile int32_t* ho = e->host_out;
+    if (mode_out) *mode_out = ho[0];
+    if (count_out) *count_out = ho[1];
+    if (ho[2] & (SB_ERR_TIMEOUT_FULL | SB_ERR_TIMEOUT_EMPTY | SB_ERR_TIMEOUT_ACC | SB_ERR_TIMEOUT_LOOKBK |
+                 SB_ERR_TIMEOUT_WGT))
+      return fail(SB_ETIMEOUT, "a bounded device wait gave up (error flags " + std::to_string(ho[2]) + ")");
+    if (ho[2]) return fail(SB_ECUDA, "device error flags " + std::to_string(ho[2]));
+  }
+  return SB_OK;
+}
+
+int dense_impl(sb_engine* e, const void* frames, int reset, cudaStream_t s) {
+  int rc = check_frames(e, frames);
+  if (rc) return rc;
+  SB_CUDA(cudaSetDevice(e->dev));
+  SB_CUDA(launch_set_mode(e->st, SB_MODE_DENSE, reset, 0, s));
+  CopyArgs c{};
+  c.frames = frames;
+  c.img = e->cache[0];
+  c.st = e->st;
+  c.n = e->n;
+  c.h = e->h;
+  c.w = e->w;
+  c.hb = e->hb;
+  c.wb = e->wb;
+  c.block = e->block;
+  c.elem_bytes = e->esz;
+  SB_CUDA(launch_copy(c, s));
+  e->last_launches = 2;
+  return launch_convs(e, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* sb_last_error(void) { return g_err.c_str(); }
+
+const char* sb_version(void) { return "sarbon_b200 0.1 sm_100a (tcgen05 fp16 tile conv, fp32 simt)"; }
+
+int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width, int block,
+              int dtype, double tau, int refresh, int dense_check_every, sb_engine** out) {
+  if (!out || !layers) return fail(SB_EINVAL, "null argument");
+  *out = nullptr;
+  if (n_layers < 1 || n_layers > SB_MAX_LAYERS) return fail(SB_EINVAL, "n_layers out of range");
+  if (n_streams < 1 || height < 1 || width < 1) return fail(SB_EINVAL, "bad frame geometry");
+  if (block < 16 || block % 16) return fail(SB_EINVAL, "block must be a multiple of 16");
+  if (height % block || width % block) return fail(SB_EINVAL, "height and width must be divisible by block");
+  if (dtype != SB_F16 && dtype != SB_F32) return fail(SB_EINVAL, "dtype must be SB_F16 or SB_F32");
+  if (refresh < 0) return fail(SB_EINVAL, "refresh must be >= 0");
+  sb_engine* e = new sb_engine();
+  auto bail = [&](int code) {
+    sb_destroy(e);
+    return code;
+  };
+  if (cudaGetDevice(&e->dev) != cudaSuccess) {
+    delete e;
+    return fail(SB_ECUDA, "no CUDA device");
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, e->dev) != cudaSuccess) return bail(fail(SB_ECUDA, "device query failed"));
+  e->n_sms = prop.multiProcessorCount;
+  e->n = n_streams;
+  e->h = height;
+  e->w = width;
+  e->block = block;
+  e->hb = height / block;
+  e->wb = width / block;
+  e->n_blocks = n_streams * e->hb * e->wb;
+  e->dtype = dtype;
+  e->esz = dtype == SB_F16 ? 2 : 4;
+  e->tau = tau;
+  e->refresh = refresh;
+  e->n_layers = n_layers;
+  // threshold = float32(tau * block * block * 3), compared as torch does (fused_engine.py:144)
+  const float thr32 = (float)(tau * block * block * 3);
+  e->thr = (double)thr32;
+  if (std::isnan(thr32)) e->thr_fx = INT64_MAX;
+  else if (thr32 < 0.f) e->thr_fx = -1;
+  else if (std::isinf(thr32) || (double)thr32 * 16777216.0 >= 9.0e18) e->thr_fx = INT64_MAX;
+  else e->thr_fx = (int64_t)std::floor((double)thr32 * 16777216.0);
+  if (std::isnan(thr32)) e->thr = INFINITY;  // sum > NaN is false for every block
+  // caches: id 0 = image, id i+1 = layer i output
+  e->shape[0][0] = n_streams;
+  e->shape[0][1] = height;
+  e->shape[0][2] = width;
+  e->shape[0][3] = 3;
+  std::vector<int> dl;
+  for (int i = 0; i < n_layers; ++i) {
+    const sb_layer_desc& L = layers[i];
+    e->layers[i] = L;
+    if (L.src < 0 || L.src > i) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": bad src id"));
+    if (L.res >= i + 1 || L.res < -1) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": bad res id"));
+    if (L.stride != 1 && L.stride != 2) return bail(fail(SB_EINVAL, "conv stride must be 1 or 2"));
+    if (L.out_stride < 1 || block % L.out_stride || height % L.out_stride || width % L.out_stride)
+      return bail(fail(SB_EINVAL, "out_stride must divide block, height and width"));
+    if (e->shape[L.src][3] != L.cin) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": cin mismatch"));
+    const int in_stride = L.src == 0 ? 1 : layers[L.src - 1].out_stride;
+    if (in_stride * L.stride != L.out_stride)
+      return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": stride chain mismatch"));
+    e->shape[i + 1][0] = n_streams;
+    e->shape[i + 1][1] = height / L.out_stride;
+    e->shape[i + 1][2] = width / L.out_stride;
+    e->shape[i + 1][3] = L.cout;
+    if (L.res >= 0 && (e->shape[L.res][3] != L.cout || e->shape[L.res][1] != e->shape[i + 1][1]))
+      return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": residual shape mismatch"));
+    e->layer_t[i] = block / L.out_stride;
+    if (dtype == SB_F16 && !conv_tc_supported(L.cin, L.cout, e->layer_t[i], L.stride))
+      return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": no tcgen05 kernel for cin=" +
+                                      std::to_string(L.cin) + " cout=" + std::to_string(L.cout) +
+                                      " tile=" + std::to_string(e->layer_t[i]) + " stride=" +
+                                      std::to_string(L.stride)));
+    const int d = (L.radius + block - 1) / block;
+    bool seen = false;
+    for (int x : dl) seen |= x == d;
+    if (!seen) dl.push_back(d);
+  }
+  std::sort(dl.begin(), dl.end());
+  if ((int)dl.size() > SB_MAX_DILATIONS) return bail(fail(SB_EINVAL, "too many distinct dilations"));
+  e->nd = (int)dl.size();
+  for (int i = 0; i < e->nd; ++i) e->ds[i] = dl[i];
+  for (int i = 0; i < n_layers; ++i) {
+    const int d = (layers[i].radius + block - 1) / block;
+    for (int j = 0; j < e->nd; ++j)
+      if (e->ds[j] == d) e->layer_di[i] = j;
+  }
+  // device memory
+  int rc;
+  for (int i = 0; i <= n_layers; ++i) {
+    const size_t bytes = (size_t)e->shape[i][0] * e->shape[i][1] * e->shape[i][2] * e->shape[i][3] * e->esz;
+    if ((rc = alloc_dev(e, &e->cache[i], bytes))) return bail(rc);
+  }
+  e->n_chunks = (e->n_blocks + 1023) / 1024;
+  if ((rc = alloc_dev(e, (void**)&e->changed, e->n_blocks))) return bail(rc);
+  if ((rc = alloc_dev(e, (void**)&e->extra, e->n_blocks))) return bail(rc);
+  if ((rc = alloc_dev(e, (void**)&e->masks, (size_t)e->nd * e->n_blocks))) return bail(rc);
+  if ((rc = alloc_dev(e, (void**)&e->lists, (size_t)e->nd * 3 * e->n_blocks * 4))) return bail(rc);
+  if ((rc = alloc_dev(e, (void**)&e->status, (size_t)e->nd * e->n_chunks * 8))) return bail(rc);
+  if ((rc = alloc_dev(e, (void**)&e->st, sizeof(State)))) return bail(rc);
+  State init{};
+  init.epoch = 1;
+  init.fallback = budget_buckets(e->n_blocks).back();
+  init.check_every = dense_check_every;
+  init.mode_cur = SB_MODE_SKIP;
+  if (cudaMemcpy(e->st, &init, sizeof(State), cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(fail(SB_ECUDA, "state upload failed"));
+  if (cudaHostAlloc((void**)&e->host_out, 16, cudaHostAllocMapped) != cudaSuccess)
+    return bail(fail(SB_ENOMEM, "pinned allocation failed"));
+  std::memset(e->host_out, 0, 16);
+  if (cudaHostGetDevicePointer((void**)&e->host_out_dev, e->host_out, 0) != cudaSuccess)
+    return bail(fail(SB_ECUDA, "mapped pointer failed"));
+  for (int i = 0; i < n_layers; ++i) {
+    const sb_layer_desc& L = layers[i];
+    if ((rc = alloc_dev(e, (void**)&e->bias[i], (size_t)L.cout * 4))) return bail(rc);
+    const size_t wbytes = dtype == SB_F16 ? conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[i], L.stride)
+                                          : (size_t)9 * L.cin * L.cout * 4;
+    if ((rc = alloc_dev(e, &e->wdev[i], wbytes))) return bail(rc);
+    if (dtype == SB_F16 && L.cin >= 16) {
+      cudaError_t err = conv_tc_make_tmap(&e->tmap[i], e->cache[L.src], n_streams, (int)e->shape[L.src][1],
+                                          (int)e->shape[L.src][2], L.cin, e->layer_t[i], L.stride);
+      if (err != cudaSuccess) return bail(fail(SB_ECUDA, std::string("tensor map: ") + cudaGetErrorString(err)));
+      e->has_tmap[i] = true;
+    }
+  }
+  *out = e;
+  return SB_OK;
+}
+
+int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias) {
+  if (!e || !w || !bias) return fail(SB_EINVAL, "null argument");
+  if (layer < 0 || layer >= e->n_layers) return fail(SB_EINVAL, "layer out of range");
+  const sb_layer_desc& L = e->layers[layer];
+  SB_CUDA(cudaSetDevice(e->dev));
+  SB_CUDA(cudaMemcpy(e->bias[layer], bias, (size_t)L.cout * 4, cudaMemcpyHostToDevice));
+  if (e->dtype == SB_F16) {
+    const size_t bytes = conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[layer], L.stride);
+    std::vector<uint16_t> img(bytes / 2);
+    conv_tc_build_wimg(L.cin, L.cout, e->layer_t[layer], L.stride, w, img.data());
+    SB_CUDA(cudaMemcpy(e->wdev[layer], img.data(), bytes, cudaMemcpyHostToDevice));
+  } else {
+    SB_CUDA(cudaMemcpy(e->wdev[layer], w, (size_t)9 * L.cin * L.cout * 4, cudaMemcpyHostToDevice));
+  }
+  e->wok[layer] = true;
+  return SB_OK;
+}
+
+int sb_reset(sb_engine* e, const void* frames_dev, void* stream) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  return dense_impl(e, frames_dev, 1, (cudaStream_t)stream);
+}
+
+int sb_dense(sb_engine* e, const void* frames_dev, void* stream) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  return dense_impl(e, frames_dev, 0, (cudaStream_t)stream);
+}
+
+int sb_step(sb_engine* e, const void* frames_dev, void* stream, int* mode_out, int64_t* count_out) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  return step_impl(e, frames_dev, e->dtype == SB_F16 ? 0 : 1, nullptr, nullptr, (cudaStream_t)stream, mode_out,
+                   count_out);
+}
+
+int sb_step_u8(sb_engine* e, const uint8_t* frames_dev, const float mean[3], const float std_[3], void* stream,
+               int* mode_out, int64_t* count_out) {
+  if (!e || !mean || !std_) return fail(SB_EINVAL, "null argument");
+  if (e->dtype != SB_F16) return fail(SB_EINVAL, "uint8 frames need an fp16 engine");
+  return step_impl(e, frames_dev, 2, mean, std_, (cudaStream_t)stream, mode_out, count_out);
+}
+
+int sb_step_profiled(sb_engine* e, const void* frames_dev, void* stream, float* kernel_ms, int capacity,
+                     int* n_kernels) {
+  if (!e || !kernel_ms || !n_kernels) return fail(SB_EINVAL, "null argument");
+  e->profiling = true;
+  e->n_events = 0;
+  int mode;
+  int64_t count;
+  const int rc = step_impl(e, frames_dev, e->dtype == SB_F16 ? 0 : 1, nullptr, nullptr, (cudaStream_t)stream,
+                           &mode, &count);
+  e->profiling = false;
+  if (rc) return rc;
+  const int n = e->n_events - 1;
+  *n_kernels = n;
+  for (int i = 0; i < n && i < capacity; ++i) {
+    float ms = 0.f;
+    SB_CUDA(cudaEventElapsedTime(&ms, e->events[i], e->events[i + 1]));
+    kernel_ms[i] = ms;
+  }
+  return SB_OK;
+}
+
+int sb_result_ptr(sb_engine* e, const int64_t** dev_ptr) {
+  if (!e || !dev_ptr) return fail(SB_EINVAL, "null argument");
+  *dev_ptr = e->st->result;
+  return SB_OK;
+}
+
+int sb_query(sb_engine* e, void* stream, int* mode_out, int64_t* count_out) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  SB_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  State st;
+  SB_CUDA(cudaMemcpy(&st, e->st, sizeof(State), cudaMemcpyDeviceToHost));
+  if (mode_out) *mode_out = st.last_mode;
+  if (count_out) *count_out = st.last_count;
+  return SB_OK;
+}
+
+int sb_set_extra(sb_engine* e, const uint8_t* mask_dev, void* stream) {
+  if (!e || !mask_dev) return fail(SB_EINVAL, "null argument");
+  SB_CUDA(cudaMemcpyAsync(e->extra, mask_dev, e->n_blocks, cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
+  return SB_OK;
+}
+
+int sb_set_fallback(sb_engine* e, int64_t fallback, void* stream) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  set_i64_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(&e->st->fallback, fallback);
+  SB_CUDA(cudaGetLastError());
+  return SB_OK;
+}
+
+int sb_set_dense_check_every(sb_engine* e, int n, void* stream) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  set_i32_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(&e->st->check_every, n);
+  SB_CUDA(cudaGetLastError());
+  return SB_OK;
+}
+
+int sb_run_sparse_forced(sb_engine* e, const void* frames_dev, int64_t n_tiles, void* stream) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (n_tiles < 1 || n_tiles > e->n_blocks) return fail(SB_EINVAL, "n_tiles out of range");
+  int rc = check_frames(e, frames_dev);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  SB_CUDA(launch_set_mode(e->st, SB_MODE_SPARSE, 0, n_tiles, s));
+  CopyArgs c{};
+  c.frames = frames_dev;
+  c.img = e->cache[0];
+  c.changed = e->changed;
+  c.st = e->st;
+  c.n = e->n;
+  c.h = e->h;
+  c.w = e->w;
+  c.hb = e->hb;
+  c.wb = e->wb;
+  c.block = e->block;
+  c.elem_bytes = e->esz;
+  SB_CUDA(launch_copy(c, s));
+  rc = launch_convs(e, s);
+  if (rc) return rc;
+  SB_CUDA(launch_set_mode(e->st, SB_MODE_SPARSE, 0, 0, s));
+  return SB_OK;
+}
+
+int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]) {
+  if (!e || !ptr) return fail(SB_EINVAL, "null argument");
+  if (cache_id < 0 || cache_id > e->n_layers) return fail(SB_EINVAL, "cache id out of range");
+  *ptr = e->cache[cache_id];
+  if (shape)
+    for (int k = 0; k < 4; ++k) shape[k] = e->shape[cache_id][k];
+  return SB_OK;
+}
+
+int sb_gate_buffers(sb_engine* e, uint8_t** changed, uint8_t** masks, uint8_t** extra, int* n_dilations,
+                    int dilations[SB_MAX_DILATIONS]) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (changed) *changed = e->changed;
+  if (masks) *masks = e->masks;
+  if (extra) *extra = e->extra;
+  if (n_dilations) *n_dilations = e->nd;
+  if (dilations)
+    for (int i = 0; i < SB_MAX_DILATIONS; ++i) dilations[i] = i < e->nd ? e->ds[i] : 0;
+  return SB_OK;
+}
+
+int sb_debug_lists(sb_engine* e, int d_index, int32_t** cam, int32_t** by, int32_t** bx, int64_t* count,
+                   void* stream) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (d_index < 0 || d_index >= e->nd) return fail(SB_EINVAL, "dilation index out of range");
+  int32_t* base = e->lists + (size_t)d_index * 3 * e->n_blocks;
+  if (cam) *cam = base;
+  if (by) *by = base + e->n_blocks;
+  if (bx) *bx = base + 2 * (size_t)e->n_blocks;
+  if (count) {
+    SB_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    State st;
+    SB_CUDA(cudaMemcpy(&st, e->st, sizeof(State), cudaMemcpyDeviceToHost));
+    *count = st.counts[d_index];
+  }
+  return SB_OK;
+}
+
+int sb_stats(sb_engine* e, void* stream, sb_stats_t* out) {
+  if (!e || !out) return fail(SB_EINVAL, "null argument");
+  SB_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+  State st;
+  SB_CUDA(cudaMemcpy(&st, e->st, sizeof(State), cudaMemcpyDeviceToHost));
+  std::memset(out, 0, sizeof(*out));
+  out->skip = st.stats[SB_MODE_SKIP];
+  out->sparse = st.stats[SB_MODE_SPARSE];
+  out->dense = st.stats[SB_MODE_DENSE];
+  out->last_count = st.last_count;
+  out->last_mode = st.last_mode;
+  out->error = st.error;
+  out->n_dilations = e->nd;
+  for (int i = 0; i < e->nd; ++i) {
+    out->counts[i] = st.counts[i];
+    out->dilations[i] = e->ds[i];
+  }
+  return SB_OK;
+}
+
+int sb_last_launch_count(sb_engine* e) { return e ? e->last_launches : 0; }
+
+int sb_destroy(sb_engine* e) {
+  if (!e) return SB_OK;
+  cudaSetDevice(e->dev);
+  cudaDeviceSynchronize();
+  for (void* p : e->allocs) cudaFree(p);
+  for (cudaEvent_t ev : e->events) cudaEventDestroy(ev);
+  if (e->host_out) cudaFreeHost(e->host_out);
+  delete e;
+  return SB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,462 @@
+// sb_gate.cu -- per-frame gating, dilation + ordered block lists, image-cache updates and
+// the device-side dispatch state machine of the temporal block-sparse engine.
+//
+// Reference (Bahrombekk/Sarbon, sarbon/sparse/fused_engine.py):
+//   gate            _gate        :140-153
+//   img update      _sparse      :155-160 (fused into the gate here)
+//   block lists     _sparse      :161-165 (nonzero_static: ascending flat order)
+//   dispatch        step         :214-240 (skip / sparse / dense + hysteresis)
+#include <cstdint>
+
+#include "sb_internal.cuh"
+#include "sb_ptx.cuh"
+
+namespace sb {
+
+// A step taken while 0 < dense_run < dense_check_every is dense without a gate look
+// (fused_engine.py:222-226).  Only finalize_kernel / set_mode_kernel change dense_run,
+// and they run after / outside the gate and list kernels of a step.
+SB_DEV bool in_hysteresis(const State* st) {
+  return st->dense_run > 0 && st->dense_run < st->check_every;
+}
+
+// ---------------------------------------------------------------- exact |fp16 diff| sums
+// |d| for fp16 d, as an integer multiple of 2^-24 (exact: every finite fp16 is one).
+SB_DEV uint64_t abs_h_fixed(uint16_t h) {
+  const uint32_t e = (h >> 10) & 0x1F, m = h & 0x3FF;
+  return e ? (uint64_t)(m | 0x400) << (e - 1) : (uint64_t)m;
+}
+
+// fp16(fp32(a) - fp32(b)) with IEEE round-to-nearest at both steps, as torch computes a
+// half-precision subtraction (fused_engine.py:142).
+SB_DEV uint16_t sub_h(uint16_t a, uint16_t b) {
+  const float fa = __half2float(__ushort_as_half(a)), fb = __half2float(__ushort_as_half(b));
+  return __half_as_ushort(__float2half_rn(__fsub_rn(fa, fb)));
+}
+
+// Flags for inf / NaN diffs: an fp32 sum with an inf term is inf (> any finite
+// threshold); with a NaN term the comparison is false.
+#define GATE_INF 1u
+#define GATE_NAN 2u
+
+SB_DEV void accum_h(uint16_t d, uint64_t& acc, uint32_t& flags) {
+  const uint16_t a = d & 0x7FFF;
+  if ((a >> 10) == 0x1F) {
+    flags |= (a & 0x3FF) ? GATE_NAN : GATE_INF;
+  } else {
+    acc += abs_h_fixed(a);
+  }
+}
+
+// Exact per-block change statistic.  One CTA per (block row, camera): reads the
+// block-row of the new frames and of the image cache with 16-byte coalesced loads,
+// sums |diff| per block exactly, thresholds, ORs `extra` and the refresh phase, then
+// copies the changed blocks of the new frames into the image cache.
+template <int KIND>  // 0: fp16 frames, 1: fp32 frames, 2: uint8 BGR frames (fused prep)
+__global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
+  if (in_hysteresis(a.st)) return;  // hysteresis dense step: the gate is not looked at (:222-226)
+  const int by = blockIdx.x, cam = blockIdx.y;
+  const int B = a.block;
+  extern __shared__ __align__(16) uint8_t gsm[];
+  unsigned long long* s_sum = reinterpret_cast<unsigned long long*>(gsm);  // [wb] fixed / bits of double
+  uint32_t* s_flag = reinterpret_cast<uint32_t*>(s_sum + a.wb);            // [wb]
+  __half* s_lut = reinterpret_cast<__half*>(s_flag + a.wb);                 // [3][256] (u8 path)
+  for (int i = threadIdx.x; i < a.wb; i += blockDim.x) {
+    s_sum[i] = 0ull;
+    s_flag[i] = 0u;
+  }
+  if (KIND == 2) {
+    // normalised value of every uint8 level per RGB channel, with the reference's ops:
+    // (x - mean[c]) / std[c] in fp32, then rounded to fp16 (video.py:99, :108)
+    for (int i = threadIdx.x; i < 768; i += blockDim.x) {
+      const int c = i >> 8, u = i & 255;
+      s_lut[i] = __float2half_rn(__fdiv_rn(__fsub_rn((float)u, a.mean[c]), a.stdv[c]));
+    }
+  }
+  __syncthreads();
+
+  const size_t row_px = (size_t)a.w;
+  const size_t img_row0 = ((size_t)cam * a.h + (size_t)by * B) * row_px * 3;  // element index
+  if (KIND == 0) {
+    // 16 B = 8 halves; a block row-segment is B*3*2/16 vectors
+    const int vpb = B * 3 / 8, vpr = vpb * a.wb;
+    const uint4* f = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.frames) + img_row0);
+    const uint4* g = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.img) + img_row0);
+    for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+      uint64_t acc = 0;
+      uint32_t flags = 0;
+#pragma unroll 4
+      for (int r = 0; r < B; ++r) {
+        const uint4 x = __ldg(f + (size_t)r * vpr + v);
+        const uint4 y = g[(size_t)r * vpr + v];
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          accum_h(sub_h(xs[k] & 0xFFFF, ys[k] & 0xFFFF), acc, flags);
+          accum_h(sub_h(xs[k] >> 16, ys[k] >> 16), acc, flags);
+        }
+      }
+      const int b = v / vpb;
+      atomicAdd(&s_sum[b], (unsigned long long)acc);
+      if (flags) atomicOr(&s_flag[b], flags);
+    }
+  } else if (KIND == 1) {
+    // fp32 frames: |f32 diff| summed in double (exact for frames within 2^29 of dynamic range)
+    const int vpb = B * 3 / 4, vpr = vpb * a.wb;
+    const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(a.frames) + img_row0);
+    const float4* g = reinterpret_cast<const float4*>(static_cast<const float*>(a.img) + img_row0);
+    double* s_d = reinterpret_cast<double*>(s_sum);
+    for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+      double acc = 0.0;
+#pragma unroll 4
+      for (int r = 0; r < B; ++r) {
+        const float4 x = __ldg(f + (size_t)r * vpr + v);
+        const float4 y = g[(size_t)r * vpr + v];
+        acc += (double)fabsf(__fsub_rn(x.x, y.x)) + (double)fabsf(__fsub_rn(x.y, y.y)) +
+               (double)fabsf(__fsub_rn(x.z, y.z)) + (double)fabsf(__fsub_rn(x.w, y.w));
+      }
+      atomicAdd(&s_d[v / vpb], acc);
+    }
+  } else {
+    // uint8 BGR: units of 16 pixels = 48 bytes of frame, 96 bytes of fp16 cache
+    const int upb = B / 16, upr = upb * a.wb;
+    const uint8_t* f = static_cast<const uint8_t*>(a.frames) + img_row0;
+    const __half* g = static_cast<const __half*>(a.img) + img_row0;
+    for (int u = threadIdx.x; u < upr; u += blockDim.x) {
+      uint64_t acc = 0;
+      uint32_t flags = 0;
+      for (int r = 0; r < B; ++r) {
+        const uint4* fp = reinterpret_cast<const uint4*>(f + (size_t)r * row_px * 3 + (size_t)u * 48);
+        const uint4* gp = reinterpret_cast<const uint4*>(g + (size_t)r * row_px * 3 + (size_t)u * 48);
+        uint4 fx[3], gx[6];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) fx[k] = __ldg(fp + k);
+#pragma unroll
+        for (int k = 0; k < 6; ++k) gx[k] = gp[k];
+        const uint8_t* fb = reinterpret_cast<const uint8_t*>(fx);
+        const uint16_t* gh = reinterpret_cast<const uint16_t*>(gx);
+#pragma unroll
+        for (int j = 0; j < 48; ++j) {
+          const int px = j / 3, c = j % 3;           // cache element j = pixel px, RGB channel c
+          const uint8_t q = fb[px * 3 + (2 - c)];    // BGR -> RGB (video.py:96 flip(-1))
+          const uint16_t hv = __half_as_ushort(s_lut[c * 256 + q]);
+          accum_h(sub_h(hv, gh[j]), acc, flags);
+        }
+      }
+      const int b = u / upb;
+      atomicAdd(&s_sum[b], (unsigned long long)acc);
+      if (flags) atomicOr(&s_flag[b], flags);
+    }
+  }
+  __syncthreads();
+
+  // threshold + extra + refresh (fused_engine.py:144-148)
+  const int64_t tick = a.st->tick;
+  for (int bx = threadIdx.x; bx < a.wb; bx += blockDim.x) {
+    const int64_t lin = ((int64_t)cam * a.hb + by) * a.wb + bx;
+    bool ch;
+    if (KIND == 1) {
+      const double s = reinterpret_cast<double*>(s_sum)[bx];
+      ch = s > a.thr;
+    } else {
+      const uint32_t fl = s_flag[bx];
+      if (fl & GATE_NAN) ch = false;
+      else if (fl & GATE_INF) ch = a.thr_fx < INT64_MAX;  // inf > finite thr; inf > inf is false
+      else ch = (int64_t)s_sum[bx] > a.thr_fx;
+    }
+    ch = ch || a.extra[lin] != 0;
+    if (a.refresh) ch = ch || (lin % a.refresh) == (tick % a.refresh);
+    a.changed[lin] = ch ? 1 : 0;
+    s_flag[bx] = ch ? 1u : 0u;  // reuse as the changed flag for the update below
+  }
+  __syncthreads();
+
+  // image-cache update for changed blocks (fused_engine.py:157-160)
+  if (KIND == 2) {
+    const int upb = B / 16, upr = upb * a.wb;
+    const uint8_t* f = static_cast<const uint8_t*>(a.frames) + img_row0;
+    __half* g = static_cast<__half*>(a.img) + img_row0;
+    for (int u = threadIdx.x; u < upr; u += blockDim.x) {
+      if (!s_flag[u / upb]) continue;
+      for (int r = 0; r < B; ++r) {
+        const uint4* fp = reinterpret_cast<const uint4*>(f + (size_t)r * row_px * 3 + (size_t)u * 48);
+        uint4* gp = reinterpret_cast<uint4*>(g + (size_t)r * row_px * 3 + (size_t)u * 48);
+        uint4 fx[3], gx[6];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) fx[k] = __ldg(fp + k);
+        const uint8_t* fb = reinterpret_cast<const uint8_t*>(fx);
+        uint16_t* gh = reinterpret_cast<uint16_t*>(gx);
+#pragma unroll
+        for (int j = 0; j < 48; ++j) {
+          const int px = j / 3, c = j % 3;
+          gh[j] = __half_as_ushort(s_lut[c * 256 + fb[px * 3 + (2 - c)]]);
+        }
+#pragma unroll
+        for (int k = 0; k < 6; ++k) gp[k] = gx[k];
+      }
+    }
+  } else {
+    const int esz = KIND == 0 ? 2 : 4;
+    const int vpb = B * 3 * esz / 16, vpr = vpb * a.wb;
+    const uint4* f = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.frames) + img_row0 * esz);
+    uint4* g = reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.img) + img_row0 * esz);
+    for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+      if (!s_flag[v / vpb]) continue;
+#pragma unroll 4
+      for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- dilation + ordered lists
+// One thread per block (flat index over all cameras), 1024 per CTA.  For each dilation d
+// the mask is max_pool2d(changed, 2d+1, 1, d) within the camera (fused_engine.py:151);
+// active blocks are compacted in ascending flat order (nonzero_static, :163) with a
+// warp ballot, a CTA prefix and a decoupled look-back across CTAs.  Chunks are taken by
+// ticket, so a CTA only ever waits on CTAs that are already running.
+#define LIST_THREADS 1024
+#define LB_FLAG_AGG 1ull
+#define LB_FLAG_INC 2ull
+
+SB_DEV unsigned long long lb_pack(uint32_t epoch, unsigned long long flag, uint32_t v) {
+  return ((unsigned long long)epoch << 32) | (flag << 30) | (unsigned long long)(v & 0x3FFFFFFFu);
+}
+SB_DEV void lb_store(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+SB_DEV unsigned long long lb_load(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
+  State* st = a.st;
+  if (in_hysteresis(st)) {  // hysteresis dense step: no gate, count -1 (fused_engine.py:222-226)
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      st->mode_cur = SB_MODE_DENSE;
+      st->count_cur = -1;
+    }
+    return;
+  }
+  __shared__ uint32_t s_chunk;
+  __shared__ uint32_t s_warp[SB_MAX_DILATIONS][32];
+  __shared__ uint32_t s_excl[SB_MAX_DILATIONS];
+  const uint32_t epoch = st->epoch;
+  if (threadIdx.x == 0) s_chunk = atomicAdd(&st->ticket, 1u);
+  __syncthreads();
+  const uint32_t chunk = s_chunk;
+  const int nchunks = gridDim.x;
+  const int f = (int)chunk * LIST_THREADS + threadIdx.x;
+  const int per = a.hb * a.wb;
+  const bool valid = f < a.n_blocks;
+  int cam = 0, by = 0, bx = 0;
+  if (valid) {
+    cam = f / per;
+    const int r = f - cam * per;
+    by = r / a.wb;
+    bx = r - by * a.wb;
+  }
+  const uint8_t* cm = a.changed + (size_t)cam * per;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t rank[SB_MAX_DILATIONS];
+  bool act[SB_MAX_DILATIONS];
+  for (int di = 0; di < a.n_dil; ++di) {
+    const int d = a.ds[di];
+    bool on = false;
+    if (valid) {
+      const int y0 = max(0, by - d), y1 = min(a.hb - 1, by + d);
+      const int x0 = max(0, bx - d), x1 = min(a.wb - 1, bx + d);
+      for (int y = y0; y <= y1 && !on; ++y)
+        for (int x = x0; x <= x1; ++x)
+          if (__ldg(cm + y * a.wb + x)) { on = true; break; }
+      a.masks[(size_t)di * a.n_blocks + f] = on ? 1 : 0;
+    }
+    act[di] = on;
+    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, on);
+    rank[di] = __popc(bal & ((1u << lane) - 1u));
+    if (lane == 0) s_warp[di][warp] = __popc(bal);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int di = 0; di < a.n_dil; ++di) {
+      const uint32_t v = s_warp[di][lane];
+      uint32_t inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= (uint32_t)o) inc += t;
+      }
+      s_warp[di][lane] = inc - v;  // exclusive warp offsets
+      const uint32_t agg = __shfl_sync(0xFFFFFFFFu, inc, 31);
+      // decoupled look-back: lane 0 publishes and walks predecessors
+      if (lane == 0) {
+        unsigned long long* stat = a.status + (size_t)di * nchunks;
+        uint32_t excl = 0;
+        if (chunk == 0) {
+          lb_store(stat, lb_pack(epoch, LB_FLAG_INC, agg));
+        } else {
+          lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_AGG, agg));
+          int p = (int)chunk - 1;
+          uint32_t spins = 0;
+          while (p >= 0) {
+            const unsigned long long w = lb_load(stat + p);
+            const uint32_t we = (uint32_t)(w >> 32);
+            const unsigned long long fl = (w >> 30) & 3ull;
+            if (we != epoch || fl == 0) {
+              if (++spins > SB_SPIN_LIMIT) {
+                atomicOr(&st->error, SB_ERR_TIMEOUT_LOOKBK);
+                break;
+              }
+              __nanosleep(32);
+              continue;
+            }
+            excl += (uint32_t)(w & 0x3FFFFFFFull);
+            if (fl == LB_FLAG_INC) break;
+            --p;
+          }
+          lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_INC, excl + agg));
+        }
+        s_excl[di] = excl;
+        if ((int)chunk == nchunks - 1) {
+          st->counts[di] = (int32_t)(excl + agg);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int di = 0; di < a.n_dil; ++di) {
+    if (!act[di]) continue;
+    const uint32_t pos = s_excl[di] + s_warp[di][warp] + rank[di];
+    if (pos < (uint32_t)a.n_blocks) {
+      int32_t* L = a.lists + (size_t)di * 3 * a.n_blocks;
+      L[pos] = cam;
+      L[a.n_blocks + pos] = by;
+      L[2 * (size_t)a.n_blocks + pos] = bx;
+    }
+  }
+  if ((int)chunk == nchunks - 1 && threadIdx.x == 0) {
+    __threadfence();
+    const int64_t k = st->counts[a.n_dil - 1];
+    st->count_cur = k;
+    st->mode_cur = k == 0 ? SB_MODE_SKIP : (k <= st->fallback ? SB_MODE_SPARSE : SB_MODE_DENSE);
+  }
+}
+
+// ---------------------------------------------------------------- img copies
+// Dense: img <- frames for every block when this step is dense (fused_engine.py:173).
+// Masked (calibration replays): img <- frames where `changed` (:157-160).
+__global__ void __launch_bounds__(256) copy_kernel(CopyArgs a) {
+  const int mode = a.st->mode_cur;
+  if (a.changed == nullptr && mode != SB_MODE_DENSE) return;
+  const int by = blockIdx.x, cam = blockIdx.y, B = a.block;
+  __shared__ __half s_lut[768];
+  if (a.u8) {
+    for (int i = threadIdx.x; i < 768; i += blockDim.x) {
+      const int c = i >> 8, u = i & 255;
+      s_lut[i] = __float2half_rn(__fdiv_rn(__fsub_rn((float)u, a.mean[c]), a.stdv[c]));
+    }
+    __syncthreads();
+  }
+  const size_t row0 = ((size_t)cam * a.h + (size_t)by * B) * a.w * 3;
+  const uint8_t* chg = a.changed ? a.changed + ((size_t)cam * a.hb + by) * a.wb : nullptr;
+  if (a.u8) {
+    const int upb = B / 16, upr = upb * a.wb;
+    const uint8_t* f = static_cast<const uint8_t*>(a.frames) + row0;
+    __half* g = static_cast<__half*>(a.img) + row0;
+    for (int u = threadIdx.x; u < upr; u += blockDim.x) {
+      if (chg && !chg[u / upb]) continue;
+      for (int r = 0; r < B; ++r) {
+        const uint4* fp = reinterpret_cast<const uint4*>(f + (size_t)r * a.w * 3 + (size_t)u * 48);
+        uint4* gp = reinterpret_cast<uint4*>(g + (size_t)r * a.w * 3 + (size_t)u * 48);
+        uint4 fx[3], gx[6];
+        for (int k = 0; k < 3; ++k) fx[k] = __ldg(fp + k);
+        const uint8_t* fb = reinterpret_cast<const uint8_t*>(fx);
+        uint16_t* gh = reinterpret_cast<uint16_t*>(gx);
+#pragma unroll
+        for (int j = 0; j < 48; ++j) {
+          const int px = j / 3, c = j % 3;
+          gh[j] = __half_as_ushort(s_lut[c * 256 + fb[px * 3 + (2 - c)]]);
+        }
+        for (int k = 0; k < 6; ++k) gp[k] = gx[k];
+      }
+    }
+  } else {
+    const int vpb = B * 3 * a.elem_bytes / 16, vpr = vpb * a.wb;
+    const uint4* f = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.frames) + row0 * a.elem_bytes);
+    uint4* g = reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.img) + row0 * a.elem_bytes);
+    for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+      if (chg && !chg[v / vpb]) continue;
+#pragma unroll 4
+      for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- state machine
+// End of a step (fused_engine.py:222-240): tick, hysteresis, stats, result slot.
+__global__ void finalize_kernel(State* st, int refresh, int32_t* host_out) {
+  if (threadIdx.x != 0) return;
+  const int mode = st->mode_cur;
+  if (in_hysteresis(st)) {
+    st->dense_run += 1;
+  } else {
+    if (refresh) st->tick += 1;
+    st->dense_run = mode == SB_MODE_DENSE ? 1 : 0;
+  }
+  st->stats[mode] += 1;
+  st->last_mode = mode;
+  st->last_count = st->count_cur;
+  st->result[0] = mode;
+  st->result[1] = st->count_cur;
+  st->epoch = st->epoch + 1u == 0u ? 1u : st->epoch + 1u;
+  st->ticket = 0u;
+  if (host_out) {
+    host_out[0] = mode;
+    host_out[1] = (int32_t)st->count_cur;
+    host_out[2] = st->error;
+    host_out[3] = 1;  // written
+  }
+}
+
+// Reset / dense replay / calibration: force the mode of the conv sequence.
+__global__ void set_mode_kernel(State* st, int mode, int reset_hyst, int64_t force_tiles) {
+  if (threadIdx.x != 0) return;
+  st->mode_cur = mode;
+  st->force_tiles = (int32_t)force_tiles;
+  if (reset_hyst) st->dense_run = 0;
+}
+
+// ---------------------------------------------------------------- launchers
+cudaError_t launch_gate(const GateArgs& a, int kind, cudaStream_t s) {
+  dim3 grid(a.hb, a.n);
+  const size_t smem = (size_t)a.wb * (8 + 4) + 768 * 2 + 16;
+  switch (kind) {
+    case 0: gate_kernel<0><<<grid, 256, smem, s>>>(a); break;
+    case 1: gate_kernel<1><<<grid, 256, smem, s>>>(a); break;
+    default: gate_kernel<2><<<grid, 256, smem, s>>>(a); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lists(const ListArgs& a, int n_chunks, cudaStream_t s) {
+  lists_kernel<<<n_chunks, LIST_THREADS, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_copy(const CopyArgs& a, cudaStream_t s) {
+  copy_kernel<<<dim3(a.hb, a.n), 256, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_finalize(State* st, int refresh, int32_t* host_out, cudaStream_t s) {
+  finalize_kernel<<<1, 32, 0, s>>>(st, refresh, host_out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_set_mode(State* st, int mode, int reset_hyst, int64_t force_tiles, cudaStream_t s) {
+  set_mode_kernel<<<1, 32, 0, s>>>(st, mode, reset_hyst, force_tiles);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

@@ -1,0 +1,106 @@
+// sb_internal.cuh -- device state, kernel arguments and launcher declarations shared by
+// the engine (sb_engine.cu) and the kernels (sb_gate.cu, sb_conv_tc.cu, sb_conv_simt.cu).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/sarbon_sparse.h"
+
+namespace sb {
+
+// Device-resident engine state.  Written only by the engine's own kernels (and by
+// cudaMemcpyAsync for host-set knobs), so a whole step runs without a host sync.
+struct State {
+  int64_t tick;         // refresh phase counter (fused_engine.py:80,146-147)
+  int64_t count_cur;    // active count of the widest dilation this step; -1 = hysteresis dense
+  int64_t fallback;     // dense above this count (fused_engine.py:89,232)
+  int64_t stats[3];     // skip / sparse / dense steps (fused_engine.py:92,239)
+  int64_t last_count;
+  int32_t counts[SB_MAX_DILATIONS];  // active blocks per dilation this step
+  int32_t mode_cur;     // SB_MODE_* of this step (read by the conv kernels)
+  int32_t hyst_unused;
+  int32_t dense_run;    // fused_engine.py:91 `_dense_run`
+  int32_t check_every;  // fused_engine.py:91 `dense_check_every`
+  int32_t force_tiles;  // >0: conv kernels process exactly this many list entries
+  uint32_t epoch;       // tag of the block-list look-back words (never 0)
+  uint32_t ticket;      // chunk ticket of the list kernel
+  int32_t error;        // sticky SB_ERR_* flags
+  int32_t last_mode;
+  int32_t pad_;
+  int64_t result[2];    // {mode, count} of the last finished step
+};
+
+struct GateArgs {
+  const void* frames;      // [N][H][W][3]: fp16, fp32 or uint8 BGR
+  void* img;               // image cache [N][H][W][3] in the engine dtype
+  const uint8_t* extra;    // [N][Hb][Wb]
+  uint8_t* changed;        // [N][Hb][Wb]
+  State* st;
+  int n, h, w, hb, wb, block;
+  int64_t thr_fx;          // floor(threshold * 2^24) (fp16/u8 paths); -1: always; INT64_MAX: never
+  double thr;              // threshold as a double (fp32 path)
+  int refresh;
+  float mean[3], stdv[3];  // u8 path normalisation (RGB order)
+};
+
+struct ListArgs {
+  const uint8_t* changed;  // [n_blocks]
+  uint8_t* masks;          // [n_dil][n_blocks]
+  int32_t* lists;          // [n_dil][3][n_blocks] (cam, by, bx)
+  unsigned long long* status;  // [n_dil][n_chunks] look-back words
+  State* st;
+  int n_blocks, hb, wb, n_dil;
+  int ds[SB_MAX_DILATIONS];
+};
+
+struct CopyArgs {          // dense img copy or masked update
+  const void* frames;
+  void* img;
+  const uint8_t* changed;  // masked update when non-null
+  State* st;
+  int n, h, w, hb, wb, block, elem_bytes;
+  int u8;                  // frames are uint8 BGR (normalise)
+  float mean[3], stdv[3];
+};
+
+struct ConvArgs {
+  const void* x;           // src cache (used directly by the gather producers)
+  void* y;                 // dst cache
+  const void* res;         // residual cache or nullptr
+  const float* bias;       // [cout] fp32
+  const void* wimg;        // fp16 path: pre-swizzled weight image; fp32 path: w [3][3][cin][cout]
+  const int32_t* lcam;
+  const int32_t* lby;
+  const int32_t* lbx;
+  State* st;
+  int d_idx;
+  int n, hx, wx, cin;
+  int ho, wo, cout;
+  int hb, wb, n_blocks;
+  int t, s, act;
+};
+
+// ---------------------------------------------------------------- launchers
+cudaError_t launch_gate(const GateArgs& a, int kind /*0 f16, 1 f32, 2 u8*/, cudaStream_t s);
+cudaError_t launch_lists(const ListArgs& a, int n_chunks, cudaStream_t s);
+cudaError_t launch_copy(const CopyArgs& a, cudaStream_t s);
+cudaError_t launch_finalize(State* st, int refresh, int32_t* host_out, cudaStream_t s);
+cudaError_t launch_set_mode(State* st, int mode, int reset_hyst, int64_t force_tiles, cudaStream_t s);
+
+// fp16 tcgen05 path.  Returns cudaErrorInvalidValue for shapes without an instantiation.
+bool conv_tc_supported(int cin, int cout, int t, int s);
+int conv_tc_nsplit(int cin, int cout, int t, int s);   // CTA splits of cout
+size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s);  // all splits
+void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w /*[3][3][cin][cout]*/,
+                        uint16_t* out /* fp16 bits */);
+cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t,
+                              int s);
+cudaError_t launch_conv_tc(const ConvArgs& a, const CUtensorMap* map, int grid_x, cudaStream_t s);
+int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s);
+
+// fp32 CUDA-core path
+cudaError_t launch_conv_simt(const ConvArgs& a, int grid_x, cudaStream_t s);
+
+}  // namespace sb

@@ -1,0 +1,165 @@
+// sb_ptx.cuh -- thin inline-PTX wrappers for sm_100a: mbarriers with bounded waits,
+// TMA tile loads, bulk copies and tcgen05 (TMEM alloc, MMA, commit, loads).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#define SB_DEV __device__ __forceinline__
+
+// Sticky device error flags (OR-ed into the engine state's `error` word).
+#define SB_ERR_TIMEOUT_FULL   0x01
+#define SB_ERR_TIMEOUT_EMPTY  0x02
+#define SB_ERR_TIMEOUT_ACC    0x04
+#define SB_ERR_TIMEOUT_LOOKBK 0x08
+#define SB_ERR_TIMEOUT_WGT    0x10
+#define SB_ERR_BAD_TILE       0x20
+
+// Poll limit for every spin-wait: ~2^24 polls with a 64 ns back-off is >1 s,
+// orders of magnitude above any legitimate wait inside one kernel.
+#define SB_SPIN_LIMIT (1u << 24)
+
+namespace sb {
+
+SB_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+SB_DEV uint32_t lane_id() { return threadIdx.x & 31; }
+SB_DEV uint32_t warp_id() { return threadIdx.x >> 5; }
+
+// ---------------------------------------------------------------- mbarrier
+SB_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+SB_DEV void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+SB_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+SB_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+SB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity.  Returns false after
+// SB_SPIN_LIMIT polls or as soon as *abort is set by another thread of the CTA.
+SB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t i = 0; i < SB_SPIN_LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (i > 64) __nanosleep(64);
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------- proxies / fences
+SB_DEV void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- TMA / bulk copies
+SB_DEV void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                        int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+SB_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+SB_DEV void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+// Allocate `ncols` TMEM columns (power of two >= 32); the base address lands in *dst (smem).
+// Executed by one full warp.
+SB_DEV void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+SB_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+SB_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+SB_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+SB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (fp16 inputs, fp32 accumulate).
+SB_DEV void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive once on `bar` when all prior tcgen05 async ops of this thread have completed.
+SB_DEV void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+// 32 lanes x 32 bit, 16 consecutive columns: thread i of the warp gets lane (base_lane + i).
+SB_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+SB_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for tcgen05 (K-major operand, swizzled rows).
+//   swz_mode: 2 = 128B swizzle (rows of 128 B), 4 = 64B swizzle (rows of 64 B).
+//   sbo: byte distance between consecutive 8-row groups.
+SB_DEV uint64_t smem_desc(uint32_t saddr, uint32_t sbo, uint32_t swz_mode) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);        // start address  [0,14)
+  d |= (uint64_t)(16u >> 4) << 16;                 // leading byte offset (unused when swizzled)
+  d |= (uint64_t)((sbo & 0x3FFFFu) >> 4) << 32;    // stride byte offset [32,46)
+  d |= (uint64_t)1 << 46;                          // descriptor version (sm100)
+  d |= (uint64_t)(swz_mode & 7u) << 61;            // layout / swizzle [61,64)
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with fp16 A/B, fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+  return (1u << 4)                       // D format: f32
+         | (0u << 7) | (0u << 10)         // A, B format: f16
+         | (0u << 15) | (0u << 16)        // A, B K-major
+         | ((uint32_t)(N >> 3) << 17)     // N >> 3
+         | ((uint32_t)(M >> 4) << 24);    // M >> 4
+}
+
+// ---------------------------------------------------------------- misc
+SB_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+SB_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+}  // namespace sb
