@@ -265,7 +265,9 @@ class OracleEngine:
         self.extra = np.zeros((self.n, self.hb, self.wb), bool)
         self.changed = np.zeros_like(self.extra)
         self.masks = {d: np.zeros_like(self.extra) for d in self.ds}
-        self.tick = 0
+        # the reference warms its gate graph up once at construction (fused_engine.py:85,
+        # 130-132), which runs `tick += 1` (:147): the first real step sees tick == 1
+        self.tick = 1
         self.buckets = budget_buckets(self.n_blocks)
         self.fallback = self.buckets[-1]
         self._dense_run = 0

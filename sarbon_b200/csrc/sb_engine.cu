@@ -60,6 +60,7 @@ struct sb_engine {
   int refresh = 0;
   int64_t thr_fx = 0;
   double thr = 0.0;
+  double band_lo = 0.0, band_hi = 0.0;
   int n_layers = 0;
   sb_layer_desc layers[SB_MAX_LAYERS];
   int nd = 0;
@@ -184,6 +185,8 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
   g.block = e->block;
   g.thr_fx = e->thr_fx;
   g.thr = e->thr;
+  g.band_lo = e->band_lo;
+  g.band_hi = e->band_hi;
   g.refresh = e->refresh;
   for (int c = 0; c < 3; ++c) {
     g.mean[c] = mean ? mean[c] : 0.f;
@@ -314,6 +317,17 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
   else if (std::isinf(thr32) || (double)thr32 * 16777216.0 >= 9.0e18) e->thr_fx = INT64_MAX;
   else e->thr_fx = (int64_t)std::floor((double)thr32 * 16777216.0);
   if (std::isnan(thr32)) e->thr = INFINITY;  // sum > NaN is false for every block
+  // A recursive fp32 sum of n non-negative fp16 terms is within (n-1)*2^-24 relative of the
+  // exact sum (any order); twice that margin decides the comparison from the fp32 sum.
+  const double gam = 2.0 * 3.0 * block * block * std::ldexp(1.0, -24);
+  if (std::isnan(thr32) || std::isinf(thr32) && thr32 > 0) {
+    e->band_lo = e->band_hi = INFINITY;                // only inf / NaN sums reach the exact path
+  } else if (thr32 < 0.f) {
+    e->band_lo = e->band_hi = -1.0;                    // every block changes
+  } else {
+    e->band_lo = (double)thr32 * (1.0 - gam);
+    e->band_hi = (double)thr32 * (1.0 + gam);
+  }
   // caches: id 0 = image, id i+1 = layer i output
   e->shape[0][0] = n_streams;
   e->shape[0][1] = height;
@@ -373,6 +387,9 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
   if ((rc = alloc_dev(e, (void**)&e->st, sizeof(State)))) return bail(rc);
   State init{};
   init.epoch = 1;
+  // The reference warms its gate graph up once at construction (fused_engine.py:85,130-132),
+  // which executes `tick += 1` (:147): its first gated step sees tick == 1.
+  init.tick = 1;
   init.fallback = budget_buckets(e->n_blocks).back();
   init.check_every = dense_check_every;
   init.mode_cur = SB_MODE_SKIP;

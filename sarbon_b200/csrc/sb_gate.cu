@@ -48,23 +48,45 @@ SB_DEV void accum_h(uint16_t d, uint64_t& acc, uint32_t& flags) {
   }
 }
 
-// Exact per-block change statistic.  One CTA per (block row, camera): reads the
-// block-row of the new frames and of the image cache with 16-byte coalesced loads,
-// sums |diff| per block exactly, thresholds, ORs `extra` and the refresh phase, then
-// copies the changed blocks of the new frames into the image cache.
+SB_DEV uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+SB_DEV __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Sum of |a - b| over the two fp16 lanes of a 32-bit word, widened to fp32.  __hsub2
+// rounds the exact difference to fp16 once; for fp16 operands that equals torch's
+// fp16(fp32(a) - fp32(b)) (the fp32 step is exact unless the exponent gap exceeds 13
+// bits, and then both round back to the larger operand).
+SB_DEV float absdiff2(uint32_t x, uint32_t y) {
+  const uint32_t d = h2_bits(__hsub2(bits_h2(x), bits_h2(y))) & 0x7FFF7FFFu;
+  const float2 f = __half22float2(bits_h2(d));
+  return f.x + f.y;
+}
+
+// Per-block change statistic.  One CTA per (block row, camera): reads the block row of
+// the new frames and of the image cache with 16-byte coalesced loads and sums |diff| per
+// block in fp32.  The fp32 sum of n non-negative terms is within (n-1)*2^-24 relative of
+// the exact sum, so it decides `sum > thr` exactly unless it falls inside that band
+// around the threshold; only those (rare) blocks are re-summed exactly, in integer
+// multiples of 2^-24.  The result equals an exact comparison (the reference sums in fp32
+// in torch's order, fused_engine.py:142-144).  Then `| extra`, the refresh phase, and the
+// changed blocks of the new frames are copied into the image cache.
 template <int KIND>  // 0: fp16 frames, 1: fp32 frames, 2: uint8 BGR frames (fused prep)
 __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
   if (in_hysteresis(a.st)) return;  // hysteresis dense step: the gate is not looked at (:222-226)
   const int by = blockIdx.x, cam = blockIdx.y;
   const int B = a.block;
   extern __shared__ __align__(16) uint8_t gsm[];
-  unsigned long long* s_sum = reinterpret_cast<unsigned long long*>(gsm);  // [wb] fixed / bits of double
-  uint32_t* s_flag = reinterpret_cast<uint32_t*>(s_sum + a.wb);            // [wb]
-  __half* s_lut = reinterpret_cast<__half*>(s_flag + a.wb);                 // [3][256] (u8 path)
+  unsigned long long* s_sx = reinterpret_cast<unsigned long long*>(gsm);  // [wb] exact sums (or double)
+  float* s_sf = reinterpret_cast<float*>(s_sx + a.wb);                    // [wb] fp32 sums
+  uint32_t* s_flag = reinterpret_cast<uint32_t*>(s_sf + a.wb);           // [wb]
+  int* s_amb = reinterpret_cast<int*>(s_flag + a.wb);                    // [wb] ambiguous blocks
+  __half* s_lut = reinterpret_cast<__half*>(s_amb + a.wb);               // [3][256] (u8 path)
+  __shared__ int s_namb;
   for (int i = threadIdx.x; i < a.wb; i += blockDim.x) {
-    s_sum[i] = 0ull;
+    s_sx[i] = 0ull;
+    s_sf[i] = 0.f;
     s_flag[i] = 0u;
   }
+  if (threadIdx.x == 0) s_namb = 0;
   if (KIND == 2) {
     // normalised value of every uint8 level per RGB channel, with the reference's ops:
     // (x - mean[c]) / std[c] in fp32, then rounded to fp16 (video.py:99, :108)
@@ -83,29 +105,21 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
     const uint4* f = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.frames) + img_row0);
     const uint4* g = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.img) + img_row0);
     for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
-      uint64_t acc = 0;
-      uint32_t flags = 0;
-#pragma unroll 4
+      float acc = 0.f;
+#pragma unroll 8
       for (int r = 0; r < B; ++r) {
         const uint4 x = __ldg(f + (size_t)r * vpr + v);
         const uint4 y = g[(size_t)r * vpr + v];
-        const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          accum_h(sub_h(xs[k] & 0xFFFF, ys[k] & 0xFFFF), acc, flags);
-          accum_h(sub_h(xs[k] >> 16, ys[k] >> 16), acc, flags);
-        }
+        acc += (absdiff2(x.x, y.x) + absdiff2(x.y, y.y)) + (absdiff2(x.z, y.z) + absdiff2(x.w, y.w));
       }
-      const int b = v / vpb;
-      atomicAdd(&s_sum[b], (unsigned long long)acc);
-      if (flags) atomicOr(&s_flag[b], flags);
+      atomicAdd(&s_sf[v / vpb], acc);
     }
   } else if (KIND == 1) {
     // fp32 frames: |f32 diff| summed in double (exact for frames within 2^29 of dynamic range)
     const int vpb = B * 3 / 4, vpr = vpb * a.wb;
     const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(a.frames) + img_row0);
     const float4* g = reinterpret_cast<const float4*>(static_cast<const float*>(a.img) + img_row0);
-    double* s_d = reinterpret_cast<double*>(s_sum);
+    double* s_d = reinterpret_cast<double*>(s_sx);
     for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
       double acc = 0.0;
 #pragma unroll 4
@@ -123,8 +137,8 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
     const uint8_t* f = static_cast<const uint8_t*>(a.frames) + img_row0;
     const __half* g = static_cast<const __half*>(a.img) + img_row0;
     for (int u = threadIdx.x; u < upr; u += blockDim.x) {
-      uint64_t acc = 0;
-      uint32_t flags = 0;
+      float acc = 0.f;
+#pragma unroll 2
       for (int r = 0; r < B; ++r) {
         const uint4* fp = reinterpret_cast<const uint4*>(f + (size_t)r * row_px * 3 + (size_t)u * 48);
         const uint4* gp = reinterpret_cast<const uint4*>(g + (size_t)r * row_px * 3 + (size_t)u * 48);
@@ -133,41 +147,102 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
         for (int k = 0; k < 3; ++k) fx[k] = __ldg(fp + k);
 #pragma unroll
         for (int k = 0; k < 6; ++k) gx[k] = gp[k];
-        const uint8_t* fb = reinterpret_cast<const uint8_t*>(fx);
-        const uint16_t* gh = reinterpret_cast<const uint16_t*>(gx);
+        const uint32_t* fw = reinterpret_cast<const uint32_t*>(fx);
+        const uint32_t* gw = reinterpret_cast<const uint32_t*>(gx);
 #pragma unroll
-        for (int j = 0; j < 48; ++j) {
-          const int px = j / 3, c = j % 3;           // cache element j = pixel px, RGB channel c
-          const uint8_t q = fb[px * 3 + (2 - c)];    // BGR -> RGB (video.py:96 flip(-1))
-          const uint16_t hv = __half_as_ushort(s_lut[c * 256 + q]);
-          accum_h(sub_h(hv, gh[j]), acc, flags);
+        for (int j = 0; j < 24; ++j) {  // cache elements 2j, 2j+1 = (pixel, RGB channel)
+          uint32_t hv = 0;
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int el = 2 * j + e, px = el / 3, c = el % 3, byte = px * 3 + (2 - c);  // BGR -> RGB
+            const uint32_t q = (fw[byte >> 2] >> ((byte & 3) * 8)) & 0xFFu;
+            hv |= (uint32_t)__half_as_ushort(s_lut[c * 256 + q]) << (16 * e);
+          }
+          acc += absdiff2(hv, gw[j]);
         }
       }
-      const int b = u / upb;
-      atomicAdd(&s_sum[b], (unsigned long long)acc);
-      if (flags) atomicOr(&s_flag[b], flags);
+      atomicAdd(&s_sf[u / upb], acc);
     }
   }
   __syncthreads();
 
-  // threshold + extra + refresh (fused_engine.py:144-148)
+  // classify with the fp32 sums; collect the blocks inside the rounding band
+  for (int bx = threadIdx.x; bx < a.wb; bx += blockDim.x) {
+    uint32_t cls;  // 0 unchanged, 1 changed, 2 ambiguous
+    if (KIND == 1) {
+      cls = reinterpret_cast<double*>(s_sx)[bx] > a.thr ? 1u : 0u;
+    } else {
+      const float sf = s_sf[bx];
+      if (isnan(sf)) cls = 0u;                         // NaN > thr is false
+      else if (sf == 0.f) cls = a.thr_fx < 0 ? 1u : 0u;  // every term was 0: the sum is exactly 0
+      else if ((double)sf > a.band_hi) cls = 1u;
+      else if ((double)sf < a.band_lo) cls = 0u;
+      else cls = 2u;
+    }
+    s_flag[bx] = cls;
+    if (cls == 2u) s_amb[atomicAdd(&s_namb, 1)] = bx;
+  }
+  __syncthreads();
+
+  // exact re-sum of the ambiguous blocks (integer multiples of 2^-24, order-free)
+  if (KIND != 1) {
+    const int namb = s_namb;
+    for (int ai = 0; ai < namb; ++ai) {
+      const int bx = s_amb[ai];
+      uint64_t acc = 0;
+      uint32_t flags = 0;
+      if (KIND == 0) {
+        const int vpb = B * 3 / 8, vpr = vpb * a.wb;
+        const uint4* f = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.frames) + img_row0);
+        const uint4* g = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.img) + img_row0);
+        for (int it = threadIdx.x; it < B * vpb; it += blockDim.x) {
+          const int r = it / vpb, v = bx * vpb + it % vpb;
+          const uint4 x = __ldg(f + (size_t)r * vpr + v), y = g[(size_t)r * vpr + v];
+          const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            accum_h(sub_h(xs[k] & 0xFFFF, ys[k] & 0xFFFF), acc, flags);
+            accum_h(sub_h(xs[k] >> 16, ys[k] >> 16), acc, flags);
+          }
+        }
+      } else {
+        const int upb = B / 16;
+        const uint8_t* f = static_cast<const uint8_t*>(a.frames) + img_row0;
+        const __half* g = static_cast<const __half*>(a.img) + img_row0;
+        for (int it = threadIdx.x; it < B * upb * 48; it += blockDim.x) {
+          const int r = it / (upb * 48), rem = it % (upb * 48), u = bx * upb + rem / 48, el = rem % 48;
+          const int px = el / 3, c = el % 3;
+          const uint8_t q = __ldg(f + (size_t)r * row_px * 3 + (size_t)u * 48 + px * 3 + (2 - c));
+          const uint16_t hv = __half_as_ushort(s_lut[c * 256 + q]);
+          const uint16_t gv = __half_as_ushort(g[(size_t)r * row_px * 3 + (size_t)u * 48 + el]);
+          accum_h(sub_h(hv, gv), acc, flags);
+        }
+      }
+      atomicAdd(&s_sx[bx], (unsigned long long)acc);
+      if (flags) atomicOr(&s_flag[bx], flags << 2);
+    }
+    __syncthreads();
+    for (int ai = threadIdx.x; ai < namb; ai += blockDim.x) {
+      const int bx = s_amb[ai];
+      const uint32_t fl = s_flag[bx] >> 2;
+      bool ch;
+      if (fl & GATE_NAN) ch = false;
+      else if (fl & GATE_INF) ch = a.thr_fx < INT64_MAX;  // inf > finite thr; inf > inf is false
+      else ch = (int64_t)s_sx[bx] > a.thr_fx;
+      s_flag[bx] = ch ? 1u : 0u;
+    }
+    __syncthreads();
+  }
+
+  // extra + refresh (fused_engine.py:144-148)
   const int64_t tick = a.st->tick;
   for (int bx = threadIdx.x; bx < a.wb; bx += blockDim.x) {
     const int64_t lin = ((int64_t)cam * a.hb + by) * a.wb + bx;
-    bool ch;
-    if (KIND == 1) {
-      const double s = reinterpret_cast<double*>(s_sum)[bx];
-      ch = s > a.thr;
-    } else {
-      const uint32_t fl = s_flag[bx];
-      if (fl & GATE_NAN) ch = false;
-      else if (fl & GATE_INF) ch = a.thr_fx < INT64_MAX;  // inf > finite thr; inf > inf is false
-      else ch = (int64_t)s_sum[bx] > a.thr_fx;
-    }
+    bool ch = s_flag[bx] == 1u;
     ch = ch || a.extra[lin] != 0;
     if (a.refresh) ch = ch || (lin % a.refresh) == (tick % a.refresh);
     a.changed[lin] = ch ? 1 : 0;
-    s_flag[bx] = ch ? 1u : 0u;  // reuse as the changed flag for the update below
+    s_flag[bx] = ch ? 1u : 0u;  // the changed flag for the update below
   }
   __syncthreads();
 
@@ -430,7 +505,7 @@ __global__ void set_mode_kernel(State* st, int mode, int reset_hyst, int64_t for
 // ---------------------------------------------------------------- launchers
 cudaError_t launch_gate(const GateArgs& a, int kind, cudaStream_t s) {
   dim3 grid(a.hb, a.n);
-  const size_t smem = (size_t)a.wb * (8 + 4) + 768 * 2 + 16;
+  const size_t smem = (size_t)a.wb * (8 + 4 + 4 + 4) + 768 * 2 + 16;
   switch (kind) {
     case 0: gate_kernel<0><<<grid, 256, smem, s>>>(a); break;
     case 1: gate_kernel<1><<<grid, 256, smem, s>>>(a); break;

@@ -41,6 +41,7 @@ struct GateArgs {
   int n, h, w, hb, wb, block;
   int64_t thr_fx;          // floor(threshold * 2^24) (fp16/u8 paths); -1: always; INT64_MAX: never
   double thr;              // threshold as a double (fp32 path)
+  double band_lo, band_hi; // fp32 sums outside [band_lo, band_hi] decide `sum > thr` exactly
   int refresh;
   float mean[3], stdv[3];  // u8 path normalisation (RGB order)
 };
