@@ -55,7 +55,13 @@ struct TcCfg {
   static constexpr int TMEM_COLS = (2 * NCTA) <= 32 ? 32 : (2 * NCTA) <= 64 ? 64 : (2 * NCTA) <= 128 ? 128 : (2 * NCTA) <= 256 ? 256 : 512;
   static constexpr int W_OFF = 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
-  static constexpr int FIXED = 1024 /*align slack*/ + NCTA * 4 + 256 /*barriers*/;
+  static constexpr int BIAS_BYTES = NCTA * 4;
+  static constexpr int BAR_BYTES = 256;
+  // first layer: staged input window of one M-tile (BOX_ROWS output rows of one tile)
+  static constexpr int WIN_ROWS = (BOX_ROWS - 1) * S + 3;
+  static constexpr int WIN_COLS = (T - 1) * S + 3;
+  static constexpr int WIN_BYTES = MANUAL ? ((WIN_ROWS * WIN_COLS * CIN * 2 + 15) / 16) * 16 : 0;
+  static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM = FIXED + A_OFF + STAGES * A_STAGE;
@@ -64,6 +70,7 @@ struct TcCfg {
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(NCTA % 16 == 0 && NCTA >= 16 && NCTA <= 256, "UMMA N");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
+  static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
 };
 
 struct TileXY {
@@ -195,16 +202,30 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
       }
     } else if (C::MANUAL && warp >= 6) {
       // ------------------------------------------------ gather producers (first layer)
+      // Per M-tile: stage the input window (with the image-border zero padding) in shared
+      // memory with coalesced loads, then build each A row (one output pixel: 3x3 taps x
+      // channels, zero-padded to KPAD) from it.
       const int r = threadIdx.x - 192;  // A row = output pixel slot, 0..127
       const __half* x = static_cast<const __half*>(a.x);
+      __half* win = reinterpret_cast<__half*>(sA + C::STAGES * C::A_STAGE + C::BIAS_BYTES + C::BAR_BYTES);
+      constexpr int RW = C::WIN_ROWS, WW = C::WIN_COLS, ROWE = WW * CIN;
       uint32_t g = 0;
       for (int it = 0; it < my_tiles && !*abort_flag; ++it, ++g) {
         const int m = blockIdx.x + it * gridDim.x;
-        int ti, p;
-        if (C::TT >= 128) { ti = m / C::MPT; p = (m % C::MPT) * 128 + r; }
-        else { ti = m * C::TPM + r / C::TT; p = r % C::TT; }
+        const int ti = m / C::MPT, sub = m % C::MPT;
         const TileXY tc = tile_at(a, mode, listed, ti < n_tiles ? ti : 0);
-        const int gy = tc.by * T + p / T, gx = tc.bx * T + p % T;
+        const int iy0 = (tc.by * T + sub * C::BOX_ROWS) * S - 1, ix0 = tc.bx * T * S - 1;
+        const __half* xc = x + (size_t)tc.cam * a.hx * a.wx * CIN;
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // previous window fully consumed
+        for (int idx = r; idx < RW * ROWE; idx += 128) {
+          const int wy = idx / ROWE, e = idx - wy * ROWE;
+          const int iy = iy0 + wy, ix = ix0 + e / CIN;
+          __half v = __ushort_as_half(0);
+          if (iy >= 0 && iy < a.hx && ix >= 0 && ix < a.wx)
+            v = __ldg(xc + ((size_t)iy * a.wx + ix) * CIN + (e % CIN));
+          win[idx] = v;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // window complete
         const int s = g % C::STAGES;
         const uint32_t ph = (g / C::STAGES) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
@@ -212,22 +233,17 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
           *abort_flag = 1;
           break;
         }
+        const int lr = r / T, lc = r % T;
+        const uint16_t* wrow = reinterpret_cast<const uint16_t*>(win) + (lr * S) * ROWE + (lc * S) * CIN;
         uint16_t v[C::KPAD > 0 ? C::KPAD : 16];
 #pragma unroll
         for (int k = 0; k < C::KPAD; ++k) v[k] = 0;
 #pragma unroll
-        for (int ky = 0; ky < 3; ++ky) {
-          const int iy = gy * S + ky - 1;
+        for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
-          for (int kx = 0; kx < 3; ++kx) {
-            const int ix = gx * S + kx - 1;
-            if (iy >= 0 && iy < a.hx && ix >= 0 && ix < a.wx) {
-              const __half* px = x + (((size_t)tc.cam * a.hx + iy) * a.wx + ix) * CIN;
+          for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-              for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = __half_as_ushort(__ldg(px + c));
-            }
-          }
-        }
+            for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = wrow[ky * ROWE + kx * CIN + c];
         uint8_t* row = sA + s * C::A_STAGE + r * C::ROWB;
         constexpr int NQ = C::ROWB / 16;
 #pragma unroll
@@ -511,7 +527,13 @@ cudaError_t launch_conv_tc(const ConvArgs& a, const CUtensorMap* map, int grid_x
     if (e != cudaSuccess) return e;
     attr_done[idx] = true;
   }
-  dim3 grid(grid_x, a.cout / v->ncta);
+  static int occ[16] = {};
+  if (occ[idx] == 0) {
+    int o = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, v->fn, v->threads, v->smem) != cudaSuccess || o < 1) o = 1;
+    occ[idx] = o;
+  }
+  dim3 grid(grid_x * occ[idx], a.cout / v->ncta);
   CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));
   v->fn<<<grid, v->threads, v->smem, st>>>(a, map ? *map : dummy);
