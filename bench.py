@@ -295,6 +295,7 @@ def run_b200(args):
 
     # --- per-kernel roofline pass (events around every launch; separate from the timing)
     prof = {"gate": 0.0, "lists": 0.0, "copy": 0.0, "conv": 0.0, "finalize": 0.0}
+    per_layer = [0.0] * len(eng.layers)
     conv_flops, gbytes, nprof = 0, 0, 0
     eng.reset(seq[0])
     for i in range(args.profile_steps):
@@ -305,6 +306,8 @@ def run_b200(args):
         prof["lists"] += kms[1]
         prof["copy"] += kms[2]
         prof["conv"] += sum(kms[3:3 + len(eng.layers)])
+        for j in range(len(eng.layers)):
+            per_layer[j] += kms[3 + j]
         prof["finalize"] += kms[3 + len(eng.layers)]
         conv_flops += layer_flops(eng, counts, mode) if mode != "skip" else 0
         gbytes += gate_bytes(eng, int(eng.changed.sum().item()))
@@ -394,6 +397,7 @@ def run_b200(args):
                        "l2": f"no flush: each step reads {S * H * W * 6 / 1e6:.0f} MB of new frames + "
                              f"the image cache (> 126 MB L2)"},
             "roofline": roof, "roofline_gate": roof_gate, "kernel_time_share": share,
+            "conv_us_per_layer": {l.dst: round(1e3 * t / max(nprof, 1), 1) for l, t in zip(eng.layers, per_layer)},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clock_info}
     print(json.dumps(line), flush=True)

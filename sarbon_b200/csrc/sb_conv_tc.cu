@@ -34,28 +34,40 @@ namespace sb {
 
 constexpr int kMaxSmem = 232448;  // 227 KB opt-in shared memory per CTA on sm_100
 
-template <int CIN, int NCTA, int T, int S>
+// WIN = 0: per-tap im2col boxes (or the first layer's gather); WIN = 1 / 2: shifted-window
+// mode for stride-1 layers, regions of WIN horizontally adjacent blocks (8 px wide, T rows).
+template <int CIN, int NCTA, int T, int S, int WIN>
 struct TcCfg {
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
   static constexpr int CH = MANUAL ? KPAD : (CIN % 64 == 0 ? 64 : 32);  // K elements per K-block
   static constexpr int NCH = MANUAL ? 1 : CIN / CH;
-  static constexpr int NKB = MANUAL ? 1 : 9 * NCH;    // K-blocks per M-tile
+  static constexpr int NKB = MANUAL ? 1 : (WIN ? 3 : 9) * NCH;  // K-blocks per M-tile
+  static constexpr int NWKB = MANUAL ? 1 : 9 * NCH;   // weight K-blocks (tap-major)
   static constexpr int ROWB = CH * 2;                 // bytes per operand row
   static constexpr int SWZ = ROWB == 128 ? 2 : 4;     // 128B / 64B swizzle
   static constexpr int SBO = 8 * ROWB;
   static constexpr int TT = T * T;
-  static constexpr int TPM = TT >= 128 ? 1 : 128 / TT;  // tiles per M-tile
-  static constexpr int MPT = TT >= 128 ? TT / 128 : 1;  // M-tiles per tile
-  static constexpr int BOX_ROWS = TT >= 128 ? 128 / T : T;
-  static constexpr int BOX_BYTES = T * BOX_ROWS * ROWB;
-  static constexpr int A_STAGE = 128 * ROWB;
+  // window mode: a region is 8 output px wide and T rows tall; its input window row is 10 px
+  static constexpr int RPX = 8 * T;                     // output pixels per region
+  static constexpr int TPM = WIN ? 128 / RPX : (TT >= 128 ? 1 : 128 / TT);  // tiles / regions per M-tile
+  static constexpr int MPT = WIN ? 1 : (TT >= 128 ? TT / 128 : 1);          // M-tiles per tile
+  static constexpr int BOX_ROWS = WIN ? T : (TT >= 128 ? 128 / T : T);
+  static constexpr int BOX_BYTES = WIN ? 10 * T * ROWB : T * BOX_ROWS * ROWB;
+  static constexpr int WSBO = 10 * ROWB;                // window mode: stride between output rows
+  static constexpr int A_STAGE = WIN ? TPM * BOX_BYTES : 128 * ROWB;
   static constexpr int B_KB = NCTA * ROWB;
-  static constexpr int W_BYTES = NKB * B_KB;
+  static constexpr int W_BYTES = NWKB * B_KB;
   static constexpr int TMEM_COLS = (2 * NCTA) <= 32 ? 32 : (2 * NCTA) <= 64 ? 64 : (2 * NCTA) <= 128 ? 128 : (2 * NCTA) <= 256 ? 256 : 512;
+  // roles: warps 0-7 epilogue (two per TMEM lane quadrant, half the columns each),
+  // warp 8 TMA producer, warp 9 MMA issuer + TMEM owner, warps 10-13 first-layer gather
+  static constexpr int EPI_THREADS = 256;
+  static constexpr int NCOL = NCTA / 2;               // accumulator columns per epilogue warp
+  static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 320;
+  static constexpr int THREADS = MANUAL ? 448 : 320;
   static constexpr int W_OFF = 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
-  static constexpr int BIAS_BYTES = NCTA * 4;
+  static constexpr int BIAS_BYTES = 256 * 4;          // every output channel (C_out <= 256)
   static constexpr int BAR_BYTES = 256;
   // first layer: staged input window of one M-tile (BOX_ROWS output rows of one tile)
   static constexpr int WIN_ROWS = (BOX_ROWS - 1) * S + 3;
@@ -65,12 +77,12 @@ struct TcCfg {
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM = FIXED + A_OFF + STAGES * A_STAGE;
-  static constexpr int THREADS = MANUAL ? 320 : 192;   // 4 epilogue + producer + MMA (+4 gather)
   static constexpr uint32_t IDESC = idesc_f16(128, NCTA);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
-  static_assert(NCTA % 16 == 0 && NCTA >= 16 && NCTA <= 256, "UMMA N");
+  static_assert(NCTA % 32 == 0 && NCTA >= 32 && NCTA <= 256, "UMMA N / epilogue split");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
+  static_assert(!WIN || (S == 1 && WIN * T == 8 && ROWB == 128 && !MANUAL), "window mode geometry");
 };
 
 struct TileXY {
@@ -79,43 +91,60 @@ struct TileXY {
 
 // Active-tile i of this layer: dense -> every block in flat order; sparse -> the
 // block list (entries past the listed count are block 0, as nonzero_static pads).
+// For WIN == 2 the entries are horizontal block pairs and `bx` is the pair column.
+template <int WIN>
 SB_DEV TileXY tile_at(const ConvArgs& a, int mode, int listed, int i) {
   TileXY r{0, 0, 0};
   if (mode == SB_MODE_DENSE) {
-    const int per = a.hb * a.wb;
+    const int wd = WIN == 2 ? (a.wb + 1) / 2 : a.wb;
+    const int per = a.hb * wd;
     r.cam = i / per;
     const int q = i - r.cam * per;
-    r.by = q / a.wb;
-    r.bx = q - r.by * a.wb;
+    r.by = q / wd;
+    r.bx = q - r.by * wd;
   } else if (i < listed) {
-    r.cam = __ldg(a.lcam + i);
-    r.by = __ldg(a.lby + i);
-    r.bx = __ldg(a.lbx + i);
+    const int32_t* lc = WIN == 2 ? a.pcam : a.lcam;
+    const int32_t* ly = WIN == 2 ? a.pby : a.lby;
+    const int32_t* lx = WIN == 2 ? a.ppx : a.lbx;
+    r.cam = __ldg(lc + i);
+    r.by = __ldg(ly + i);
+    r.bx = __ldg(lx + i);
   }
   return r;
 }
 
-template <int CIN, int NCTA, int T, int S>
-__global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
+// Work item -> (C_out slice, M-tile).  Items are ordered slice-major, so a persistent CTA
+// changes slice (and reloads its weights) at most nsplit-1 times.
+struct Item {
+  int split, m;
+};
+SB_DEV Item item_at(int it, int n_mtiles) {
+  const int item = (int)blockIdx.x + it * (int)gridDim.x;
+  return Item{item / n_mtiles, item % n_mtiles};
+}
+
+template <int CIN, int NCTA, int T, int S, int WIN>
+__global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
     conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmap) {
-  using C = TcCfg<CIN, NCTA, T, S>;
+  using C = TcCfg<CIN, NCTA, T, S, WIN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem + C::W_OFF;
   uint8_t* sA = smem + C::A_OFF;
   float* sBias = reinterpret_cast<float*>(sA + C::STAGES * C::A_STAGE);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sBias + NCTA);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sBias) + C::BIAS_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::STAGES;
   uint64_t* accf = bars + 2 * C::STAGES;
   uint64_t* acce = accf + 2;
-  uint64_t* wbar = acce + 2;
-  uint64_t* dbar = wbar + 1;
+  uint64_t* wfull = acce + 2;
+  uint64_t* wempty = wfull + 1;
+  uint64_t* dbar = wempty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(dbar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  __half* win = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
 
   const int warp = warp_id(), lane = lane_id();
-  const int n0 = blockIdx.y * NCTA;  // output-channel slice of this CTA
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
@@ -124,19 +153,20 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], 128);
+      mbar_init(&acce[i], C::EPI_THREADS);
     }
-    mbar_init(wbar, 1);
+    mbar_init(wfull, 1);
+    mbar_init(wempty, 1);
     mbar_init(dbar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == C::MMA_WARP) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
     tmem_relinquish();
   }
-  for (int i = threadIdx.x; i < NCTA; i += blockDim.x) sBias[i] = a.bias[n0 + i];
-  if (!C::MANUAL && warp == 4 && lane == 0) prefetch_tmap(&tmap);
+  for (int i = threadIdx.x; i < a.cout; i += blockDim.x) sBias[i] = a.bias[i];
+  if (!C::MANUAL && warp == C::PROD_WARP && lane == 0) prefetch_tmap(&tmap);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -144,87 +174,127 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
 
   // work of this launch, decided on the device (no host sync)
   const int mode = a.st->mode_cur;
-  const int listed = a.st->counts[a.d_idx];
+  const int listed = WIN == 2 ? a.st->pcounts[a.d_idx] : a.st->counts[a.d_idx];
+  const int n_units = WIN == 2 ? a.n_blocks / (a.hb * a.wb) * a.hb * ((a.wb + 1) / 2) : a.n_blocks;
   int n_tiles = 0;
-  if (mode == SB_MODE_DENSE) n_tiles = a.n_blocks;
+  if (mode == SB_MODE_DENSE) n_tiles = n_units;
   else if (mode == SB_MODE_SPARSE) n_tiles = a.st->force_tiles > 0 ? a.st->force_tiles : listed;
-  if (n_tiles > a.n_blocks && mode != SB_MODE_DENSE) n_tiles = a.n_blocks;
-  const int n_mtiles = C::TT >= 128 ? n_tiles * C::MPT : (n_tiles + C::TPM - 1) / C::TPM;
-  const int my_tiles = (int)blockIdx.x < n_mtiles ? (n_mtiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  if (n_tiles > n_units) n_tiles = n_units;
+  const int n_mtiles = (!WIN && C::TT >= 128) ? n_tiles * C::MPT : (n_tiles + C::TPM - 1) / C::TPM;
+  const int n_items = n_mtiles * (a.cout / NCTA);
+  const int my_items = (int)blockIdx.x < n_items ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
-  if (my_tiles > 0) {
-    if (warp == 4 && lane == 0) {
-      // ------------------------------------------------ producer: weights, then A stages
-      const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)blockIdx.y * C::W_BYTES;
-      mbar_arrive_expect_tx(wbar, C::W_BYTES);
-      for (int off = 0; off < C::W_BYTES; off += 32768) {
-        const int len = C::W_BYTES - off < 32768 ? C::W_BYTES - off : 32768;
-        bulk_load(sW + off, wsrc + off, len, wbar);
-      }
-      if (!C::MANUAL) {
-        uint32_t g = 0;
-        for (int it = 0; it < my_tiles && !*abort_flag; ++it) {
-          const int m = blockIdx.x + it * gridDim.x;
-          int cam[C::TPM], y0[C::TPM], x0[C::TPM];
+  if (my_items > 0) {
+    if (warp == C::PROD_WARP) {
+      // ------------------------------------------------ producer: weights per C_out slice, A stages
+      // The whole warp runs the loop (warp-uniform control flow); lane 0 issues the copies.
+      const bool leader = lane == 0;
+      uint32_t g = 0, nload = 0;
+      int cur = -1;
+      int ncam[C::TPM], ny0[C::TPM], nx0[C::TPM];
+      auto fetch = [&](const Item& w) {
 #pragma unroll
-          for (int j = 0; j < C::TPM; ++j) {
-            int ti, sub;
-            if (C::TT >= 128) { ti = m / C::MPT; sub = m % C::MPT; }
-            else { ti = m * C::TPM + j; sub = 0; }
-            const TileXY p = tile_at(a, mode, listed, ti < n_tiles ? ti : 0);
-            cam[j] = p.cam;
-            y0[j] = (p.by * T + sub * C::BOX_ROWS) * S - 1;
-            x0[j] = p.bx * T * S - 1;
+        for (int j = 0; j < C::TPM; ++j) {
+          int ti, sub;
+          if (!WIN && C::TT >= 128) { ti = w.m / C::MPT; sub = w.m % C::MPT; }
+          else { ti = w.m * C::TPM + j; sub = 0; }
+          const TileXY p = tile_at<WIN>(a, mode, listed, ti < n_tiles ? ti : 0);
+          ncam[j] = p.cam;
+          ny0[j] = (p.by * T + sub * C::BOX_ROWS) * S - 1;
+          nx0[j] = (WIN ? p.bx * 8 : p.bx * T * S) - 1;
+        }
+      };
+      if (!C::MANUAL) fetch(item_at(0, n_mtiles));
+      for (int it = 0; it < my_items && !*abort_flag; ++it) {
+        const Item w = item_at(it, n_mtiles);
+        if (w.split != cur) {
+          if (nload > 0 && !warp_wait(wempty, (nload - 1) & 1u, abort_flag)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
+            *abort_flag = 1;
+            break;
           }
-          for (int kb = 0; kb < C::NKB; ++kb, ++g) {
-            const int tap = kb / C::NCH, ch = kb % C::NCH;
-            const int ky = tap / 3, kx = tap % 3;
-            const int s = g % C::STAGES;
-            const uint32_t ph = (g / C::STAGES) & 1u;
-            if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
-              atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
-              *abort_flag = 1;
-              break;
+          const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)w.split * C::W_BYTES;
+          if (leader) {
+            mbar_arrive_expect_tx(wfull, C::W_BYTES);
+            for (int off = 0; off < C::W_BYTES; off += 32768) {
+              const int len = C::W_BYTES - off < 32768 ? C::W_BYTES - off : 32768;
+              bulk_load(sW + off, wsrc + off, len, wfull);
             }
+          }
+          __syncwarp();
+          ++nload;
+          cur = w.split;
+        }
+        if (C::MANUAL) continue;
+        // coordinates of this item were fetched one item ahead; fetch the next item's now so
+        // the list lookups overlap this item's K-blocks instead of stalling the pipeline
+        int cam[C::TPM], y0[C::TPM], x0[C::TPM];
+#pragma unroll
+        for (int j = 0; j < C::TPM; ++j) {
+          cam[j] = ncam[j];
+          y0[j] = ny0[j];
+          x0[j] = nx0[j];
+        }
+        if (it + 1 < my_items) fetch(item_at(it + 1, n_mtiles));
+        for (int kb = 0; kb < C::NKB; ++kb, ++g) {
+          // im2col: K-block = (tap, chunk); window: K-block = (ky, chunk), the 3 kx taps read
+          // the same window rows at offsets of kx pixels
+          const int tap = WIN ? (kb / C::NCH) * 3 : kb / C::NCH, ch = kb % C::NCH;
+          const int ky = tap / 3, kx = WIN ? 0 : tap % 3;
+          const int s = g % C::STAGES;
+          const uint32_t ph = (g / C::STAGES) & 1u;
+          if (!warp_wait(&empty[s], ph ^ 1u, abort_flag)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+            break;
+          }
+          if (leader) {
             mbar_arrive_expect_tx(&full[s], C::A_STAGE);
             uint8_t* dst = sA + s * C::A_STAGE;
 #pragma unroll
             for (int j = 0; j < C::TPM; ++j)
               tma_load_4d(dst + j * C::BOX_BYTES, &tmap, &full[s], ch * C::CH, x0[j] + kx, y0[j] + ky, cam[j]);
           }
-        }
-        // drain: every issued A load has landed before the CTA may exit
-        const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0u;
-        for (uint32_t q = first; q < g; ++q) {
-          volatile int never = 0;
-          mbar_wait(&full[q % C::STAGES], (q / C::STAGES) & 1u, &never);
+          __syncwarp();
         }
       }
-    } else if (C::MANUAL && warp >= 6) {
+      // drain: every issued copy has landed before the CTA may exit
+      volatile int never = 0;
+      const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0u;
+      for (uint32_t q = first; q < g; ++q) warp_wait(&full[q % C::STAGES], (q / C::STAGES) & 1u, &never);
+      if (nload > 0) warp_wait(wfull, (nload - 1) & 1u, &never);
+    } else if (C::MANUAL && (int)threadIdx.x >= C::GATHER0) {
       // ------------------------------------------------ gather producers (first layer)
       // Per M-tile: stage the input window (with the image-border zero padding) in shared
       // memory with coalesced loads, then build each A row (one output pixel: 3x3 taps x
       // channels, zero-padded to KPAD) from it.
-      const int r = threadIdx.x - 192;  // A row = output pixel slot, 0..127
+      const int r = threadIdx.x - C::GATHER0;  // A row = output pixel slot, 0..127
       const __half* x = static_cast<const __half*>(a.x);
-      __half* win = reinterpret_cast<__half*>(sA + C::STAGES * C::A_STAGE + C::BIAS_BYTES + C::BAR_BYTES);
       constexpr int RW = C::WIN_ROWS, WW = C::WIN_COLS, ROWE = WW * CIN;
       uint32_t g = 0;
-      for (int it = 0; it < my_tiles && !*abort_flag; ++it, ++g) {
-        const int m = blockIdx.x + it * gridDim.x;
-        const int ti = m / C::MPT, sub = m % C::MPT;
-        const TileXY tc = tile_at(a, mode, listed, ti < n_tiles ? ti : 0);
+      for (int it = 0; it < my_items && !*abort_flag; ++it, ++g) {
+        const Item w = item_at(it, n_mtiles);
+        const int ti = w.m / C::MPT, sub = w.m % C::MPT;
+        const TileXY tc = tile_at<WIN>(a, mode, listed, ti < n_tiles ? ti : 0);
         const int iy0 = (tc.by * T + sub * C::BOX_ROWS) * S - 1, ix0 = tc.bx * T * S - 1;
         const __half* xc = x + (size_t)tc.cam * a.hx * a.wx * CIN;
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // previous window fully consumed
-        for (int idx = r; idx < RW * ROWE; idx += 128) {
+        // all loads of this thread's window share first (independent, in flight together),
+        // then the shared-memory stores
+        constexpr int NLD = (RW * ROWE + 127) / 128;
+        uint16_t wv[NLD];
+#pragma unroll
+        for (int k = 0; k < NLD; ++k) {
+          const int idx = r + 128 * k;
           const int wy = idx / ROWE, e = idx - wy * ROWE;
           const int iy = iy0 + wy, ix = ix0 + e / CIN;
-          __half v = __ushort_as_half(0);
-          if (iy >= 0 && iy < a.hx && ix >= 0 && ix < a.wx)
-            v = __ldg(xc + ((size_t)iy * a.wx + ix) * CIN + (e % CIN));
-          win[idx] = v;
+          wv[k] = 0;
+          if (idx < RW * ROWE && iy >= 0 && iy < a.hx && ix >= 0 && ix < a.wx)
+            wv[k] = __half_as_ushort(__ldg(xc + ((size_t)iy * a.wx + ix) * CIN + (e % CIN)));
         }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // previous window fully consumed
+#pragma unroll
+        for (int k = 0; k < NLD; ++k)
+          if (r + 128 * k < RW * ROWE) reinterpret_cast<uint16_t*>(win)[r + 128 * k] = wv[k];
         asm volatile("bar.sync 1, 128;" ::: "memory");  // window complete
         const int s = g % C::STAGES;
         const uint32_t ph = (g / C::STAGES) & 1u;
@@ -259,17 +329,27 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
         fence_proxy_async_smem();
         mbar_arrive(&full[s]);
       }
-    } else if (warp == 5 && lane == 0) {
+    } else if (warp == C::MMA_WARP) {
       // ------------------------------------------------ MMA issuer
-      bool ok = mbar_wait(wbar, 0, abort_flag);
-      if (!ok) {
-        atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
-        *abort_flag = 1;
-      }
-      uint32_t g = 0;
-      for (int it = 0; ok && it < my_tiles; ++it) {
+      // The whole warp runs the loop; lane 0 issues tcgen05.mma / tcgen05.commit.
+      const bool leader = lane == 0;
+      uint32_t g = 0, nload = 0;
+      int cur = -1;
+      bool ok = true;
+      for (int it = 0; ok && it < my_items; ++it) {
+        const Item w = item_at(it, n_mtiles);
+        if (w.split != cur) {
+          if (nload > 0 && leader) mma_commit(wempty);  // old weights free once the issued MMAs are done
+          if (!warp_wait(wfull, nload & 1u, abort_flag)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
+            *abort_flag = 1;
+            break;
+          }
+          ++nload;
+          cur = w.split;
+        }
         const int ab = it & 1;
-        if (!mbar_wait(&acce[ab], ((it >> 1) & 1) ^ 1, abort_flag)) {
+        if (!warp_wait(&acce[ab], ((it >> 1) & 1) ^ 1, abort_flag)) {
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
           *abort_flag = 1;
           break;
@@ -278,37 +358,90 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
         const uint32_t d_tmem = tmem_base + ab * NCTA;
         for (int kb = 0; kb < C::NKB; ++kb, ++g) {
           const int s = g % C::STAGES;
-          if (!mbar_wait(&full[s], (g / C::STAGES) & 1u, abort_flag)) {
+          if (!warp_wait(&full[s], (g / C::STAGES) & 1u, abort_flag)) {
             atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
             *abort_flag = 1;
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + s * C::A_STAGE);
-          const uint32_t b_addr = smem_u32(sW + kb * C::B_KB);
+          if (leader) {
+            const uint32_t a_addr = smem_u32(sA + s * C::A_STAGE);
+            if (WIN) {
+              // the three kx taps: A = window rows shifted by kx pixels (128 B rows, the
+              // hardware swizzle follows absolute smem addresses), B = that tap's weights
+              const int ky = kb / C::NCH, ch = kb % C::NCH;
 #pragma unroll
-          for (int kk = 0; kk < C::CH / 16; ++kk) {
-            const uint64_t ad = smem_desc(a_addr + kk * 32, C::SBO, C::SWZ);
-            const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
-            mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+              for (int kx = 0; kx < 3; ++kx) {
+                const uint32_t b_addr = smem_u32(sW + ((ky * 3 + kx) * C::NCH + ch) * C::B_KB);
+#pragma unroll
+                for (int kk = 0; kk < C::CH / 16; ++kk) {
+                  const uint64_t ad = smem_desc(a_addr + kx * C::ROWB + kk * 32, C::WSBO, C::SWZ);
+                  const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
+                  mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | kx | kk) != 0 ? 1u : 0u);
+                }
+              }
+            } else {
+              const uint32_t b_addr = smem_u32(sW + kb * C::B_KB);
+#pragma unroll
+              for (int kk = 0; kk < C::CH / 16; ++kk) {
+                const uint64_t ad = smem_desc(a_addr + kk * 32, C::SBO, C::SWZ);
+                const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
+                mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+              }
+            }
+            mma_commit(&empty[s]);  // stage free once these MMAs have read it
           }
-          mma_commit(&empty[s]);  // stage free once these MMAs have read it
+          __syncwarp();
         }
         if (!ok) break;
-        mma_commit(&accf[ab]);    // accumulator ready for the epilogue
+        if (leader) mma_commit(&accf[ab]);  // accumulator ready for the epilogue
+        __syncwarp();
       }
       // drain: all issued MMAs complete before TMEM is released
-      mma_commit(dbar);
+      if (leader) mma_commit(dbar);
+      __syncwarp();
       volatile int never = 0;
-      mbar_wait(dbar, 0, &never);
-    } else if (warp < 4) {
+      warp_wait(dbar, 0, &never);
+    } else if (warp < 8) {
       // ------------------------------------------------ epilogue: TMEM -> bias/res/ReLU -> cache
-      const int r = warp * 32 + lane;  // accumulator row = TMEM lane
+      // Warp w reads TMEM lanes 32*(w%4).. (its accumulator rows) and columns
+      // (w/4)*NCOL.. of them.  The residual is fetched before the accumulator wait and the
+      // TMEM buffer is released as soon as it sits in registers.
+      const int q = warp & 3, col0 = (warp >> 2) * C::NCOL;
+      const int r = q * 32 + lane;  // accumulator row = TMEM lane
       __half* y = static_cast<__half*>(a.y);
       const __half* res = static_cast<const __half*>(a.res);
-      for (int it = 0; it < my_tiles; ++it) {
-        const int m = blockIdx.x + it * gridDim.x;
+      // per-row destination and residual of one item, fetched one item ahead
+      struct Row {
+        size_t pix;
+        int n0;
+        bool st;
+        uint4 rr[C::NCOL / 8];
+      };
+      auto fetch = [&](int it, Row& o) {
+        const Item w = item_at(it, n_mtiles);
+        o.n0 = w.split * NCTA + col0;
+        int ti, p;
+        if (WIN) { ti = w.m * C::TPM + r / C::RPX; p = r % C::RPX; }
+        else if (C::TT >= 128) { ti = w.m / C::MPT; p = (w.m % C::MPT) * 128 + r; }
+        else { ti = w.m * C::TPM + r / C::TT; p = r % C::TT; }
+        const bool valid = ti < n_tiles;
+        const TileXY tc = tile_at<WIN>(a, mode, listed, valid ? ti : 0);
+        const int gy = WIN ? tc.by * T + p / 8 : tc.by * T + p / T;
+        const int gx = WIN ? tc.bx * 8 + p % 8 : tc.bx * T + p % T;
+        const bool inb = tc.cam < a.n && gy < a.ho && gx < a.wo;
+        if (valid && !inb) atomicOr(&a.st->error, SB_ERR_BAD_TILE);
+        o.st = valid && inb;
+        o.pix = (((size_t)tc.cam * a.ho + gy) * a.wo + gx) * a.cout + o.n0;
+        if (res != nullptr && o.st) {
+#pragma unroll
+          for (int j = 0; j < C::NCOL / 8; ++j) o.rr[j] = __ldg(reinterpret_cast<const uint4*>(res + o.pix) + j);
+        }
+      };
+      Row cur, nxt;
+      fetch(0, cur);
+      for (int it = 0; it < my_items; ++it) {
         const int ab = it & 1;
         const bool got = mbar_wait(&accf[ab], (it >> 1) & 1, abort_flag);
         if (!got) {
@@ -318,64 +451,48 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
         // warp-uniform exit: tcgen05.ld below is .sync.aligned
         if (__any_sync(0xFFFFFFFFu, !got || *abort_flag != 0)) break;
         tc_fence_after();
-        int ti, p;
-        if (C::TT >= 128) { ti = m / C::MPT; p = (m % C::MPT) * 128 + r; }
-        else { ti = m * C::TPM + r / C::TT; p = r % C::TT; }
-        const bool valid = ti < n_tiles;
-        const TileXY tc = tile_at(a, mode, listed, valid ? ti : 0);
-        const int gy = tc.by * T + p / T, gx = tc.bx * T + p % T;
-        const bool inb = tc.cam < a.n && gy < a.ho && gx < a.wo;
-        if (valid && !inb) atomicOr(&a.st->error, SB_ERR_BAD_TILE);
-        const size_t pix = (((size_t)tc.cam * a.ho + gy) * a.wo + gx) * a.cout + n0;
-        const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16) + ab * NCTA;
-#pragma unroll 1
-        for (int c0 = 0; c0 < NCTA; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(taddr + c0, v);
-          tmem_ld_wait();
-          float f[16];
+        uint32_t v[C::NCOL];
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + ab * NCTA + col0;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]) + sBias[c0 + j];
-          if (valid && inb) {
+        for (int j = 0; j < C::NCOL / 16; ++j)
+          tmem_ld16(taddr + j * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[j * 16]));
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&acce[ab]);  // the MMA may overwrite this buffer now
+        if (it + 1 < my_items) fetch(it + 1, nxt);
+        if (cur.st) {
+#pragma unroll
+          for (int j = 0; j < C::NCOL / 8; ++j) {
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + sBias[cur.n0 + j * 8 + e];
             if (res != nullptr) {
-              const uint4* rp = reinterpret_cast<const uint4*>(res + pix + c0);
-              const uint4 r0 = __ldg(rp), r1 = __ldg(rp + 1);
-              const __half2* h0 = reinterpret_cast<const __half2*>(&r0);
-              const __half2* h1 = reinterpret_cast<const __half2*>(&r1);
+              const __half2* h = reinterpret_cast<const __half2*>(&cur.rr[j]);
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float2 q0 = __half22float2(h0[j]), q1 = __half22float2(h1[j]);
-                f[2 * j] += q0.x;
-                f[2 * j + 1] += q0.y;
-                f[8 + 2 * j] += q1.x;
-                f[8 + 2 * j + 1] += q1.y;
+              for (int e = 0; e < 4; ++e) {
+                const float2 t2 = __half22float2(h[e]);
+                f[2 * e] += t2.x;
+                f[2 * e + 1] += t2.y;
               }
             }
             if (a.act) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) f[j] = fmaxf(f[j], 0.0f);
+              for (int e = 0; e < 8; ++e) f[e] = fmaxf(f[e], 0.0f);
             }
-            uint4 o0, o1;
-            __half2* p0 = reinterpret_cast<__half2*>(&o0);
-            __half2* p1 = reinterpret_cast<__half2*>(&o1);
+            uint4 o;
+            __half2* ph = reinterpret_cast<__half2*>(&o);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              p0[j] = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
-              p1[j] = __floats2half2_rn(f[8 + 2 * j], f[8 + 2 * j + 1]);
-            }
-            uint4* op = reinterpret_cast<uint4*>(y + pix + c0);
-            op[0] = o0;
-            op[1] = o1;
+            for (int e = 0; e < 4; ++e) ph[e] = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+            reinterpret_cast<uint4*>(y + cur.pix)[j] = o;
           }
         }
-        tc_fence_before();
-        mbar_arrive(&acce[ab]);
+        cur = nxt;
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == C::MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
@@ -385,15 +502,15 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S>::THREADS, 1)
 namespace {
 
 struct Variant {
-  int cin, cout, t, s, ncta;
+  int cin, cout, t, s, win, ncta;
   void (*fn)(const ConvArgs, const CUtensorMap);
   int smem, threads, w_bytes, ch, box_rows;
 };
 
-template <int CIN, int NCTA, int T, int S>
+template <int CIN, int NCTA, int T, int S, int WIN = 0>
 Variant make_variant(int cout) {
-  using C = TcCfg<CIN, NCTA, T, S>;
-  return Variant{CIN, cout, T, S, NCTA, conv_tc_kernel<CIN, NCTA, T, S>, C::SMEM, C::THREADS, C::W_BYTES,
+  using C = TcCfg<CIN, NCTA, T, S, WIN>;
+  return Variant{CIN, cout, T, S, WIN, NCTA, conv_tc_kernel<CIN, NCTA, T, S, WIN>, C::SMEM, C::THREADS, C::W_BYTES,
                  C::CH, C::BOX_ROWS};
 }
 
@@ -403,15 +520,15 @@ const std::vector<Variant>& variants() {
       // block 32
       make_variant<3, 32, 16, 2>(32),
       make_variant<32, 64, 8, 2>(64),
-      make_variant<64, 64, 8, 1>(64),
+      make_variant<64, 64, 8, 1, 1>(64),    // shifted window, 8x8 blocks
       make_variant<64, 128, 4, 2>(128),
-      make_variant<128, 64, 4, 1>(128),  // two C_out slices of 64 (weights fit smem)
+      make_variant<128, 64, 4, 1, 2>(128),  // shifted window over block pairs; two C_out slices
       // block 64
       make_variant<3, 32, 32, 2>(32),
       make_variant<32, 64, 16, 2>(64),
       make_variant<64, 64, 16, 1>(64),
       make_variant<64, 128, 8, 2>(128),
-      make_variant<128, 64, 8, 1>(128),
+      make_variant<128, 64, 8, 1, 1>(128),  // shifted window, 8x8 blocks
   };
   return v;
 }
@@ -421,6 +538,15 @@ const Variant* find_variant(int cin, int cout, int t, int s) {
     if (v.cin == cin && v.cout == cout && v.t == t && v.s == s) return &v;
   return nullptr;
 }
+
+}  // namespace
+
+int conv_tc_region(int cin, int cout, int t, int s) {
+  const Variant* v = find_variant(cin, cout, t, s);
+  return v ? v->win : -1;
+}
+
+namespace {
 
 }  // namespace
 
@@ -504,11 +630,13 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
   for (const auto& c : variants())
     if (c.cin == cin && c.t == t && c.s == s) { v = &c; break; }
   if (!v || cin < 16) return cudaErrorInvalidValue;
+  const bool win = v->win != 0;
   PFN_encodeTiled enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[4] = {(cuuint64_t)cin, (cuuint64_t)wx, (cuuint64_t)hx, (cuuint64_t)n};
   cuuint64_t strides[3] = {(cuuint64_t)cin * 2, (cuuint64_t)wx * cin * 2, (cuuint64_t)hx * wx * cin * 2};
-  cuuint32_t box[4] = {(cuuint32_t)v->ch, (cuuint32_t)(t * s), (cuuint32_t)(v->box_rows * s), 1};
+  // window mode: 10 input px (8 output px + halo) x T rows; im2col: the strided tile itself
+  cuuint32_t box[4] = {(cuuint32_t)v->ch, win ? 10u : (cuuint32_t)(t * s), (cuuint32_t)(v->box_rows * s), 1};
   cuuint32_t estr[4] = {1, (cuuint32_t)s, (cuuint32_t)s, 1};
   const CUtensorMapSwizzle swz = v->ch * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(src), dims, strides, box, estr,
@@ -533,7 +661,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, const CUtensorMap* map, int grid_x
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, v->fn, v->threads, v->smem) != cudaSuccess || o < 1) o = 1;
     occ[idx] = o;
   }
-  dim3 grid(grid_x * occ[idx], a.cout / v->ncta);
+  dim3 grid(grid_x * occ[idx], 1);  // C_out slices are work items of the persistent loop
   CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));
   v->fn<<<grid, v->threads, v->smem, st>>>(a, map ? *map : dummy);

@@ -73,6 +73,8 @@ struct sb_engine {
   uint8_t* extra = nullptr;
   uint8_t* masks = nullptr;
   int32_t* lists = nullptr;
+  int32_t* plists = nullptr;   // horizontal block-pair lists (window-mode 4x4-tile layers)
+  int n_pairs = 0;
   unsigned long long* status = nullptr;
   int n_chunks = 0;
   State* st = nullptr;
@@ -142,6 +144,10 @@ int launch_convs(sb_engine* e, cudaStream_t s) {
     a.t = e->layer_t[i];
     a.s = L.stride;
     a.act = L.act;
+    a.region = e->dtype == SB_F16 ? conv_tc_region(L.cin, L.cout, a.t, a.s) : 0;
+    a.pcam = e->plists + (size_t)di * 3 * e->n_pairs;
+    a.pby = a.pcam + e->n_pairs;
+    a.ppx = a.pby + e->n_pairs;
     cudaError_t err;
     if (e->dtype == SB_F16) {
       err = launch_conv_tc(a, e->has_tmap[i] ? &e->tmap[i] : nullptr, e->n_sms, s);
@@ -199,6 +205,7 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
   l.changed = e->changed;
   l.masks = e->masks;
   l.lists = e->lists;
+  l.plists = e->plists;
   l.status = e->status;
   l.st = e->st;
   l.n_blocks = e->n_blocks;
@@ -383,7 +390,9 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
   if ((rc = alloc_dev(e, (void**)&e->extra, e->n_blocks))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->masks, (size_t)e->nd * e->n_blocks))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->lists, (size_t)e->nd * 3 * e->n_blocks * 4))) return bail(rc);
-  if ((rc = alloc_dev(e, (void**)&e->status, (size_t)e->nd * e->n_chunks * 8))) return bail(rc);
+  e->n_pairs = n_streams * e->hb * ((e->wb + 1) / 2);
+  if ((rc = alloc_dev(e, (void**)&e->plists, (size_t)e->nd * 3 * e->n_pairs * 4))) return bail(rc);
+  if ((rc = alloc_dev(e, (void**)&e->status, (size_t)2 * e->nd * e->n_chunks * 8))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->st, sizeof(State)))) return bail(rc);
   State init{};
   init.epoch = 1;

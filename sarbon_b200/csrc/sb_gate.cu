@@ -314,59 +314,73 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
     }
     return;
   }
+  // compaction lanes: kind 0 = blocks, kind 1 = horizontal block pairs; one per dilation
+  constexpr int ML = 2 * SB_MAX_DILATIONS;
   __shared__ uint32_t s_chunk;
-  __shared__ uint32_t s_warp[SB_MAX_DILATIONS][32];
-  __shared__ uint32_t s_excl[SB_MAX_DILATIONS];
+  __shared__ uint32_t s_warp[ML][32];
+  __shared__ uint32_t s_excl[ML];
   const uint32_t epoch = st->epoch;
   if (threadIdx.x == 0) s_chunk = atomicAdd(&st->ticket, 1u);
   __syncthreads();
   const uint32_t chunk = s_chunk;
   const int nchunks = gridDim.x;
   const int f = (int)chunk * LIST_THREADS + threadIdx.x;
-  const int per = a.hb * a.wb;
-  const bool valid = f < a.n_blocks;
-  int cam = 0, by = 0, bx = 0;
-  if (valid) {
-    cam = f / per;
-    const int r = f - cam * per;
-    by = r / a.wb;
-    bx = r - by * a.wb;
-  }
-  const uint8_t* cm = a.changed + (size_t)cam * per;
+  const int per = a.hb * a.wb, wp = (a.wb + 1) / 2, perp = a.hb * wp;
+  const int n_pairs = a.n_blocks / per * perp;
+  const int nl = 2 * a.n_dil;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t rank[SB_MAX_DILATIONS];
-  bool act[SB_MAX_DILATIONS];
-  for (int di = 0; di < a.n_dil; ++di) {
-    const int d = a.ds[di];
-    bool on = false;
+  uint32_t rank[ML];
+  bool act[ML];
+  int coord[2][3];
+#pragma unroll
+  for (int kind = 0; kind < 2; ++kind) {
+    const bool valid = kind == 0 ? f < a.n_blocks : f < n_pairs;
+    int cam = 0, by = 0, bx = 0;
     if (valid) {
-      const int y0 = max(0, by - d), y1 = min(a.hb - 1, by + d);
-      const int x0 = max(0, bx - d), x1 = min(a.wb - 1, bx + d);
-      for (int y = y0; y <= y1 && !on; ++y)
-        for (int x = x0; x <= x1; ++x)
-          if (__ldg(cm + y * a.wb + x)) { on = true; break; }
-      a.masks[(size_t)di * a.n_blocks + f] = on ? 1 : 0;
+      const int pr = kind == 0 ? per : perp, wd = kind == 0 ? a.wb : wp;
+      cam = f / pr;
+      const int r = f - cam * pr;
+      by = r / wd;
+      bx = r - by * wd;
     }
-    act[di] = on;
-    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, on);
-    rank[di] = __popc(bal & ((1u << lane) - 1u));
-    if (lane == 0) s_warp[di][warp] = __popc(bal);
+    coord[kind][0] = cam;
+    coord[kind][1] = by;
+    coord[kind][2] = bx;
+    const uint8_t* cm = a.changed + (size_t)cam * per;
+    const int xlo = kind == 0 ? bx : 2 * bx, xhi = kind == 0 ? bx : 2 * bx + 1;
+    for (int di = 0; di < a.n_dil; ++di) {
+      const int d = a.ds[di], L = kind * a.n_dil + di;
+      bool on = false;
+      if (valid) {
+        // block: max_pool(2d+1) of `changed` (fused_engine.py:151); pair: either block of the pair
+        const int y0 = max(0, by - d), y1 = min(a.hb - 1, by + d);
+        const int x0 = max(0, xlo - d), x1 = min(a.wb - 1, xhi + d);
+        for (int y = y0; y <= y1 && !on; ++y)
+          for (int x = x0; x <= x1; ++x)
+            if (__ldg(cm + y * a.wb + x)) { on = true; break; }
+        if (kind == 0) a.masks[(size_t)di * a.n_blocks + f] = on ? 1 : 0;
+      }
+      act[L] = on;
+      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, on);
+      rank[L] = __popc(bal & ((1u << lane) - 1u));
+      if (lane == 0) s_warp[L][warp] = __popc(bal);
+    }
   }
   __syncthreads();
   if (warp == 0) {
-    for (int di = 0; di < a.n_dil; ++di) {
-      const uint32_t v = s_warp[di][lane];
+    for (int L = 0; L < nl; ++L) {
+      const uint32_t v = s_warp[L][lane];
       uint32_t inc = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
         if (lane >= (uint32_t)o) inc += t;
       }
-      s_warp[di][lane] = inc - v;  // exclusive warp offsets
+      s_warp[L][lane] = inc - v;  // exclusive warp offsets
       const uint32_t agg = __shfl_sync(0xFFFFFFFFu, inc, 31);
       // decoupled look-back: lane 0 publishes and walks predecessors
       if (lane == 0) {
-        unsigned long long* stat = a.status + (size_t)di * nchunks;
+        unsigned long long* stat = a.status + (size_t)L * nchunks;
         uint32_t excl = 0;
         if (chunk == 0) {
           lb_store(stat, lb_pack(epoch, LB_FLAG_INC, agg));
@@ -392,22 +406,25 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
           }
           lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_INC, excl + agg));
         }
-        s_excl[di] = excl;
+        s_excl[L] = excl;
         if ((int)chunk == nchunks - 1) {
-          st->counts[di] = (int32_t)(excl + agg);
+          if (L < a.n_dil) st->counts[L] = (int32_t)(excl + agg);
+          else st->pcounts[L - a.n_dil] = (int32_t)(excl + agg);
         }
       }
     }
   }
   __syncthreads();
-  for (int di = 0; di < a.n_dil; ++di) {
-    if (!act[di]) continue;
-    const uint32_t pos = s_excl[di] + s_warp[di][warp] + rank[di];
-    if (pos < (uint32_t)a.n_blocks) {
-      int32_t* L = a.lists + (size_t)di * 3 * a.n_blocks;
-      L[pos] = cam;
-      L[a.n_blocks + pos] = by;
-      L[2 * (size_t)a.n_blocks + pos] = bx;
+  for (int L = 0; L < nl; ++L) {
+    if (!act[L]) continue;
+    const int kind = L >= a.n_dil, di = L - kind * a.n_dil;
+    const uint32_t pos = s_excl[L] + s_warp[L][warp] + rank[L];
+    const int cap = kind ? n_pairs : a.n_blocks;
+    if (pos < (uint32_t)cap) {
+      int32_t* Lp = (kind ? a.plists : a.lists) + (size_t)di * 3 * cap;
+      Lp[pos] = coord[kind][0];
+      Lp[cap + pos] = coord[kind][1];
+      Lp[2 * (size_t)cap + pos] = coord[kind][2];
     }
   }
   if ((int)chunk == nchunks - 1 && threadIdx.x == 0) {

@@ -30,6 +30,7 @@ struct State {
   int32_t last_mode;
   int32_t pad_;
   int64_t result[2];    // {mode, count} of the last finished step
+  int32_t pcounts[SB_MAX_DILATIONS];  // active horizontal block pairs per dilation this step
 };
 
 struct GateArgs {
@@ -50,7 +51,8 @@ struct ListArgs {
   const uint8_t* changed;  // [n_blocks]
   uint8_t* masks;          // [n_dil][n_blocks]
   int32_t* lists;          // [n_dil][3][n_blocks] (cam, by, bx)
-  unsigned long long* status;  // [n_dil][n_chunks] look-back words
+  int32_t* plists;         // [n_dil][3][n_pairs] (cam, by, bx/2): horizontal block pairs
+  unsigned long long* status;  // [2*n_dil][n_chunks] look-back words
   State* st;
   int n_blocks, hb, wb, n_dil;
   int ds[SB_MAX_DILATIONS];
@@ -81,6 +83,10 @@ struct ConvArgs {
   int ho, wo, cout;
   int hb, wb, n_blocks;
   int t, s, act;
+  int region;              // 0: tiles = blocks; 1: windowed blocks; 2: windowed horizontal block pairs
+  const int32_t* pcam;     // pair lists (region 2)
+  const int32_t* pby;
+  const int32_t* ppx;
 };
 
 // ---------------------------------------------------------------- launchers
@@ -92,6 +98,7 @@ cudaError_t launch_set_mode(State* st, int mode, int reset_hyst, int64_t force_t
 
 // fp16 tcgen05 path.  Returns cudaErrorInvalidValue for shapes without an instantiation.
 bool conv_tc_supported(int cin, int cout, int t, int s);
+int conv_tc_region(int cin, int cout, int t, int s);  // ConvArgs::region the kernel expects
 int conv_tc_nsplit(int cin, int cout, int t, int s);   // CTA splits of cout
 size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s);  // all splits
 void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w /*[3][3][cin][cout]*/,

@@ -15,8 +15,10 @@
 #define SB_ERR_TIMEOUT_WGT    0x10
 #define SB_ERR_BAD_TILE       0x20
 
-// Poll limit for every spin-wait: ~2^24 polls with a 64 ns back-off is >1 s,
-// orders of magnitude above any legitimate wait inside one kernel.
+// Limits of every spin-wait: 2 s of waiting on an mbarrier (SB_WAIT_NS), 2^24 polls with
+// a short back-off on a global flag (SB_SPIN_LIMIT); both are orders of magnitude above
+// any legitimate wait inside one kernel.
+#define SB_WAIT_NS 2000000000ull
 #define SB_SPIN_LIMIT (1u << 24)
 
 namespace sb {
@@ -56,15 +58,32 @@ SB_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity.  Returns false after
-// SB_SPIN_LIMIT polls or as soon as *abort is set by another thread of the CTA.
+SB_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity.  mbarrier.try_wait suspends the
+// thread in hardware until the phase completes or a short system time limit passes, so
+// the loop needs no extra back-off.  Returns false after SB_WAIT_NS of waiting (far above
+// any legitimate wait inside one kernel) or as soon as *abort is set by another thread.
 SB_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  for (uint32_t i = 0; i < SB_SPIN_LIMIT; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort) return false;
-    if (i > 64) __nanosleep(64);
+    if ((i & 15u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > SB_WAIT_NS) return false;
+    }
   }
-  return false;
+}
+
+// mbar_wait executed by a full warp with a warp-uniform result.
+SB_DEV bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xFFFFFFFFu, ok);
 }
 
 // ---------------------------------------------------------------- proxies / fences
