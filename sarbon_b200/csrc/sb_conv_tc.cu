@@ -24,6 +24,7 @@
 //     (27 taps x channels, zero-padded to K=32) are gathered by four producer warps.
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -34,28 +35,34 @@ namespace sb {
 
 constexpr int kMaxSmem = 232448;  // 227 KB opt-in shared memory per CTA on sm_100
 
-// WIN = 0: per-tap im2col boxes (or the first layer's gather); WIN = 1 / 2: shifted-window
-// mode for stride-1 layers, regions of WIN horizontally adjacent blocks (8 px wide, T rows).
+// WIN = 0: per-tap im2col boxes over blocks (or the first layer's gather);
+// WIN = 1: row windows -- regions of 8/T x 1 blocks (8 px x T rows), one box per (ky, chunk)
+//          feeds the three kx taps;
+// WIN = 3: full windows -- regions of 8/T x 16/T blocks (8 px x 16 rows), one 10 x 18 px box
+//          per chunk feeds all nine taps.  Both window modes are for stride-1 layers.
 template <int CIN, int NCTA, int T, int S, int WIN>
 struct TcCfg {
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
   static constexpr int CH = MANUAL ? KPAD : (CIN % 64 == 0 ? 64 : 32);  // K elements per K-block
   static constexpr int NCH = MANUAL ? 1 : CIN / CH;
-  static constexpr int NKB = MANUAL ? 1 : (WIN ? 3 : 9) * NCH;  // K-blocks per M-tile
+  static constexpr int NKB = MANUAL ? 1 : (WIN == 3 ? 1 : WIN == 1 ? 3 : 9) * NCH;  // K-blocks per M-tile
   static constexpr int NWKB = MANUAL ? 1 : 9 * NCH;   // weight K-blocks (tap-major)
   static constexpr int ROWB = CH * 2;                 // bytes per operand row
   static constexpr int SWZ = ROWB == 128 ? 2 : 4;     // 128B / 64B swizzle
   static constexpr int SBO = 8 * ROWB;
   static constexpr int TT = T * T;
-  // window mode: a region is 8 output px wide and T rows tall; its input window row is 10 px
-  static constexpr int RPX = 8 * T;                     // output pixels per region
+  // window modes: a region is 8 output px wide and RROWS tall; its input window row is 10 px
+  static constexpr int RROWS = WIN == 3 ? 16 : T;
+  static constexpr int RW = WIN ? 8 / T : 1, RH = WIN == 3 ? 16 / T : 1;  // region in blocks
+  static constexpr int RPX = 8 * RROWS;                 // output pixels per region
   static constexpr int TPM = WIN ? 128 / RPX : (TT >= 128 ? 1 : 128 / TT);  // tiles / regions per M-tile
   static constexpr int MPT = WIN ? 1 : (TT >= 128 ? TT / 128 : 1);          // M-tiles per tile
-  static constexpr int BOX_ROWS = WIN ? T : (TT >= 128 ? 128 / T : T);
-  static constexpr int BOX_BYTES = WIN ? 10 * T * ROWB : T * BOX_ROWS * ROWB;
-  static constexpr int WSBO = 10 * ROWB;                // window mode: stride between output rows
-  static constexpr int A_STAGE = WIN ? TPM * BOX_BYTES : 128 * ROWB;
+  static constexpr int BOX_ROWS = WIN == 3 ? 18 : WIN ? T : (TT >= 128 ? 128 / T : T);
+  static constexpr int BOX_BYTES = WIN ? 10 * BOX_ROWS * ROWB : T * BOX_ROWS * ROWB;
+  static constexpr int WSBO = 10 * ROWB;                // window modes: stride between output rows
+  static constexpr int A_BYTES = WIN ? TPM * BOX_BYTES : 128 * ROWB;  // bytes the TMA boxes of a stage deliver
+  static constexpr int A_STAGE = ((A_BYTES + 1023) / 1024) * 1024;     // stage stride (1024-aligned)
   static constexpr int B_KB = NCTA * ROWB;
   static constexpr int W_BYTES = NWKB * B_KB;
   static constexpr int TMEM_COLS = (2 * NCTA) <= 32 ? 32 : (2 * NCTA) <= 64 ? 64 : (2 * NCTA) <= 128 ? 128 : (2 * NCTA) <= 256 ? 256 : 512;
@@ -68,21 +75,32 @@ struct TcCfg {
   static constexpr int W_OFF = 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
   static constexpr int BIAS_BYTES = 256 * 4;          // every output channel (C_out <= 256)
-  static constexpr int BAR_BYTES = 256;
-  // first layer: staged input window of one M-tile (BOX_ROWS output rows of one tile)
+  static constexpr int CRING = 16;                    // item-coordinate ring (producer -> epilogue)
+  static constexpr int CRING_BYTES = CRING * 8 * 4 * 4; // <= 8 units x (cam, row, col, pad) per item
+  static constexpr int BAR_BYTES = 768;
+  // first layer: the input window of one M-tile (BOX_ROWS output rows of one tile), loaded
+  // by one 3-D TMA box from the image cache viewed as [N][H][W*CIN]; the box starts 8
+  // elements (16 B) before the window's first element... rounded so x stays 16-byte aligned
   static constexpr int WIN_ROWS = (BOX_ROWS - 1) * S + 3;
-  static constexpr int WIN_COLS = (T - 1) * S + 3;
-  static constexpr int WIN_BYTES = MANUAL ? ((WIN_ROWS * WIN_COLS * CIN * 2 + 15) / 16) * 16 : 0;
-  static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES;
+  static constexpr int WIN_ELEMS = ((T - 1) * S + 3) * CIN;
+  static constexpr int WIN_COLS = ((8 + WIN_ELEMS + 7) / 8) * 8;     // box inner extent (elements)
+  static constexpr int WIN_LEAD = 8 - CIN;                            // elements before the first used one
+  static constexpr int WIN_BUF = ((WIN_ROWS * WIN_COLS * 2 + 127) / 128) * 128;
+  static constexpr int NWB = 4;                                       // window ring depth
+  static constexpr int WIN_BYTES = MANUAL ? NWB * WIN_BUF : 0;
+  static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr int SMEM = FIXED + A_OFF + STAGES * A_STAGE;
   static constexpr uint32_t IDESC = idesc_f16(128, NCTA);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
+  static_assert(TPM <= 8, "coordinate ring holds up to 8 units per item");
   static_assert(NCTA % 32 == 0 && NCTA >= 32 && NCTA <= 256, "UMMA N / epilogue split");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
-  static_assert(!WIN || (S == 1 && WIN * T == 8 && ROWB == 128 && !MANUAL), "window mode geometry");
+  static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256), "first-layer window box");
+  static_assert(!WIN || ((WIN == 1 || WIN == 3) && S == 1 && 8 % T == 0 && T <= 8 && ROWB == 128 && !MANUAL),
+                "window mode geometry");
 };
 
 struct TileXY {
@@ -91,21 +109,24 @@ struct TileXY {
 
 // Active-tile i of this layer: dense -> every block in flat order; sparse -> the
 // block list (entries past the listed count are block 0, as nonzero_static pads).
-// For WIN == 2 the entries are horizontal block pairs and `bx` is the pair column.
+// Unit i of this layer (a block, or for window modes a region of a.rw x a.rh blocks):
+// dense -> every unit in flat order; sparse -> the ordered list (entries past the listed
+// count are unit 0, as nonzero_static pads).  Returns (cam, unit row, unit column).
 template <int WIN>
 SB_DEV TileXY tile_at(const ConvArgs& a, int mode, int listed, int i) {
   TileXY r{0, 0, 0};
   if (mode == SB_MODE_DENSE) {
-    const int wd = WIN == 2 ? (a.wb + 1) / 2 : a.wb;
-    const int per = a.hb * wd;
+    const int gw = WIN ? (a.wb + a.rw - 1) / a.rw : a.wb;
+    const int gh = WIN ? (a.hb + a.rh - 1) / a.rh : a.hb;
+    const int per = gh * gw;
     r.cam = i / per;
     const int q = i - r.cam * per;
-    r.by = q / wd;
-    r.bx = q - r.by * wd;
+    r.by = q / gw;
+    r.bx = q - r.by * gw;
   } else if (i < listed) {
-    const int32_t* lc = WIN == 2 ? a.pcam : a.lcam;
-    const int32_t* ly = WIN == 2 ? a.pby : a.lby;
-    const int32_t* lx = WIN == 2 ? a.ppx : a.lbx;
+    const int32_t* lc = WIN ? a.rcam : a.lcam;
+    const int32_t* ly = WIN ? a.rry : a.lby;
+    const int32_t* lx = WIN ? a.rrx : a.lbx;
     r.cam = __ldg(lc + i);
     r.by = __ldg(ly + i);
     r.bx = __ldg(lx + i);
@@ -140,9 +161,14 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
   uint64_t* wfull = acce + 2;
   uint64_t* wempty = wfull + 1;
   uint64_t* dbar = wempty + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(dbar + 1);
+  uint64_t* winfull = dbar + 1;          // first-layer window ring
+  uint64_t* winempty = winfull + C::NWB;
+  uint64_t* cfull = winempty + C::NWB;   // item-coordinate ring
+  uint64_t* cempty = cfull + C::CRING;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(cempty + C::CRING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   __half* win = reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);
+  int4* sCoord = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(win) + C::WIN_BYTES);  // [CRING][8]
 
   const int warp = warp_id(), lane = lane_id();
 
@@ -158,6 +184,14 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
     mbar_init(wfull, 1);
     mbar_init(wempty, 1);
     mbar_init(dbar, 1);
+    for (int i = 0; i < C::NWB; ++i) {
+      mbar_init(&winfull[i], 1);
+      mbar_init(&winempty[i], 128);
+    }
+    for (int i = 0; i < C::CRING; ++i) {
+      mbar_init(&cfull[i], 1);
+      mbar_init(&cempty[i], 8);  // one arrival per epilogue warp
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -174,8 +208,9 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
 
   // work of this launch, decided on the device (no host sync)
   const int mode = a.st->mode_cur;
-  const int listed = WIN == 2 ? a.st->pcounts[a.d_idx] : a.st->counts[a.d_idx];
-  const int n_units = WIN == 2 ? a.n_blocks / (a.hb * a.wb) * a.hb * ((a.wb + 1) / 2) : a.n_blocks;
+  const int listed = WIN ? a.st->rcounts[a.rkind][a.d_idx] : a.st->counts[a.d_idx];
+  const int n_units =
+      WIN ? a.n_blocks / (a.hb * a.wb) * ((a.hb + a.rh - 1) / a.rh) * ((a.wb + a.rw - 1) / a.rw) : a.n_blocks;
   int n_tiles = 0;
   if (mode == SB_MODE_DENSE) n_tiles = n_units;
   else if (mode == SB_MODE_SPARSE) n_tiles = a.st->force_tiles > 0 ? a.st->force_tiles : listed;
@@ -188,30 +223,52 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
     if (warp == C::PROD_WARP) {
       // ------------------------------------------------ producer: weights per C_out slice, A stages
       // The whole warp runs the loop (warp-uniform control flow); lane 0 issues the copies.
+      // Tile coordinates are fetched one item ahead into the other of two register sets
+      // (the loop is unrolled by two, so no set is ever copied while its loads are in flight).
       const bool leader = lane == 0;
       uint32_t g = 0, nload = 0;
       int cur = -1;
-      int ncam[C::TPM], ny0[C::TPM], nx0[C::TPM];
-      auto fetch = [&](const Item& w) {
+      struct Coords {
+        int cam[C::TPM], y0[C::TPM], x0[C::TPM], uy[C::TPM], ux[C::TPM];
+      };
+      auto fetch = [&](int it, Coords& o) {
+        const Item w = item_at(it, n_mtiles);
 #pragma unroll
         for (int j = 0; j < C::TPM; ++j) {
           int ti, sub;
           if (!WIN && C::TT >= 128) { ti = w.m / C::MPT; sub = w.m % C::MPT; }
           else { ti = w.m * C::TPM + j; sub = 0; }
           const TileXY p = tile_at<WIN>(a, mode, listed, ti < n_tiles ? ti : 0);
-          ncam[j] = p.cam;
-          ny0[j] = (p.by * T + sub * C::BOX_ROWS) * S - 1;
-          nx0[j] = (WIN ? p.bx * 8 : p.bx * T * S) - 1;
+          o.uy[j] = p.by;
+          o.ux[j] = p.bx;
+          o.cam[j] = p.cam;
+          o.y0[j] = (WIN ? p.by * C::RROWS : (p.by * T + sub * C::BOX_ROWS) * S) - 1;
+          o.x0[j] = (WIN ? p.bx * 8 : p.bx * T * S) - 1;
         }
       };
-      if (!C::MANUAL) fetch(item_at(0, n_mtiles));
-      for (int it = 0; it < my_items && !*abort_flag; ++it) {
+      // returns false when the pipeline was aborted
+      auto issue = [&](int it, const Coords& cc) -> bool {
         const Item w = item_at(it, n_mtiles);
+        // publish this item's unit coordinates for the epilogue
+        {
+          const int slot = it % C::CRING;
+          if (!warp_wait(&cempty[slot], ((it / C::CRING) & 1) ^ 1, abort_flag)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+            return false;
+          }
+          if (leader) {
+#pragma unroll
+            for (int j = 0; j < C::TPM; ++j) sCoord[slot * 8 + j] = make_int4(cc.cam[j], cc.uy[j], cc.ux[j], 0);
+            mbar_arrive(&cfull[slot]);
+          }
+          __syncwarp();
+        }
         if (w.split != cur) {
           if (nload > 0 && !warp_wait(wempty, (nload - 1) & 1u, abort_flag)) {
             atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
             *abort_flag = 1;
-            break;
+            return false;
           }
           const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)w.split * C::W_BYTES;
           if (leader) {
@@ -225,77 +282,80 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           ++nload;
           cur = w.split;
         }
-        if (C::MANUAL) continue;
-        // coordinates of this item were fetched one item ahead; fetch the next item's now so
-        // the list lookups overlap this item's K-blocks instead of stalling the pipeline
-        int cam[C::TPM], y0[C::TPM], x0[C::TPM];
-#pragma unroll
-        for (int j = 0; j < C::TPM; ++j) {
-          cam[j] = ncam[j];
-          y0[j] = ny0[j];
-          x0[j] = nx0[j];
+        if (C::MANUAL) {
+          // first layer: one window box per item into the ring
+          const int b = it % C::NWB;
+          if (!warp_wait(&winempty[b], ((it / C::NWB) & 1) ^ 1, abort_flag)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+            return false;
+          }
+          if (leader) {
+            mbar_arrive_expect_tx(&winfull[b], C::WIN_ROWS * C::WIN_COLS * 2);
+            tma_load_3d(reinterpret_cast<uint8_t*>(win) + b * C::WIN_BUF, &tmap, &winfull[b],
+                        (cc.x0[0] + 1) * CIN - CIN - C::WIN_LEAD, cc.y0[0], cc.cam[0]);
+          }
+          __syncwarp();
+          ++g;
+          return true;
         }
-        if (it + 1 < my_items) fetch(item_at(it + 1, n_mtiles));
         for (int kb = 0; kb < C::NKB; ++kb, ++g) {
           // im2col: K-block = (tap, chunk); window: K-block = (ky, chunk), the 3 kx taps read
           // the same window rows at offsets of kx pixels
-          const int tap = WIN ? (kb / C::NCH) * 3 : kb / C::NCH, ch = kb % C::NCH;
+          // full window: K-block = chunk, the box covers all taps
+          const int tap = WIN == 3 ? 0 : WIN ? (kb / C::NCH) * 3 : kb / C::NCH, ch = kb % C::NCH;
           const int ky = tap / 3, kx = WIN ? 0 : tap % 3;
           const int s = g % C::STAGES;
           const uint32_t ph = (g / C::STAGES) & 1u;
           if (!warp_wait(&empty[s], ph ^ 1u, abort_flag)) {
             atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
             *abort_flag = 1;
-            break;
+            return false;
           }
           if (leader) {
-            mbar_arrive_expect_tx(&full[s], C::A_STAGE);
+            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
             uint8_t* dst = sA + s * C::A_STAGE;
 #pragma unroll
             for (int j = 0; j < C::TPM; ++j)
-              tma_load_4d(dst + j * C::BOX_BYTES, &tmap, &full[s], ch * C::CH, x0[j] + kx, y0[j] + ky, cam[j]);
+              tma_load_4d(dst + j * C::BOX_BYTES, &tmap, &full[s], ch * C::CH, cc.x0[j] + kx, cc.y0[j] + ky,
+                          cc.cam[j]);
           }
           __syncwarp();
         }
+        return true;
+      };
+      Coords ca, cb;
+      fetch(0, ca);
+      for (int it = 0; it < my_items && !*abort_flag; it += 2) {
+        if (it + 1 < my_items) fetch(it + 1, cb);
+        if (!issue(it, ca) || it + 1 >= my_items) break;
+        if (it + 2 < my_items) fetch(it + 2, ca);
+        if (!issue(it + 1, cb)) break;
       }
       // drain: every issued copy has landed before the CTA may exit
       volatile int never = 0;
-      const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0u;
-      for (uint32_t q = first; q < g; ++q) warp_wait(&full[q % C::STAGES], (q / C::STAGES) & 1u, &never);
+      if (C::MANUAL) {
+        const uint32_t first = g > (uint32_t)C::NWB ? g - C::NWB : 0u;
+        for (uint32_t q = first; q < g; ++q) warp_wait(&winfull[q % C::NWB], (q / C::NWB) & 1u, &never);
+      } else {
+        const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0u;
+        for (uint32_t q = first; q < g; ++q) warp_wait(&full[q % C::STAGES], (q / C::STAGES) & 1u, &never);
+      }
       if (nload > 0) warp_wait(wfull, (nload - 1) & 1u, &never);
     } else if (C::MANUAL && (int)threadIdx.x >= C::GATHER0) {
       // ------------------------------------------------ gather producers (first layer)
-      // Per M-tile: stage the input window (with the image-border zero padding) in shared
-      // memory with coalesced loads, then build each A row (one output pixel: 3x3 taps x
-      // channels, zero-padded to KPAD) from it.
+      // Each thread builds one A row (one output pixel: 3x3 taps x channels, zero-padded to
+      // KPAD) from the TMA-loaded input window of its item.
       const int r = threadIdx.x - C::GATHER0;  // A row = output pixel slot, 0..127
-      const __half* x = static_cast<const __half*>(a.x);
-      constexpr int RW = C::WIN_ROWS, WW = C::WIN_COLS, ROWE = WW * CIN;
+      const int lr = r / T, lc = r % T;
       uint32_t g = 0;
       for (int it = 0; it < my_items && !*abort_flag; ++it, ++g) {
-        const Item w = item_at(it, n_mtiles);
-        const int ti = w.m / C::MPT, sub = w.m % C::MPT;
-        const TileXY tc = tile_at<WIN>(a, mode, listed, ti < n_tiles ? ti : 0);
-        const int iy0 = (tc.by * T + sub * C::BOX_ROWS) * S - 1, ix0 = tc.bx * T * S - 1;
-        const __half* xc = x + (size_t)tc.cam * a.hx * a.wx * CIN;
-        // all loads of this thread's window share first (independent, in flight together),
-        // then the shared-memory stores
-        constexpr int NLD = (RW * ROWE + 127) / 128;
-        uint16_t wv[NLD];
-#pragma unroll
-        for (int k = 0; k < NLD; ++k) {
-          const int idx = r + 128 * k;
-          const int wy = idx / ROWE, e = idx - wy * ROWE;
-          const int iy = iy0 + wy, ix = ix0 + e / CIN;
-          wv[k] = 0;
-          if (idx < RW * ROWE && iy >= 0 && iy < a.hx && ix >= 0 && ix < a.wx)
-            wv[k] = __half_as_ushort(__ldg(xc + ((size_t)iy * a.wx + ix) * CIN + (e % CIN)));
+        const int b = it % C::NWB;
+        if (!mbar_wait(&winfull[b], (it / C::NWB) & 1u, abort_flag)) {
+          atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+          *abort_flag = 1;
+          break;
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // previous window fully consumed
-#pragma unroll
-        for (int k = 0; k < NLD; ++k)
-          if (r + 128 * k < RW * ROWE) reinterpret_cast<uint16_t*>(win)[r + 128 * k] = wv[k];
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // window complete
         const int s = g % C::STAGES;
         const uint32_t ph = (g / C::STAGES) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
@@ -303,8 +363,11 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           *abort_flag = 1;
           break;
         }
-        const int lr = r / T, lc = r % T;
-        const uint16_t* wrow = reinterpret_cast<const uint16_t*>(win) + (lr * S) * ROWE + (lc * S) * CIN;
+        // element (ky, kx, c) of output (lr, lc): window row S*lr+ky, column
+        // lead + (S*lc + kx)*CIN + c  (the window starts one input pixel left of the tile)
+        const uint16_t* wrow = reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(win) +
+                                                                 b * C::WIN_BUF) +
+                               (S * lr) * C::WIN_COLS + C::WIN_LEAD + (S * lc) * CIN;
         uint16_t v[C::KPAD > 0 ? C::KPAD : 16];
 #pragma unroll
         for (int k = 0; k < C::KPAD; ++k) v[k] = 0;
@@ -313,7 +376,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
 #pragma unroll
           for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-            for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = wrow[ky * ROWE + kx * CIN + c];
+            for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = wrow[ky * C::WIN_COLS + kx * CIN + c];
         uint8_t* row = sA + s * C::A_STAGE + r * C::ROWB;
         constexpr int NQ = C::ROWB / 16;
 #pragma unroll
@@ -328,6 +391,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         }
         fence_proxy_async_smem();
         mbar_arrive(&full[s]);
+        mbar_arrive(&winempty[b]);
       }
     } else if (warp == C::MMA_WARP) {
       // ------------------------------------------------ MMA issuer
@@ -368,17 +432,24 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           if (leader) {
             const uint32_t a_addr = smem_u32(sA + s * C::A_STAGE);
             if (WIN) {
-              // the three kx taps: A = window rows shifted by kx pixels (128 B rows, the
-              // hardware swizzle follows absolute smem addresses), B = that tap's weights
-              const int ky = kb / C::NCH, ch = kb % C::NCH;
+              // window taps: A = the window shifted by (ky*10 + kx) pixels (128 B rows; the
+              // hardware swizzle follows absolute smem addresses), B = that tap's weights.
+              // Row windows hold one ky per K-block, full windows all three.
+              const int ch = kb % C::NCH;
+              const int ky0 = WIN == 3 ? 0 : kb / C::NCH, nky = WIN == 3 ? 3 : 1;
 #pragma unroll
-              for (int kx = 0; kx < 3; ++kx) {
-                const uint32_t b_addr = smem_u32(sW + ((ky * 3 + kx) * C::NCH + ch) * C::B_KB);
+              for (int dy = 0; dy < nky; ++dy) {
+                const int ky = ky0 + dy;
 #pragma unroll
-                for (int kk = 0; kk < C::CH / 16; ++kk) {
-                  const uint64_t ad = smem_desc(a_addr + kx * C::ROWB + kk * 32, C::WSBO, C::SWZ);
-                  const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
-                  mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | kx | kk) != 0 ? 1u : 0u);
+                for (int kx = 0; kx < 3; ++kx) {
+                  const uint32_t b_addr = smem_u32(sW + ((ky * 3 + kx) * C::NCH + ch) * C::B_KB);
+                  const uint32_t off = ((WIN == 3 ? ky * 10 : 0) + kx) * C::ROWB;
+#pragma unroll
+                  for (int kk = 0; kk < C::CH / 16; ++kk) {
+                    const uint64_t ad = smem_desc(a_addr + off + kk * 32, C::WSBO, C::SWZ);
+                    const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
+                    mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | dy | kx | kk) != 0 ? 1u : 0u);
+                  }
                 }
               }
             } else {
@@ -419,29 +490,41 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         bool st;
         uint4 rr[C::NCOL / 8];
       };
-      auto fetch = [&](int it, Row& o) {
+      // unit coordinates come from the producer through the shared-memory ring, so the
+      // residual prefetch below depends on no global load
+      auto fetch = [&](int it, Row& o) -> bool {
         const Item w = item_at(it, n_mtiles);
         o.n0 = w.split * NCTA + col0;
-        int ti, p;
-        if (WIN) { ti = w.m * C::TPM + r / C::RPX; p = r % C::RPX; }
-        else if (C::TT >= 128) { ti = w.m / C::MPT; p = (w.m % C::MPT) * 128 + r; }
-        else { ti = w.m * C::TPM + r / C::TT; p = r % C::TT; }
+        int ti, p, j;
+        if (WIN) { j = r / C::RPX; ti = w.m * C::TPM + j; p = r % C::RPX; }
+        else if (C::TT >= 128) { j = 0; ti = w.m / C::MPT; p = (w.m % C::MPT) * 128 + r; }
+        else { j = r / C::TT; ti = w.m * C::TPM + j; p = r % C::TT; }
+        const int slot = it % C::CRING;
+        if (!mbar_wait(&cfull[slot], (it / C::CRING) & 1, abort_flag)) return false;
+        const int4 u = sCoord[slot * 8 + j];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cempty[slot]);
         const bool valid = ti < n_tiles;
-        const TileXY tc = tile_at<WIN>(a, mode, listed, valid ? ti : 0);
-        const int gy = WIN ? tc.by * T + p / 8 : tc.by * T + p / T;
+        TileXY tc{u.x, u.y, u.z};
+        const int gy = WIN ? tc.by * C::RROWS + p / 8 : tc.by * T + p / T;
         const int gx = WIN ? tc.bx * 8 + p % 8 : tc.bx * T + p % T;
         const bool inb = tc.cam < a.n && gy < a.ho && gx < a.wo;
-        if (valid && !inb) atomicOr(&a.st->error, SB_ERR_BAD_TILE);
+        // a region may overhang the image's right / bottom edge (those pixels are skipped);
+        // only a unit whose origin lies outside the image is a corrupt list entry
+        const bool origin_ok = tc.cam < a.n && (WIN ? tc.by * C::RROWS : tc.by * T) < a.ho &&
+                               (WIN ? tc.bx * 8 : tc.bx * T) < a.wo;
+        if (valid && !origin_ok) atomicOr(&a.st->error, SB_ERR_BAD_TILE);
         o.st = valid && inb;
         o.pix = (((size_t)tc.cam * a.ho + gy) * a.wo + gx) * a.cout + o.n0;
         if (res != nullptr && o.st) {
 #pragma unroll
-          for (int j = 0; j < C::NCOL / 8; ++j) o.rr[j] = __ldg(reinterpret_cast<const uint4*>(res + o.pix) + j);
+          for (int q2 = 0; q2 < C::NCOL / 8; ++q2) o.rr[q2] = __ldg(reinterpret_cast<const uint4*>(res + o.pix) + q2);
         }
+        return true;
       };
-      Row cur, nxt;
-      fetch(0, cur);
-      for (int it = 0; it < my_items; ++it) {
+      // one item: wait for the accumulator, move it to registers, release TMEM, prefetch the
+      // next item into `nx`, then bias / residual / ReLU / store item `it` from `cu`
+      auto step = [&](int it, const Row& cu, Row& nx) -> bool {
         const int ab = it & 1;
         const bool got = mbar_wait(&accf[ab], (it >> 1) & 1, abort_flag);
         if (!got) {
@@ -449,7 +532,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           *abort_flag = 1;
         }
         // warp-uniform exit: tcgen05.ld below is .sync.aligned
-        if (__any_sync(0xFFFFFFFFu, !got || *abort_flag != 0)) break;
+        if (__any_sync(0xFFFFFFFFu, !got || *abort_flag != 0)) return false;
         tc_fence_after();
         uint32_t v[C::NCOL];
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + ab * NCTA + col0;
@@ -459,15 +542,18 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&acce[ab]);  // the MMA may overwrite this buffer now
-        if (it + 1 < my_items) fetch(it + 1, nxt);
-        if (cur.st) {
+        if (it + 1 < my_items && !fetch(it + 1, nx)) {
+          atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+          *abort_flag = 1;
+        }
+        if (cu.st) {
 #pragma unroll
           for (int j = 0; j < C::NCOL / 8; ++j) {
             float f[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + sBias[cur.n0 + j * 8 + e];
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + sBias[cu.n0 + j * 8 + e];
             if (res != nullptr) {
-              const __half2* h = reinterpret_cast<const __half2*>(&cur.rr[j]);
+              const __half2* h = reinterpret_cast<const __half2*>(&cu.rr[j]);
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 t2 = __half22float2(h[e]);
@@ -483,10 +569,19 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
             __half2* ph = reinterpret_cast<__half2*>(&o);
 #pragma unroll
             for (int e = 0; e < 4; ++e) ph[e] = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
-            reinterpret_cast<uint4*>(y + cur.pix)[j] = o;
+            reinterpret_cast<uint4*>(y + cu.pix)[j] = o;
           }
         }
-        cur = nxt;
+        return true;
+      };
+      Row ra, rb;
+      if (!fetch(0, ra)) {
+        atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+        *abort_flag = 1;
+      }
+      for (int it = 0; it < my_items; it += 2) {
+        if (!step(it, ra, rb) || it + 1 >= my_items) break;
+        if (!step(it + 1, rb, ra)) break;
       }
     }
   }
@@ -504,14 +599,14 @@ namespace {
 struct Variant {
   int cin, cout, t, s, win, ncta;
   void (*fn)(const ConvArgs, const CUtensorMap);
-  int smem, threads, w_bytes, ch, box_rows;
+  int smem, threads, w_bytes, ch, box_rows, win_cols, win_rows;
 };
 
 template <int CIN, int NCTA, int T, int S, int WIN = 0>
 Variant make_variant(int cout) {
   using C = TcCfg<CIN, NCTA, T, S, WIN>;
   return Variant{CIN, cout, T, S, WIN, NCTA, conv_tc_kernel<CIN, NCTA, T, S, WIN>, C::SMEM, C::THREADS, C::W_BYTES,
-                 C::CH, C::BOX_ROWS};
+                 C::CH, C::BOX_ROWS, C::WIN_COLS, C::WIN_ROWS};
 }
 
 // Sarbon stem shapes (widths 32/64/128, Res blocks) at block 32 and block 64.
@@ -520,30 +615,41 @@ const std::vector<Variant>& variants() {
       // block 32
       make_variant<3, 32, 16, 2>(32),
       make_variant<32, 64, 8, 2>(64),
-      make_variant<64, 64, 8, 1, 1>(64),    // shifted window, 8x8 blocks
+      make_variant<64, 64, 8, 1, 1>(64),    // row windows over blocks
+      make_variant<64, 64, 8, 1, 3>(64),    // full windows over 1x2-block regions
       make_variant<64, 128, 4, 2>(128),
-      make_variant<128, 64, 4, 1, 2>(128),  // shifted window over block pairs; two C_out slices
+      make_variant<128, 64, 4, 1, 1>(128),  // row windows over horizontal block pairs; two C_out slices
+      make_variant<128, 64, 4, 1, 3>(128),  // full windows over 2x4-block regions
       // block 64
       make_variant<3, 32, 32, 2>(32),
       make_variant<32, 64, 16, 2>(64),
       make_variant<64, 64, 16, 1>(64),
       make_variant<64, 128, 8, 2>(128),
-      make_variant<128, 64, 8, 1, 1>(128),  // shifted window, 8x8 blocks
+      make_variant<128, 64, 8, 1, 3>(128),  // full windows over 1x2-block regions
+      make_variant<128, 64, 8, 1, 1>(128),
   };
   return v;
 }
 
-const Variant* find_variant(int cin, int cout, int t, int s) {
+// The first variant of a shape is its default mode; SARBON_WINDOW_MODE=0|1|3 overrides it
+// for the window-capable shapes (measurement aid).
+const Variant* find_variant(int cin, int cout, int t, int s, int win = -1) {
   for (const auto& v : variants())
-    if (v.cin == cin && v.cout == cout && v.t == t && v.s == s) return &v;
+    if (v.cin == cin && v.cout == cout && v.t == t && v.s == s && (win < 0 || v.win == win)) return &v;
   return nullptr;
 }
 
 }  // namespace
 
-int conv_tc_region(int cin, int cout, int t, int s) {
+int conv_tc_pick_mode(int cin, int cout, int t, int s) {
   const Variant* v = find_variant(cin, cout, t, s);
-  return v ? v->win : -1;
+  if (!v) return -1;
+  const char* env = std::getenv("SARBON_WINDOW_MODE");
+  if (env && v->win != 0) {
+    const int want = std::atoi(env);
+    if (find_variant(cin, cout, t, s, want)) return want;
+  }
+  return v->win;
 }
 
 namespace {
@@ -625,12 +731,26 @@ static PFN_encodeTiled get_encode() {
 // 4-D tiled map over an NHWC fp16 cache: dims {C, W, H, N}; box {CH, T*S, rows*S, 1}
 // with element strides {1, S, S, 1} so that one box is the strided im2col slice of one
 // tap for one tile.
-cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s) {
+cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s,
+                              int mode) {
   const Variant* v = nullptr;
   for (const auto& c : variants())
-    if (c.cin == cin && c.t == t && c.s == s) { v = &c; break; }
-  if (!v || cin < 16) return cudaErrorInvalidValue;
+    if (c.cin == cin && c.t == t && c.s == s && c.win == mode) { v = &c; break; }
+  if (!v) return cudaErrorInvalidValue;
   const bool win = v->win != 0;
+  if (cin < 16) {
+    // first layer: the image cache as [N][H][W*cin] fp16, one box = one M-tile's window
+    PFN_encodeTiled enc = get_encode();
+    if (!enc) return cudaErrorNotSupported;
+    cuuint64_t dims[3] = {(cuuint64_t)wx * cin, (cuuint64_t)hx, (cuuint64_t)n};
+    cuuint64_t strides[2] = {(cuuint64_t)wx * cin * 2, (cuuint64_t)hx * wx * cin * 2};
+    cuuint32_t box[3] = {(cuuint32_t)v->win_cols, (cuuint32_t)v->win_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(src), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+  }
   PFN_encodeTiled enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
   cuuint64_t dims[4] = {(cuuint64_t)cin, (cuuint64_t)wx, (cuuint64_t)hx, (cuuint64_t)n};
@@ -645,17 +765,17 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t launch_conv_tc(const ConvArgs& a, const CUtensorMap* map, int grid_x, cudaStream_t st) {
-  const Variant* v = find_variant(a.cin, a.cout, a.t, a.s);
-  if (!v) return cudaErrorInvalidValue;
-  static bool attr_done[16] = {};
+cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, int grid_x, cudaStream_t st) {
+  const Variant* v = find_variant(a.cin, a.cout, a.t, a.s, mode);
+  if (!v || map == nullptr) return cudaErrorInvalidValue;  // every variant loads through TMA
+  static bool attr_done[32] = {};
   const int idx = (int)(v - variants().data());
   if (!attr_done[idx]) {
     cudaError_t e = cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem);
     if (e != cudaSuccess) return e;
     attr_done[idx] = true;
   }
-  static int occ[16] = {};
+  static int occ[32] = {};
   if (occ[idx] == 0) {
     int o = 1;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, v->fn, v->threads, v->smem) != cudaSuccess || o < 1) o = 1;

@@ -73,8 +73,12 @@ struct sb_engine {
   uint8_t* extra = nullptr;
   uint8_t* masks = nullptr;
   int32_t* lists = nullptr;
-  int32_t* plists = nullptr;   // horizontal block-pair lists (window-mode 4x4-tile layers)
-  int n_pairs = 0;
+  // region kinds (rw x rh blocks) of the window-mode layers and their ordered lists
+  int n_rk = 0;
+  int rk_w[SB_MAX_RKINDS] = {}, rk_h[SB_MAX_RKINDS] = {}, rk_cap[SB_MAX_RKINDS] = {};
+  int32_t* rlists[SB_MAX_RKINDS] = {};
+  int layer_mode[SB_MAX_LAYERS] = {};   // 0 im2col / gather, 1 row windows, 3 full windows
+  int layer_rk[SB_MAX_LAYERS] = {};     // region kind of a window-mode layer (-1: blocks)
   unsigned long long* status = nullptr;
   int n_chunks = 0;
   State* st = nullptr;
@@ -144,13 +148,18 @@ int launch_convs(sb_engine* e, cudaStream_t s) {
     a.t = e->layer_t[i];
     a.s = L.stride;
     a.act = L.act;
-    a.region = e->dtype == SB_F16 ? conv_tc_region(L.cin, L.cout, a.t, a.s) : 0;
-    a.pcam = e->plists + (size_t)di * 3 * e->n_pairs;
-    a.pby = a.pcam + e->n_pairs;
-    a.ppx = a.pby + e->n_pairs;
+    const int rk = e->layer_rk[i];
+    a.rkind = rk;
+    a.rw = rk >= 0 ? e->rk_w[rk] : 1;
+    a.rh = rk >= 0 ? e->rk_h[rk] : 1;
+    if (rk >= 0) {
+      a.rcam = e->rlists[rk] + (size_t)di * 3 * e->rk_cap[rk];
+      a.rry = a.rcam + e->rk_cap[rk];
+      a.rrx = a.rry + e->rk_cap[rk];
+    }
     cudaError_t err;
     if (e->dtype == SB_F16) {
-      err = launch_conv_tc(a, e->has_tmap[i] ? &e->tmap[i] : nullptr, e->n_sms, s);
+      err = launch_conv_tc(a, e->layer_mode[i], e->has_tmap[i] ? &e->tmap[i] : nullptr, e->n_sms, s);
     } else {
       err = launch_conv_simt(a, e->n_sms * 4, s);
     }
@@ -205,7 +214,12 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
   l.changed = e->changed;
   l.masks = e->masks;
   l.lists = e->lists;
-  l.plists = e->plists;
+  l.n_rk = e->n_rk;
+  for (int k = 0; k < e->n_rk; ++k) {
+    l.rw[k] = e->rk_w[k];
+    l.rh[k] = e->rk_h[k];
+    l.rlists[k] = e->rlists[k];
+  }
   l.status = e->status;
   l.st = e->st;
   l.n_blocks = e->n_blocks;
@@ -390,9 +404,29 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
   if ((rc = alloc_dev(e, (void**)&e->extra, e->n_blocks))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->masks, (size_t)e->nd * e->n_blocks))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->lists, (size_t)e->nd * 3 * e->n_blocks * 4))) return bail(rc);
-  e->n_pairs = n_streams * e->hb * ((e->wb + 1) / 2);
-  if ((rc = alloc_dev(e, (void**)&e->plists, (size_t)e->nd * 3 * e->n_pairs * 4))) return bail(rc);
-  if ((rc = alloc_dev(e, (void**)&e->status, (size_t)2 * e->nd * e->n_chunks * 8))) return bail(rc);
+  // window-mode layers: the region kind each one iterates over
+  for (int i = 0; i < n_layers; ++i) {
+    e->layer_rk[i] = -1;
+    e->layer_mode[i] = dtype == SB_F16 ? conv_tc_pick_mode(layers[i].cin, layers[i].cout, e->layer_t[i],
+                                                           layers[i].stride)
+                                       : 0;
+    if (e->layer_mode[i] == 0) continue;
+    const int t = e->layer_t[i];
+    const int rw = 8 / t, rh = e->layer_mode[i] == 3 ? 16 / t : 1;
+    int k = 0;
+    while (k < e->n_rk && !(e->rk_w[k] == rw && e->rk_h[k] == rh)) ++k;
+    if (k == e->n_rk) {
+      if (k == SB_MAX_RKINDS) return bail(fail(SB_EINVAL, "too many region kinds"));
+      e->rk_w[k] = rw;
+      e->rk_h[k] = rh;
+      e->rk_cap[k] = n_streams * ((e->hb + rh - 1) / rh) * ((e->wb + rw - 1) / rw);
+      ++e->n_rk;
+    }
+    e->layer_rk[i] = k;
+  }
+  for (int k = 0; k < e->n_rk; ++k)
+    if ((rc = alloc_dev(e, (void**)&e->rlists[k], (size_t)e->nd * 3 * e->rk_cap[k] * 4))) return bail(rc);
+  if ((rc = alloc_dev(e, (void**)&e->status, (size_t)(1 + e->n_rk) * e->nd * e->n_chunks * 8))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->st, sizeof(State)))) return bail(rc);
   State init{};
   init.epoch = 1;
@@ -415,9 +449,10 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
     const size_t wbytes = dtype == SB_F16 ? conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[i], L.stride)
                                           : (size_t)9 * L.cin * L.cout * 4;
     if ((rc = alloc_dev(e, &e->wdev[i], wbytes))) return bail(rc);
-    if (dtype == SB_F16 && L.cin >= 16) {
+    if (dtype == SB_F16) {  // every fp16 layer loads its input by TMA (the first layer: window boxes)
       cudaError_t err = conv_tc_make_tmap(&e->tmap[i], e->cache[L.src], n_streams, (int)e->shape[L.src][1],
-                                          (int)e->shape[L.src][2], L.cin, e->layer_t[i], L.stride);
+                                          (int)e->shape[L.src][2], L.cin, e->layer_t[i], L.stride,
+                                          e->layer_mode[i]);
       if (err != cudaSuccess) return bail(fail(SB_ECUDA, std::string("tensor map: ") + cudaGetErrorString(err)));
       e->has_tmap[i] = true;
     }

@@ -314,8 +314,10 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
     }
     return;
   }
-  // compaction lanes: kind 0 = blocks, kind 1 = horizontal block pairs; one per dilation
-  constexpr int ML = 2 * SB_MAX_DILATIONS;
+  // compaction lanes: one per (unit kind, dilation); kind 0 = blocks, kind k >= 1 = regions
+  // of rw[k-1] x rh[k-1] blocks (active when any of their blocks is active at that dilation)
+  constexpr int NK = 1 + SB_MAX_RKINDS;
+  constexpr int ML = NK * SB_MAX_DILATIONS;
   __shared__ uint32_t s_chunk;
   __shared__ uint32_t s_warp[ML][32];
   __shared__ uint32_t s_excl[ML];
@@ -325,36 +327,38 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
   const uint32_t chunk = s_chunk;
   const int nchunks = gridDim.x;
   const int f = (int)chunk * LIST_THREADS + threadIdx.x;
-  const int per = a.hb * a.wb, wp = (a.wb + 1) / 2, perp = a.hb * wp;
-  const int n_pairs = a.n_blocks / per * perp;
-  const int nl = 2 * a.n_dil;
+  const int per = a.hb * a.wb, ncam = a.n_blocks / per;
+  const int nk = 1 + a.n_rk, nl = nk * a.n_dil;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t rank[ML];
   bool act[ML];
-  int coord[2][3];
+  int coord[NK][3];
+  int caps[NK];
 #pragma unroll
-  for (int kind = 0; kind < 2; ++kind) {
-    const bool valid = kind == 0 ? f < a.n_blocks : f < n_pairs;
-    int cam = 0, by = 0, bx = 0;
+  for (int kind = 0; kind < NK; ++kind) {
+    if (kind >= nk) break;
+    const int rw = kind ? a.rw[kind - 1] : 1, rh = kind ? a.rh[kind - 1] : 1;
+    const int gw = (a.wb + rw - 1) / rw, gh = (a.hb + rh - 1) / rh;
+    caps[kind] = ncam * gh * gw;
+    const bool valid = f < caps[kind];
+    int cam = 0, ry = 0, rx = 0;
     if (valid) {
-      const int pr = kind == 0 ? per : perp, wd = kind == 0 ? a.wb : wp;
-      cam = f / pr;
-      const int r = f - cam * pr;
-      by = r / wd;
-      bx = r - by * wd;
+      cam = f / (gh * gw);
+      const int r = f - cam * gh * gw;
+      ry = r / gw;
+      rx = r - ry * gw;
     }
     coord[kind][0] = cam;
-    coord[kind][1] = by;
-    coord[kind][2] = bx;
+    coord[kind][1] = ry;
+    coord[kind][2] = rx;
     const uint8_t* cm = a.changed + (size_t)cam * per;
-    const int xlo = kind == 0 ? bx : 2 * bx, xhi = kind == 0 ? bx : 2 * bx + 1;
     for (int di = 0; di < a.n_dil; ++di) {
       const int d = a.ds[di], L = kind * a.n_dil + di;
       bool on = false;
       if (valid) {
-        // block: max_pool(2d+1) of `changed` (fused_engine.py:151); pair: either block of the pair
-        const int y0 = max(0, by - d), y1 = min(a.hb - 1, by + d);
-        const int x0 = max(0, xlo - d), x1 = min(a.wb - 1, xhi + d);
+        // blocks: max_pool(2d+1) of `changed` (fused_engine.py:151); regions: any of their blocks
+        const int y0 = max(0, ry * rh - d), y1 = min(a.hb - 1, ry * rh + rh - 1 + d);
+        const int x0 = max(0, rx * rw - d), x1 = min(a.wb - 1, rx * rw + rw - 1 + d);
         for (int y = y0; y <= y1 && !on; ++y)
           for (int x = x0; x <= x1; ++x)
             if (__ldg(cm + y * a.wb + x)) { on = true; break; }
@@ -408,8 +412,9 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
         }
         s_excl[L] = excl;
         if ((int)chunk == nchunks - 1) {
-          if (L < a.n_dil) st->counts[L] = (int32_t)(excl + agg);
-          else st->pcounts[L - a.n_dil] = (int32_t)(excl + agg);
+          const int kind = L / a.n_dil, di = L - kind * a.n_dil;
+          if (kind == 0) st->counts[di] = (int32_t)(excl + agg);
+          else st->rcounts[kind - 1][di] = (int32_t)(excl + agg);
         }
       }
     }
@@ -417,11 +422,11 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
   __syncthreads();
   for (int L = 0; L < nl; ++L) {
     if (!act[L]) continue;
-    const int kind = L >= a.n_dil, di = L - kind * a.n_dil;
+    const int kind = L / a.n_dil, di = L - kind * a.n_dil;
     const uint32_t pos = s_excl[L] + s_warp[L][warp] + rank[L];
-    const int cap = kind ? n_pairs : a.n_blocks;
+    const int cap = caps[kind];
     if (pos < (uint32_t)cap) {
-      int32_t* Lp = (kind ? a.plists : a.lists) + (size_t)di * 3 * cap;
+      int32_t* Lp = (kind ? a.rlists[kind - 1] : a.lists) + (size_t)di * 3 * cap;
       Lp[pos] = coord[kind][0];
       Lp[cap + pos] = coord[kind][1];
       Lp[2 * (size_t)cap + pos] = coord[kind][2];

@@ -10,6 +10,10 @@
 
 namespace sb {
 
+// Region kinds: groups of rw x rh blocks a window-mode conv processes as one unit (the
+// block itself is kind "blocks" and has its own lists).
+#define SB_MAX_RKINDS 3
+
 // Device-resident engine state.  Written only by the engine's own kernels (and by
 // cudaMemcpyAsync for host-set knobs), so a whole step runs without a host sync.
 struct State {
@@ -30,7 +34,7 @@ struct State {
   int32_t last_mode;
   int32_t pad_;
   int64_t result[2];    // {mode, count} of the last finished step
-  int32_t pcounts[SB_MAX_DILATIONS];  // active horizontal block pairs per dilation this step
+  int32_t rcounts[SB_MAX_RKINDS][SB_MAX_DILATIONS];  // active regions per region kind and dilation
 };
 
 struct GateArgs {
@@ -51,8 +55,10 @@ struct ListArgs {
   const uint8_t* changed;  // [n_blocks]
   uint8_t* masks;          // [n_dil][n_blocks]
   int32_t* lists;          // [n_dil][3][n_blocks] (cam, by, bx)
-  int32_t* plists;         // [n_dil][3][n_pairs] (cam, by, bx/2): horizontal block pairs
-  unsigned long long* status;  // [2*n_dil][n_chunks] look-back words
+  int n_rk;                // region kinds
+  int rw[SB_MAX_RKINDS], rh[SB_MAX_RKINDS];   // region shape in blocks
+  int32_t* rlists[SB_MAX_RKINDS];             // [n_dil][3][rcap] (cam, ry, rx)
+  unsigned long long* status;  // [(1+n_rk)*n_dil][n_chunks] look-back words
   State* st;
   int n_blocks, hb, wb, n_dil;
   int ds[SB_MAX_DILATIONS];
@@ -83,10 +89,11 @@ struct ConvArgs {
   int ho, wo, cout;
   int hb, wb, n_blocks;
   int t, s, act;
-  int region;              // 0: tiles = blocks; 1: windowed blocks; 2: windowed horizontal block pairs
-  const int32_t* pcam;     // pair lists (region 2)
-  const int32_t* pby;
-  const int32_t* ppx;
+  int rkind;               // -1: units are blocks; else the region kind of rcam/rry/rrx
+  int rw, rh;              // region shape in blocks (1, 1 for blocks)
+  const int32_t* rcam;     // region lists of this layer's dilation
+  const int32_t* rry;
+  const int32_t* rrx;
 };
 
 // ---------------------------------------------------------------- launchers
@@ -97,15 +104,17 @@ cudaError_t launch_finalize(State* st, int refresh, int32_t* host_out, cudaStrea
 cudaError_t launch_set_mode(State* st, int mode, int reset_hyst, int64_t force_tiles, cudaStream_t s);
 
 // fp16 tcgen05 path.  Returns cudaErrorInvalidValue for shapes without an instantiation.
-bool conv_tc_supported(int cin, int cout, int t, int s);
-int conv_tc_region(int cin, int cout, int t, int s);  // ConvArgs::region the kernel expects
+bool conv_tc_supported(int cin, int cout, int t, int s);  // some mode exists for the shape
+// window mode the engine runs a layer with: 0 per-tap im2col (or first-layer gather),
+// 1 per-ky row windows over (8/t)x1-block regions, 3 full windows over (8/t)x(16/t) regions
+int conv_tc_pick_mode(int cin, int cout, int t, int s);
 int conv_tc_nsplit(int cin, int cout, int t, int s);   // CTA splits of cout
 size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s);  // all splits
 void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w /*[3][3][cin][cout]*/,
                         uint16_t* out /* fp16 bits */);
-cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t,
-                              int s);
-cudaError_t launch_conv_tc(const ConvArgs& a, const CUtensorMap* map, int grid_x, cudaStream_t s);
+cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s,
+                              int mode);
+cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, int grid_x, cudaStream_t s);
 int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s);
 
 // fp32 CUDA-core path
