@@ -158,6 +158,31 @@ SB_API int sb_gate_buffers(sb_engine* e, uint8_t** changed, uint8_t** masks, uin
 SB_API int sb_debug_lists(sb_engine* e, int d_index, int32_t** cam, int32_t** by, int32_t** bx,
                    int64_t* count, void* stream);
 
+/* Allocation-free block lists for a caller-supplied change mask.  No counterpart in
+ * the reference (it builds lists only inside FusedSparseEngine); this is for callers
+ * that cannot allocate device memory while they run -- a serving process that has
+ * planned all of its device memory up front, or code that must not stall other streams
+ * with the device-wide synchronisation cudaMalloc/cudaFree can imply -- and have no
+ * engine, e.g. a scheduler deciding which cameras' blocks to run.
+ *
+ * From `changed_dev` (uint8 [n_cams][hb][wb], nonzero = changed) it writes, on `stream`:
+ *   masks_dev  uint8 [n_dil][n_cams*hb*wb]: max_pool2d(changed, 2d+1, 1, d) per camera
+ *              for each d = dilations[i] (fused_engine.py:151)
+ *   lists_dev  int32 [n_dil][3][n_cams*hb*wb]: cam, by, bx of the active blocks in
+ *              ascending flat order (nonzero_static, fused_engine.py:161-165); entries
+ *              past the count are left as they were
+ *   counts_dev int32 [n_dil] (may be NULL): active blocks per dilation, or -1 in every
+ *              slot if a bounded device wait gave up (the lists are then invalid).
+ * Its scratch is one static device array sized for n_cams*hb*wb <= SB_STATIC_LISTS_MAX_BLOCKS;
+ * larger masks are rejected with SB_EINVAL.  Every call on a device shares that array:
+ * calls must be ordered (one stream, or events between streams); overlapping calls race.
+ * The first call on each device looks the array up (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture on the device. */
+#define SB_STATIC_LISTS_MAX_BLOCKS (1 << 20)
+SB_API int sb_block_lists_static(const uint8_t* changed_dev, int n_cams, int hb, int wb, const int* dilations,
+                                 int n_dil, uint8_t* masks_dev, int32_t* lists_dev, int32_t* counts_dev,
+                                 void* stream);
+
 /* Counters (fused_engine.py:92,239) and sticky device errors (synchronises). */
 SB_API int sb_stats(sb_engine* e, void* stream, sb_stats_t* out);
 

@@ -29,6 +29,13 @@ int fail(int code, const std::string& msg) {
   return code;
 }
 
+}  // namespace
+
+// Error recording for entry points defined in other translation units.
+int sb::record_error(int code, const char* msg) { return fail(code, msg); }
+
+namespace {
+
 #define SB_CUDA(call)                                                                  \
   do {                                                                                 \
     cudaError_t e_ = (call);                                                           \

@@ -117,6 +117,9 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
 cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, int grid_x, cudaStream_t s);
 int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s);
 
+// Sets the message sb_last_error() returns on this thread; returns `code`.
+int record_error(int code, const char* msg);
+
 // fp32 CUDA-core path
 cudaError_t launch_conv_simt(const ConvArgs& a, int grid_x, cudaStream_t s);
 
