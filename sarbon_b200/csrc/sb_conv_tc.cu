@@ -67,17 +67,17 @@ struct TcCfg {
   static constexpr int W_BYTES = NWKB * B_KB;
   static constexpr int TMEM_COLS = (2 * NCTA) <= 32 ? 32 : (2 * NCTA) <= 64 ? 64 : (2 * NCTA) <= 128 ? 128 : (2 * NCTA) <= 256 ? 256 : 512;
   // roles: warps 0-7 epilogue (two per TMEM lane quadrant, half the columns each),
-  // warp 8 TMA producer, warp 9 MMA issuer + TMEM owner, warps 10-13 first-layer gather
+  // warp 8 TMA producer, warps 9-10 MMA issuers (warp 9 owns TMEM), warps 11-14 first-layer gather
   static constexpr int EPI_THREADS = 256;
   static constexpr int NCOL = NCTA / 2;               // accumulator columns per epilogue warp
-  static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 320;
-  static constexpr int THREADS = MANUAL ? 448 : 320;
+  static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 352;  // MMA issuers: warps 9, 10
+  static constexpr int THREADS = MANUAL ? 480 : 352;
   static constexpr int W_OFF = 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
   static constexpr int BIAS_BYTES = 256 * 4;          // every output channel (C_out <= 256)
   static constexpr int CRING = 16;                    // item-coordinate ring (producer -> epilogue)
   static constexpr int CRING_BYTES = CRING * 8 * 4 * 4; // <= 8 units x (cam, row, col, pad) per item
-  static constexpr int BAR_BYTES = 768;
+  static constexpr int BAR_BYTES = 1024;
   // first layer: the input window of one M-tile (BOX_ROWS output rows of one tile), loaded
   // by one 3-D TMA box from the image cache viewed as [N][H][W*CIN]; the box starts 8
   // elements (16 B) before the window's first element... rounded so x stays 16-byte aligned
@@ -90,7 +90,12 @@ struct TcCfg {
   static constexpr int WIN_BYTES = MANUAL ? NWB * WIN_BUF : 0;
   static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
-  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+  static constexpr int STAGES = STAGES_FIT > 24 ? 24 : STAGES_FIT;
+  // MMA issuers: two (alternate items, one accumulator each) when the ring holds two items'
+  // K-blocks; each issuer then owns a sub-ring of SUB stages that the producer fills in
+  // item order, so every stage has one in-order consumer and the phase parities stay exact
+  static constexpr int NISS = STAGES >= 2 * NKB ? 2 : 1;
+  static constexpr int SUB = STAGES / NISS;
   static constexpr int SMEM = FIXED + A_OFF + STAGES * A_STAGE;
   static constexpr uint32_t IDESC = idesc_f16(128, NCTA);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
@@ -134,14 +139,24 @@ SB_DEV TileXY tile_at(const ConvArgs& a, int mode, int listed, int i) {
   return r;
 }
 
-// Work item -> (C_out slice, M-tile).  Items are ordered slice-major, so a persistent CTA
-// changes slice (and reloads its weights) at most nsplit-1 times.
+// Work item -> (C_out slice, M-tile).  A CTA keeps one C_out slice for the whole launch
+// (slice = CTA index mod nsplit; the grid is a multiple of nsplit), so its weights are
+// loaded once, and strides over the M-tiles with the gridDim/nsplit CTAs of its slice.
 struct Item {
   int split, m;
 };
-SB_DEV Item item_at(int it, int n_mtiles) {
-  const int item = (int)blockIdx.x + it * (int)gridDim.x;
-  return Item{item / n_mtiles, item % n_mtiles};
+SB_DEV Item item_at(int it, int nsplit) {
+  return Item{(int)blockIdx.x % nsplit, (int)blockIdx.x / nsplit + it * ((int)gridDim.x / nsplit)};
+}
+
+// Stage and phase of K-block kb of item it: item it belongs to issuer it % NISS, whose
+// sub-ring holds stages [u*SUB, (u+1)*SUB) used in the order of that issuer's K-blocks.
+template <class C>
+SB_DEV void stage_of(int it, int kb, uint32_t& s, uint32_t& ph) {
+  const uint32_t u = C::NISS == 2 ? (uint32_t)(it & 1) : 0u;
+  const uint32_t gu = (uint32_t)(C::NISS == 2 ? (it >> 1) : it) * C::NKB + (uint32_t)kb;
+  s = u * C::SUB + gu % C::SUB;
+  ph = (gu / C::SUB) & 1u;
 }
 
 template <int CIN, int NCTA, int T, int S, int WIN>
@@ -159,9 +174,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
   uint64_t* accf = bars + 2 * C::STAGES;
   uint64_t* acce = accf + 2;
   uint64_t* wfull = acce + 2;
-  uint64_t* wempty = wfull + 1;
-  uint64_t* dbar = wempty + 1;
-  uint64_t* winfull = dbar + 1;          // first-layer window ring
+  uint64_t* dbar = wfull + 1;            // [2]: drain of each MMA issuer
+  uint64_t* winfull = dbar + 2;          // first-layer window ring
   uint64_t* winempty = winfull + C::NWB;
   uint64_t* cfull = winempty + C::NWB;   // item-coordinate ring
   uint64_t* cempty = cfull + C::CRING;
@@ -182,8 +196,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
       mbar_init(&acce[i], C::EPI_THREADS);
     }
     mbar_init(wfull, 1);
-    mbar_init(wempty, 1);
-    mbar_init(dbar, 1);
+    mbar_init(&dbar[0], 1);
+    mbar_init(&dbar[1], 1);
     for (int i = 0; i < C::NWB; ++i) {
       mbar_init(&winfull[i], 1);
       mbar_init(&winempty[i], 128);
@@ -216,23 +230,23 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
   else if (mode == SB_MODE_SPARSE) n_tiles = a.st->force_tiles > 0 ? a.st->force_tiles : listed;
   if (n_tiles > n_units) n_tiles = n_units;
   const int n_mtiles = (!WIN && C::TT >= 128) ? n_tiles * C::MPT : (n_tiles + C::TPM - 1) / C::TPM;
-  const int n_items = n_mtiles * (a.cout / NCTA);
-  const int my_items = (int)blockIdx.x < n_items ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nsplit = a.cout / NCTA;
+  const int m_first = (int)blockIdx.x / nsplit, m_stride = (int)gridDim.x / nsplit;
+  const int my_items = m_first < n_mtiles ? (n_mtiles - 1 - m_first) / m_stride + 1 : 0;
 
   if (my_items > 0) {
     if (warp == C::PROD_WARP) {
-      // ------------------------------------------------ producer: weights per C_out slice, A stages
+      // ------------------------------------------------ producer: the slice's weights, A stages
       // The whole warp runs the loop (warp-uniform control flow); lane 0 issues the copies.
       // Tile coordinates are fetched one item ahead into the other of two register sets
       // (the loop is unrolled by two, so no set is ever copied while its loads are in flight).
       const bool leader = lane == 0;
       uint32_t g = 0, nload = 0;
-      int cur = -1;
       struct Coords {
         int cam[C::TPM], y0[C::TPM], x0[C::TPM], uy[C::TPM], ux[C::TPM];
       };
       auto fetch = [&](int it, Coords& o) {
-        const Item w = item_at(it, n_mtiles);
+        const Item w = item_at(it, nsplit);
 #pragma unroll
         for (int j = 0; j < C::TPM; ++j) {
           int ti, sub;
@@ -248,7 +262,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
       };
       // returns false when the pipeline was aborted
       auto issue = [&](int it, const Coords& cc) -> bool {
-        const Item w = item_at(it, n_mtiles);
+        const Item w = item_at(it, nsplit);
         // publish this item's unit coordinates for the epilogue
         {
           const int slot = it % C::CRING;
@@ -264,12 +278,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           }
           __syncwarp();
         }
-        if (w.split != cur) {
-          if (nload > 0 && !warp_wait(wempty, (nload - 1) & 1u, abort_flag)) {
-            atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
-            *abort_flag = 1;
-            return false;
-          }
+        if (nload == 0) {  // the CTA's C_out slice never changes: weights are loaded once
           const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)w.split * C::W_BYTES;
           if (leader) {
             mbar_arrive_expect_tx(wfull, C::W_BYTES);
@@ -280,7 +289,6 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           }
           __syncwarp();
           ++nload;
-          cur = w.split;
         }
         if (C::MANUAL) {
           // first layer: one window box per item into the ring
@@ -305,8 +313,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           // full window: K-block = chunk, the box covers all taps
           const int tap = WIN == 3 ? 0 : WIN ? (kb / C::NCH) * 3 : kb / C::NCH, ch = kb % C::NCH;
           const int ky = tap / 3, kx = WIN ? 0 : tap % 3;
-          const int s = g % C::STAGES;
-          const uint32_t ph = (g / C::STAGES) & 1u;
+          uint32_t s, ph;
+          stage_of<C>(it, kb, s, ph);
           if (!warp_wait(&empty[s], ph ^ 1u, abort_flag)) {
             atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
             *abort_flag = 1;
@@ -338,10 +346,15 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         const uint32_t first = g > (uint32_t)C::NWB ? g - C::NWB : 0u;
         for (uint32_t q = first; q < g; ++q) warp_wait(&winfull[q % C::NWB], (q / C::NWB) & 1u, &never);
       } else {
-        const uint32_t first = g > (uint32_t)C::STAGES ? g - C::STAGES : 0u;
-        for (uint32_t q = first; q < g; ++q) warp_wait(&full[q % C::STAGES], (q / C::STAGES) & 1u, &never);
+        // the last fill of every stage of each sub-ring (earlier fills were consumed)
+        for (int u = 0; u < C::NISS; ++u) {
+          const uint32_t uses = (uint32_t)((my_items - u + C::NISS - 1) / C::NISS) * C::NKB;
+          const uint32_t first = uses > (uint32_t)C::SUB ? uses - C::SUB : 0u;
+          for (uint32_t q = first; q < uses; ++q)
+            warp_wait(&full[u * C::SUB + q % C::SUB], (q / C::SUB) & 1u, &never);
+        }
       }
-      if (nload > 0) warp_wait(wfull, (nload - 1) & 1u, &never);
+      if (nload > 0) warp_wait(wfull, 0, &never);
     } else if (C::MANUAL && (int)threadIdx.x >= C::GATHER0) {
       // ------------------------------------------------ gather producers (first layer)
       // Each thread builds one A row (one output pixel: 3x3 taps x channels, zero-padded to
@@ -356,8 +369,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           *abort_flag = 1;
           break;
         }
-        const int s = g % C::STAGES;
-        const uint32_t ph = (g / C::STAGES) & 1u;
+        uint32_t s, ph;
+        stage_of<C>(it, 0, s, ph);
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
@@ -393,87 +406,88 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         mbar_arrive(&full[s]);
         mbar_arrive(&winempty[b]);
       }
-    } else if (warp == C::MMA_WARP) {
-      // ------------------------------------------------ MMA issuer
-      // The whole warp runs the loop; lane 0 issues tcgen05.mma / tcgen05.commit.
-      const bool leader = lane == 0;
-      uint32_t g = 0, nload = 0;
-      int cur = -1;
-      bool ok = true;
-      for (int it = 0; ok && it < my_items; ++it) {
-        const Item w = item_at(it, n_mtiles);
-        if (w.split != cur) {
-          if (nload > 0 && leader) mma_commit(wempty);  // old weights free once the issued MMAs are done
-          if (!warp_wait(wfull, nload & 1u, abort_flag)) {
-            atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
-            *abort_flag = 1;
-            break;
-          }
-          ++nload;
-          cur = w.split;
-        }
-        const int ab = it & 1;
-        if (!warp_wait(&acce[ab], ((it >> 1) & 1) ^ 1, abort_flag)) {
-          atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
+    } else if (warp == C::MMA_WARP || warp == C::MMA_WARP + 1) {
+      // ------------------------------------------------ MMA issuers
+      // With NISS = 2, lane 0 of warp 9 issues the MMAs of the even items into accumulator
+      // 0 and lane 0 of warp 10 those of the odd items into accumulator 1 (NISS = 1: warp 9
+      // issues every item, alternating accumulators).  tcgen05.mma issue is
+      // back-pressured by the tensor pipe and an N <= 96 MMA takes ~48 cycles, so the
+      // instruction queue holds little work; an mbarrier wait of the issuing thread (its
+      // shared-memory access queues behind the MMAs' operand reads) would let the pipe run
+      // dry.  With two issuers one keeps the pipe fed while the other waits.  The K-block
+      // loop is unrolled and both descriptors advance by compile-time offsets (which cannot
+      // carry out of the 14-bit start-address field: shared memory < 256 KB).
+      const int u = warp - C::MMA_WARP;
+      if (lane == 0 && u < C::NISS) {
+        const uint64_t a_desc0 = smem_desc(smem_u32(sA), WIN ? C::WSBO : C::SBO, C::SWZ);
+        const uint64_t b_desc0 = smem_desc(smem_u32(sW), C::SBO, C::SWZ);
+        constexpr uint32_t ASTEP = C::A_STAGE >> 4;
+        bool ok = true;
+        if (u < my_items && !mbar_wait(wfull, 0, abort_flag)) {  // this CTA's C_out slice
+          atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
           *abort_flag = 1;
-          break;
+          ok = false;
         }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ab * NCTA;
-        for (int kb = 0; kb < C::NKB; ++kb, ++g) {
-          const int s = g % C::STAGES;
-          if (!warp_wait(&full[s], (g / C::STAGES) & 1u, abort_flag)) {
-            atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+        for (int it = u; ok && it < my_items; it += C::NISS) {
+          const int ab = it & 1;
+          if (!mbar_wait(&acce[ab], ((it >> 1) & 1) ^ 1, abort_flag)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
             *abort_flag = 1;
-            ok = false;
             break;
           }
           tc_fence_after();
-          if (leader) {
-            const uint32_t a_addr = smem_u32(sA + s * C::A_STAGE);
+          const uint32_t d_tmem = tmem_base + ab * NCTA;
+          uint32_t s, ph;
+          stage_of<C>(it, 0, s, ph);
+          const uint32_t s_end = (uint32_t)u * C::SUB + C::SUB;  // one past this sub-ring
+#pragma unroll
+          for (int kb = 0; kb < C::NKB; ++kb) {
+            if (!mbar_wait(&full[s], ph, abort_flag)) {
+              atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t a_desc = a_desc0 + s * ASTEP;
             if (WIN) {
               // window taps: A = the window shifted by (ky*10 + kx) pixels (128 B rows; the
               // hardware swizzle follows absolute smem addresses), B = that tap's weights.
               // Row windows hold one ky per K-block, full windows all three.
-              const int ch = kb % C::NCH;
-              const int ky0 = WIN == 3 ? 0 : kb / C::NCH, nky = WIN == 3 ? 3 : 1;
+              constexpr int NKY = WIN == 3 ? 3 : 1;
+              const int ch = kb % C::NCH, ky0 = WIN == 3 ? 0 : kb / C::NCH;
 #pragma unroll
-              for (int dy = 0; dy < nky; ++dy) {
-                const int ky = ky0 + dy;
+              for (int dy = 0; dy < NKY; ++dy)
 #pragma unroll
-                for (int kx = 0; kx < 3; ++kx) {
-                  const uint32_t b_addr = smem_u32(sW + ((ky * 3 + kx) * C::NCH + ch) * C::B_KB);
-                  const uint32_t off = ((WIN == 3 ? ky * 10 : 0) + kx) * C::ROWB;
+                for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
                   for (int kk = 0; kk < C::CH / 16; ++kk) {
-                    const uint64_t ad = smem_desc(a_addr + off + kk * 32, C::WSBO, C::SWZ);
-                    const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
-                    mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | dy | kx | kk) != 0 ? 1u : 0u);
+                    const uint32_t a_off = ((WIN == 3 ? dy * 10 : 0) + kx) * C::ROWB + kk * 32;
+                    const uint32_t b_off = (((ky0 + dy) * 3 + kx) * C::NCH + ch) * C::B_KB + kk * 32;
+                    mma_f16_ss(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
+                               (kb | dy | kx | kk) != 0 ? 1u : 0u);
                   }
-                }
-              }
             } else {
-              const uint32_t b_addr = smem_u32(sW + kb * C::B_KB);
 #pragma unroll
-              for (int kk = 0; kk < C::CH / 16; ++kk) {
-                const uint64_t ad = smem_desc(a_addr + kk * 32, C::SBO, C::SWZ);
-                const uint64_t bd = smem_desc(b_addr + kk * 32, C::SBO, C::SWZ);
-                mma_f16_ss(d_tmem, ad, bd, C::IDESC, (kb | kk) != 0 ? 1u : 0u);
-              }
+              for (int kk = 0; kk < C::CH / 16; ++kk)
+                mma_f16_ss(d_tmem, a_desc + ((kk * 32) >> 4), b_desc0 + ((kb * C::B_KB + kk * 32) >> 4), C::IDESC,
+                           (kb | kk) != 0 ? 1u : 0u);
             }
             mma_commit(&empty[s]);  // stage free once these MMAs have read it
+            if (++s == s_end) {
+              s = s_end - C::SUB;
+              ph ^= 1u;
+            }
           }
-          __syncwarp();
+          if (!ok) break;
+          mma_commit(&accf[ab]);  // accumulator ready for the epilogue
         }
-        if (!ok) break;
-        if (leader) mma_commit(&accf[ab]);  // accumulator ready for the epilogue
-        __syncwarp();
+        // drain: all MMAs this thread issued complete before TMEM is released
+        mma_commit(&dbar[u]);
+        volatile int never = 0;
+        mbar_wait(&dbar[u], 0, &never);
       }
-      // drain: all issued MMAs complete before TMEM is released
-      if (leader) mma_commit(dbar);
       __syncwarp();
-      volatile int never = 0;
-      warp_wait(dbar, 0, &never);
     } else if (warp < 8) {
       // ------------------------------------------------ epilogue: TMEM -> bias/res/ReLU -> cache
       // Warp w reads TMEM lanes 32*(w%4).. (its accumulator rows) and columns
@@ -493,7 +507,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
       // unit coordinates come from the producer through the shared-memory ring, so the
       // residual prefetch below depends on no global load
       auto fetch = [&](int it, Row& o) -> bool {
-        const Item w = item_at(it, n_mtiles);
+        const Item w = item_at(it, nsplit);
         o.n0 = w.split * NCTA + col0;
         int ti, p, j;
         if (WIN) { j = r / C::RPX; ti = w.m * C::TPM + j; p = r % C::RPX; }
@@ -781,7 +795,12 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, v->fn, v->threads, v->smem) != cudaSuccess || o < 1) o = 1;
     occ[idx] = o;
   }
-  dim3 grid(grid_x * occ[idx], 1);  // C_out slices are work items of the persistent loop
+  // each CTA keeps one C_out slice: the grid is a multiple of the number of slices
+  const int nsplit = a.cout / v->ncta;
+  int gx = grid_x * occ[idx];
+  gx -= gx % nsplit;
+  if (gx < nsplit) gx = nsplit;
+  dim3 grid(gx, 1);
   CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));
   v->fn<<<grid, v->threads, v->smem, st>>>(a, map ? *map : dummy);
