@@ -40,7 +40,10 @@ constexpr int kMaxSmem = 232448;  // 227 KB opt-in shared memory per CTA on sm_1
 //          feeds the three kx taps;
 // WIN = 3: full windows -- regions of 8/T x 16/T blocks (8 px x 16 rows), one 10 x 18 px box
 //          per chunk feeds all nine taps.  Both window modes are for stride-1 layers.
-template <int CIN, int NCTA, int T, int S, int WIN>
+// PAIR = 1: a 2-CTA cluster runs M=256 cta_group::2 MMAs; each CTA holds NCTA of the
+//           2*NCTA output channels as its half of B and all 2*NCTA accumulator columns of
+//           its own 128 pixels.
+template <int CIN, int NCTA, int T, int S, int WIN, int PAIR = 0>
 struct TcCfg {
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
@@ -65,11 +68,12 @@ struct TcCfg {
   static constexpr int A_STAGE = ((A_BYTES + 1023) / 1024) * 1024;     // stage stride (1024-aligned)
   static constexpr int B_KB = NCTA * ROWB;
   static constexpr int W_BYTES = NWKB * B_KB;
-  static constexpr int TMEM_COLS = (2 * NCTA) <= 32 ? 32 : (2 * NCTA) <= 64 ? 64 : (2 * NCTA) <= 128 ? 128 : (2 * NCTA) <= 256 ? 256 : 512;
+  static constexpr int NMMA = PAIR ? 2 * NCTA : NCTA;  // MMA N = accumulator columns per CTA
+  static constexpr int TMEM_COLS = (2 * NMMA) <= 32 ? 32 : (2 * NMMA) <= 64 ? 64 : (2 * NMMA) <= 128 ? 128 : (2 * NMMA) <= 256 ? 256 : 512;
   // roles: warps 0-7 epilogue (two per TMEM lane quadrant, half the columns each),
   // warp 8 TMA producer, warps 9-10 MMA issuers (warp 9 owns TMEM), warps 11-14 first-layer gather
   static constexpr int EPI_THREADS = 256;
-  static constexpr int NCOL = NCTA / 2;               // accumulator columns per epilogue warp
+  static constexpr int NCOL = NMMA / 2;               // accumulator columns per epilogue warp
   static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 352;  // MMA issuers: warps 9, 10
   static constexpr int THREADS = MANUAL ? 480 : 352;
   static constexpr int W_OFF = 0;
@@ -97,10 +101,11 @@ struct TcCfg {
   static constexpr int NISS = STAGES >= 2 * NKB ? 2 : 1;
   static constexpr int SUB = STAGES / NISS;
   static constexpr int SMEM = FIXED + A_OFF + STAGES * A_STAGE;
-  static constexpr uint32_t IDESC = idesc_f16(128, NCTA);
+  static constexpr uint32_t IDESC = idesc_f16(PAIR ? 256 : 128, NMMA);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(TPM <= 8, "coordinate ring holds up to 8 units per item");
-  static_assert(NCTA % 32 == 0 && NCTA >= 32 && NCTA <= 256, "UMMA N / epilogue split");
+  static_assert(NCTA % 32 == 0 && NCTA >= 32 && NMMA <= 256, "UMMA N / epilogue split");
+  static_assert(!PAIR || !MANUAL, "CTA pairs need TMA-loaded A stages");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
   static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256), "first-layer window box");
@@ -159,10 +164,10 @@ SB_DEV void stage_of(int it, int kb, uint32_t& s, uint32_t& ph) {
   ph = (gu / C::SUB) & 1u;
 }
 
-template <int CIN, int NCTA, int T, int S, int WIN>
-__global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
+template <int CIN, int NCTA, int T, int S, int WIN, int PAIR>
+__global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
     conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmap) {
-  using C = TcCfg<CIN, NCTA, T, S, WIN>;
+  using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem + C::W_OFF;
@@ -175,7 +180,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
   uint64_t* acce = accf + 2;
   uint64_t* wfull = acce + 2;
   uint64_t* dbar = wfull + 1;            // [2]: drain of each MMA issuer
-  uint64_t* winfull = dbar + 2;          // first-layer window ring
+  uint64_t* wpeer = dbar + 2;            // pairs: the odd CTA's weights have landed
+  uint64_t* winfull = dbar + 3;          // first-layer window ring
   uint64_t* winempty = winfull + C::NWB;
   uint64_t* cfull = winempty + C::NWB;   // item-coordinate ring
   uint64_t* cempty = cfull + C::CRING;
@@ -193,11 +199,12 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], C::EPI_THREADS);
+      mbar_init(&acce[i], PAIR ? 16 : C::EPI_THREADS);  // pairs: one arrival per epilogue warp of both CTAs
     }
     mbar_init(wfull, 1);
     mbar_init(&dbar[0], 1);
     mbar_init(&dbar[1], 1);
+    mbar_init(wpeer, 1);
     for (int i = 0; i < C::NWB; ++i) {
       mbar_init(&winfull[i], 1);
       mbar_init(&winempty[i], 128);
@@ -210,15 +217,22 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
     fence_mbar_init();
   }
   if (warp == C::MMA_WARP) {
-    tmem_alloc(tmem_holder, C::TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc2(tmem_holder, C::TMEM_COLS);  // the same columns on both SMs of the pair
+      tmem_relinquish2();
+    } else {
+      tmem_alloc(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   for (int i = threadIdx.x; i < a.cout; i += blockDim.x) sBias[i] = a.bias[i];
   if (!C::MANUAL && warp == C::PROD_WARP && lane == 0) prefetch_tmap(&tmap);
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync();  // the leader's barriers are initialised before the odd CTA uses them
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
 
   // work of this launch, decided on the device (no host sync)
   const int mode = a.st->mode_cur;
@@ -230,9 +244,21 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
   else if (mode == SB_MODE_SPARSE) n_tiles = a.st->force_tiles > 0 ? a.st->force_tiles : listed;
   if (n_tiles > n_units) n_tiles = n_units;
   const int n_mtiles = (!WIN && C::TT >= 128) ? n_tiles * C::MPT : (n_tiles + C::TPM - 1) / C::TPM;
-  const int nsplit = a.cout / NCTA;
-  const int m_first = (int)blockIdx.x / nsplit, m_stride = (int)gridDim.x / nsplit;
-  const int my_items = m_first < n_mtiles ? (n_mtiles - 1 - m_first) / m_stride + 1 : 0;
+  const int nsplit = PAIR ? 1 : a.cout / NCTA;
+  // pairs: cluster p runs M-tiles 2q, 2q+1 (q = p, p + npairs, ...); CTA rank r takes 2q+r
+  const int npairs = (int)gridDim.x / 2, pair = (int)blockIdx.x / 2;
+  int my_items;
+  if (PAIR) {
+    const int pm = (n_mtiles + 1) / 2;
+    my_items = pair < pm ? (pm - 1 - pair) / npairs + 1 : 0;
+  } else {
+    const int m_first = (int)blockIdx.x / nsplit, m_stride = (int)gridDim.x / nsplit;
+    my_items = m_first < n_mtiles ? (n_mtiles - 1 - m_first) / m_stride + 1 : 0;
+  }
+  auto item_of = [&](int it) -> Item {
+    if (PAIR) return Item{(int)rank, 2 * (pair + it * npairs) + (int)rank};
+    return item_at(it, nsplit);
+  };
 
   if (my_items > 0) {
     if (warp == C::PROD_WARP) {
@@ -246,7 +272,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         int cam[C::TPM], y0[C::TPM], x0[C::TPM], uy[C::TPM], ux[C::TPM];
       };
       auto fetch = [&](int it, Coords& o) {
-        const Item w = item_at(it, nsplit);
+        const Item w = item_of(it);
 #pragma unroll
         for (int j = 0; j < C::TPM; ++j) {
           int ti, sub;
@@ -262,7 +288,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
       };
       // returns false when the pipeline was aborted
       auto issue = [&](int it, const Coords& cc) -> bool {
-        const Item w = item_at(it, nsplit);
+        const Item w = item_of(it);
         // publish this item's unit coordinates for the epilogue
         {
           const int slot = it % C::CRING;
@@ -289,6 +315,15 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
           }
           __syncwarp();
           ++nload;
+          if (PAIR && rank == 1) {  // tell the leader that this CTA's half of B is resident
+            if (!warp_wait(wfull, 0, abort_flag)) {
+              atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
+              *abort_flag = 1;
+              return false;
+            }
+            if (leader) mbar_arrive_cluster(mapa_shared(smem_u32(wpeer), 0));
+            __syncwarp();
+          }
         }
         if (C::MANUAL) {
           // first layer: one window box per item into the ring
@@ -321,12 +356,22 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
             return false;
           }
           if (leader) {
-            mbar_arrive_expect_tx(&full[s], C::A_BYTES);
             uint8_t* dst = sA + s * C::A_STAGE;
+            if (PAIR) {
+              // both CTAs' boxes complete on the leader's barrier; the leader expects both
+              const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+              if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
 #pragma unroll
-            for (int j = 0; j < C::TPM; ++j)
-              tma_load_4d(dst + j * C::BOX_BYTES, &tmap, &full[s], ch * C::CH, cc.x0[j] + kx, cc.y0[j] + ky,
-                          cc.cam[j]);
+              for (int j = 0; j < C::TPM; ++j)
+                tma_load_4d_pair(dst + j * C::BOX_BYTES, &tmap, fb, ch * C::CH, cc.x0[j] + kx, cc.y0[j] + ky,
+                                 cc.cam[j]);
+            } else {
+              mbar_arrive_expect_tx(&full[s], C::A_BYTES);
+#pragma unroll
+              for (int j = 0; j < C::TPM; ++j)
+                tma_load_4d(dst + j * C::BOX_BYTES, &tmap, &full[s], ch * C::CH, cc.x0[j] + kx, cc.y0[j] + ky,
+                            cc.cam[j]);
+            }
           }
           __syncwarp();
         }
@@ -346,12 +391,16 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         const uint32_t first = g > (uint32_t)C::NWB ? g - C::NWB : 0u;
         for (uint32_t q = first; q < g; ++q) warp_wait(&winfull[q % C::NWB], (q / C::NWB) & 1u, &never);
       } else {
-        // the last fill of every stage of each sub-ring (earlier fills were consumed)
+        // the last fill of every stage of each sub-ring (earlier fills were consumed); the
+        // odd CTA of a pair has no full barriers of its own: it waits until the leader's
+        // MMAs have released its last stages (no copy or commit into it is then pending)
         for (int u = 0; u < C::NISS; ++u) {
           const uint32_t uses = (uint32_t)((my_items - u + C::NISS - 1) / C::NISS) * C::NKB;
           const uint32_t first = uses > (uint32_t)C::SUB ? uses - C::SUB : 0u;
-          for (uint32_t q = first; q < uses; ++q)
-            warp_wait(&full[u * C::SUB + q % C::SUB], (q / C::SUB) & 1u, &never);
+          for (uint32_t q = first; q < uses; ++q) {
+            uint64_t* b = (PAIR && rank == 1) ? &empty[u * C::SUB + q % C::SUB] : &full[u * C::SUB + q % C::SUB];
+            warp_wait(b, (q / C::SUB) & 1u, &never);
+          }
         }
       }
       if (nload > 0) warp_wait(wfull, 0, &never);
@@ -418,12 +467,13 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
       // loop is unrolled and both descriptors advance by compile-time offsets (which cannot
       // carry out of the 14-bit start-address field: shared memory < 256 KB).
       const int u = warp - C::MMA_WARP;
-      if (lane == 0 && u < C::NISS) {
+      if (lane == 0 && u < C::NISS && rank == 0) {  // pairs: only the even CTA issues
         const uint64_t a_desc0 = smem_desc(smem_u32(sA), WIN ? C::WSBO : C::SBO, C::SWZ);
         const uint64_t b_desc0 = smem_desc(smem_u32(sW), C::SBO, C::SWZ);
         constexpr uint32_t ASTEP = C::A_STAGE >> 4;
         bool ok = true;
-        if (u < my_items && !mbar_wait(wfull, 0, abort_flag)) {  // this CTA's C_out slice
+        if (u < my_items && (!mbar_wait(wfull, 0, abort_flag) ||        // this CTA's C_out slice
+                             (PAIR && !mbar_wait(wpeer, 0, abort_flag)))) {  // and the odd CTA's
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
           *abort_flag = 1;
           ok = false;
@@ -436,7 +486,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem_base + ab * NCTA;
+          const uint32_t d_tmem = tmem_base + ab * C::NMMA;
           uint32_t s, ph;
           stage_of<C>(it, 0, s, ph);
           const uint32_t s_end = (uint32_t)u * C::SUB + C::SUB;  // one past this sub-ring
@@ -464,26 +514,44 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
                   for (int kk = 0; kk < C::CH / 16; ++kk) {
                     const uint32_t a_off = ((WIN == 3 ? dy * 10 : 0) + kx) * C::ROWB + kk * 32;
                     const uint32_t b_off = (((ky0 + dy) * 3 + kx) * C::NCH + ch) * C::B_KB + kk * 32;
-                    mma_f16_ss(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
-                               (kb | dy | kx | kk) != 0 ? 1u : 0u);
+                    if (PAIR)
+                      mma_f16_ss2(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
+                                  (kb | dy | kx | kk) != 0 ? 1u : 0u);
+                    else
+                      mma_f16_ss(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
+                                 (kb | dy | kx | kk) != 0 ? 1u : 0u);
                   }
             } else {
 #pragma unroll
-              for (int kk = 0; kk < C::CH / 16; ++kk)
-                mma_f16_ss(d_tmem, a_desc + ((kk * 32) >> 4), b_desc0 + ((kb * C::B_KB + kk * 32) >> 4), C::IDESC,
-                           (kb | kk) != 0 ? 1u : 0u);
+              for (int kk = 0; kk < C::CH / 16; ++kk) {
+                if (PAIR)
+                  mma_f16_ss2(d_tmem, a_desc + ((kk * 32) >> 4), b_desc0 + ((kb * C::B_KB + kk * 32) >> 4),
+                              C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+                else
+                  mma_f16_ss(d_tmem, a_desc + ((kk * 32) >> 4), b_desc0 + ((kb * C::B_KB + kk * 32) >> 4),
+                             C::IDESC, (kb | kk) != 0 ? 1u : 0u);
+              }
             }
-            mma_commit(&empty[s]);  // stage free once these MMAs have read it
+            if (PAIR) {
+              mma_commit2_both(&empty[s]);  // the stage is free in both CTAs once read
+            } else {
+              mma_commit(&empty[s]);  // stage free once these MMAs have read it
+            }
             if (++s == s_end) {
               s = s_end - C::SUB;
               ph ^= 1u;
             }
           }
           if (!ok) break;
-          mma_commit(&accf[ab]);  // accumulator ready for the epilogue
+          if (PAIR) {
+            mma_commit2_both(&accf[ab]);  // both CTAs' accumulators are ready
+          } else {
+            mma_commit(&accf[ab]);  // accumulator ready for the epilogue
+          }
         }
         // drain: all MMAs this thread issued complete before TMEM is released
-        mma_commit(&dbar[u]);
+        if (PAIR) mma_commit2(smem_u32(&dbar[u]));
+        else mma_commit(&dbar[u]);
         volatile int never = 0;
         mbar_wait(&dbar[u], 0, &never);
       }
@@ -508,7 +576,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
       // residual prefetch below depends on no global load
       auto fetch = [&](int it, Row& o) -> bool {
         const Item w = item_at(it, nsplit);
-        o.n0 = w.split * NCTA + col0;
+        o.n0 = PAIR ? col0 : w.split * NCTA + col0;
         int ti, p, j;
         if (WIN) { j = r / C::RPX; ti = w.m * C::TPM + j; p = r % C::RPX; }
         else if (C::TT >= 128) { j = 0; ti = w.m / C::MPT; p = (w.m % C::MPT) * 128 + r; }
@@ -549,13 +617,18 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
         if (__any_sync(0xFFFFFFFFu, !got || *abort_flag != 0)) return false;
         tc_fence_after();
         uint32_t v[C::NCOL];
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + ab * NCTA + col0;
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + ab * C::NMMA + col0;
 #pragma unroll
         for (int j = 0; j < C::NCOL / 16; ++j)
           tmem_ld16(taddr + j * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[j * 16]));
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&acce[ab]);  // the MMA may overwrite this buffer now
+        if (PAIR) {  // one arrival per warp on the leader's barrier
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[ab]), 0));
+        } else {
+          mbar_arrive(&acce[ab]);  // the MMA may overwrite this buffer now
+        }
         if (it + 1 < my_items && !fetch(it + 1, nx)) {
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
           *abort_flag = 1;
@@ -601,89 +674,118 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN>::THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // both CTAs are done with TMEM and with each other's barriers
   if (warp == C::MMA_WARP) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if (PAIR) tmem_dealloc2(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (PAIR) cluster_sync();  // neither CTA exits while the other may still address it
 }
 
 // ---------------------------------------------------------------- host side
 namespace {
 
 struct Variant {
-  int cin, cout, t, s, win, ncta;
+  int cin, cout, t, s, win, ncta, pair;
   void (*fn)(const ConvArgs, const CUtensorMap);
   int smem, threads, w_bytes, ch, box_rows, win_cols, win_rows;
+  int mode() const { return win | (pair << 3); }
 };
 
-template <int CIN, int NCTA, int T, int S, int WIN = 0>
+template <int CIN, int NCTA, int T, int S, int WIN = 0, int PAIR = 0>
 Variant make_variant(int cout) {
-  using C = TcCfg<CIN, NCTA, T, S, WIN>;
-  return Variant{CIN, cout, T, S, WIN, NCTA, conv_tc_kernel<CIN, NCTA, T, S, WIN>, C::SMEM, C::THREADS, C::W_BYTES,
-                 C::CH, C::BOX_ROWS, C::WIN_COLS, C::WIN_ROWS};
+  using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
+  return Variant{CIN,       cout,       T,         S,         WIN,       NCTA,      PAIR,
+                 conv_tc_kernel<CIN, NCTA, T, S, WIN, PAIR>,  C::SMEM,   C::THREADS, C::W_BYTES,
+                 C::CH,     C::BOX_ROWS, C::WIN_COLS, C::WIN_ROWS};
 }
 
-// Sarbon stem shapes (widths 32/64/128, Res blocks) at block 32 and block 64.
+// Sarbon stem shapes (widths 32/64/128, Res blocks) at block 32 and block 64.  The first
+// variant of a shape is its default.
 const std::vector<Variant>& variants() {
   static const std::vector<Variant> v = {
       // block 32
       make_variant<3, 32, 16, 2>(32),
       make_variant<32, 64, 8, 2>(64),
-      make_variant<64, 64, 8, 1, 1>(64),    // row windows over blocks
-      make_variant<64, 64, 8, 1, 3>(64),    // full windows over 1x2-block regions
+      make_variant<64, 64, 8, 1, 1>(64),       // row windows over blocks
+      make_variant<64, 64, 8, 1, 3>(64),       // full windows over 1x2-block regions
+      make_variant<64, 64, 4, 2, 0, 1>(128),   // CTA pairs: M=256, N=128
       make_variant<64, 128, 4, 2>(128),
-      make_variant<128, 64, 4, 1, 1>(128),  // row windows over horizontal block pairs; two C_out slices
-      make_variant<128, 64, 4, 1, 3>(128),  // full windows over 2x4-block regions
+      make_variant<128, 64, 4, 1, 1, 1>(128),  // CTA pairs, row windows over horizontal block pairs
+      make_variant<128, 64, 4, 1, 1>(128),     // row windows, two C_out slices
+      make_variant<128, 64, 4, 1, 3, 1>(128),  // CTA pairs, full windows over 2x4-block regions
+      make_variant<128, 64, 4, 1, 3>(128),     // full windows, two C_out slices
       // block 64
       make_variant<3, 32, 32, 2>(32),
       make_variant<32, 64, 16, 2>(64),
       make_variant<64, 64, 16, 1>(64),
+      make_variant<64, 64, 8, 2, 0, 1>(128),
       make_variant<64, 128, 8, 2>(128),
-      make_variant<128, 64, 8, 1, 3>(128),  // full windows over 1x2-block regions
+      make_variant<128, 64, 8, 1, 3, 1>(128),  // CTA pairs, full windows over 1x2-block regions
+      make_variant<128, 64, 8, 1, 3>(128),
+      make_variant<128, 64, 8, 1, 1, 1>(128),
       make_variant<128, 64, 8, 1, 1>(128),
   };
   return v;
 }
 
-// The first variant of a shape is its default mode; SARBON_WINDOW_MODE=0|1|3 overrides it
-// for the window-capable shapes (measurement aid).
-const Variant* find_variant(int cin, int cout, int t, int s, int win = -1) {
-  for (const auto& v : variants())
-    if (v.cin == cin && v.cout == cout && v.t == t && v.s == s && (win < 0 || v.win == win)) return &v;
+// SARBON_NO_PAIR=1 skips the CTA-pair variants (measurement aid).
+bool pairs_disabled() {
+  const char* env = std::getenv("SARBON_NO_PAIR");
+  return env && std::atoi(env) != 0;
+}
+
+// mode < 0: the default variant of the shape; else the variant with that mode
+// (window mode | pair << 3).
+const Variant* find_variant(int cin, int cout, int t, int s, int mode = -1) {
+  const bool no_pair = pairs_disabled();
+  for (const auto& v : variants()) {
+    if (v.cin != cin || v.cout != cout || v.t != t || v.s != s) continue;
+    if (mode < 0 ? (no_pair && v.pair) : v.mode() != mode) continue;
+    return &v;
+  }
   return nullptr;
 }
 
 }  // namespace
 
+// The mode the engine runs a layer with: the default variant's, or with
+// SARBON_WINDOW_MODE=0|1|3 (measurement aid) that window mode where the shape has it.
 int conv_tc_pick_mode(int cin, int cout, int t, int s) {
   const Variant* v = find_variant(cin, cout, t, s);
   if (!v) return -1;
   const char* env = std::getenv("SARBON_WINDOW_MODE");
   if (env && v->win != 0) {
     const int want = std::atoi(env);
+    if (find_variant(cin, cout, t, s, want | (v->pair << 3))) return want | (v->pair << 3);
     if (find_variant(cin, cout, t, s, want)) return want;
   }
-  return v->win;
+  return v->mode();
 }
 
 namespace {
-
+// The variant the engine runs (and whose weight image it builds) for a shape.
+const Variant* picked(int cin, int cout, int t, int s) {
+  const int m = conv_tc_pick_mode(cin, cout, t, s);
+  return m < 0 ? nullptr : find_variant(cin, cout, t, s, m);
+}
 }  // namespace
 
 bool conv_tc_supported(int cin, int cout, int t, int s) { return find_variant(cin, cout, t, s) != nullptr; }
 
 int conv_tc_nsplit(int cin, int cout, int t, int s) {
-  const Variant* v = find_variant(cin, cout, t, s);
+  const Variant* v = picked(cin, cout, t, s);
   return v ? v->cout / v->ncta : 0;
 }
 
 size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s) {
-  const Variant* v = find_variant(cin, cout, t, s);
+  const Variant* v = picked(cin, cout, t, s);
   return v ? (size_t)v->w_bytes * (v->cout / v->ncta) : 0;
 }
 
 int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s) {
-  const Variant* v = find_variant(cin, cout, t, s);
+  const Variant* v = picked(cin, cout, t, s);
   if (!v) return 0;
   return 1;
 }
@@ -692,7 +794,7 @@ int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s) {
 // then channel chunk), NCTA rows of ROWB bytes, K-major, with the 128B/64B swizzle
 // applied exactly as the MMA reads it from a 1024-byte-aligned shared buffer.
 void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_t* out) {
-  const Variant* v = find_variant(cin, cout, t, s);
+  const Variant* v = picked(cin, cout, t, s);
   if (!v) return;
   const bool manual = cin < 16;
   const int ch = v->ch, rowb = ch * 2, ncta = v->ncta, nsplit = cout / ncta;
@@ -749,7 +851,7 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
                               int mode) {
   const Variant* v = nullptr;
   for (const auto& c : variants())
-    if (c.cin == cin && c.t == t && c.s == s && c.win == mode) { v = &c; break; }
+    if (c.cin == cin && c.t == t && c.s == s && c.win == (mode & 7)) { v = &c; break; }
   if (!v) return cudaErrorInvalidValue;
   const bool win = v->win != 0;
   if (cin < 16) {
@@ -795,15 +897,40 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, v->fn, v->threads, v->smem) != cudaSuccess || o < 1) o = 1;
     occ[idx] = o;
   }
+  if (v->pair) {
+    // 2-CTA clusters, as many as can be resident at once (the loop over M-tile pairs is
+    // persistent, so every cluster must be running)
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(v->threads, 1, 1);
+    cfg.dynamicSmemBytes = v->smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int max_clusters[32] = {};
+    if (max_clusters[idx] == 0) {
+      cfg.gridDim = dim3(2 * (grid_x / 2 > 0 ? grid_x / 2 : 1), 1, 1);
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, v->fn, &cfg) != cudaSuccess || n < 1) n = 1;
+      max_clusters[idx] = n;
+    }
+    int pairs = grid_x / 2;
+    if (pairs > max_clusters[idx]) pairs = max_clusters[idx];
+    if (pairs < 1) pairs = 1;
+    cfg.gridDim = dim3(2 * pairs, 1, 1);
+    return cudaLaunchKernelEx(&cfg, v->fn, a, *map);
+  }
   // each CTA keeps one C_out slice: the grid is a multiple of the number of slices
   const int nsplit = a.cout / v->ncta;
   int gx = grid_x * occ[idx];
   gx -= gx % nsplit;
   if (gx < nsplit) gx = nsplit;
   dim3 grid(gx, 1);
-  CUtensorMap dummy;
-  std::memset(&dummy, 0, sizeof(dummy));
-  v->fn<<<grid, v->threads, v->smem, st>>>(a, map ? *map : dummy);
+  v->fn<<<grid, v->threads, v->smem, st>>>(a, *map);
   return cudaGetLastError();
 }
 

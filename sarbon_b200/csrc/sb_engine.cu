@@ -84,7 +84,7 @@ struct sb_engine {
   int n_rk = 0;
   int rk_w[SB_MAX_RKINDS] = {}, rk_h[SB_MAX_RKINDS] = {}, rk_cap[SB_MAX_RKINDS] = {};
   int32_t* rlists[SB_MAX_RKINDS] = {};
-  int layer_mode[SB_MAX_LAYERS] = {};   // 0 im2col / gather, 1 row windows, 3 full windows
+  int layer_mode[SB_MAX_LAYERS] = {};   // 0 im2col / gather, 1 row windows, 3 full windows; +8 CTA pairs
   int layer_rk[SB_MAX_LAYERS] = {};     // region kind of a window-mode layer (-1: blocks)
   unsigned long long* status = nullptr;
   int n_chunks = 0;
@@ -417,9 +417,10 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
     e->layer_mode[i] = dtype == SB_F16 ? conv_tc_pick_mode(layers[i].cin, layers[i].cout, e->layer_t[i],
                                                            layers[i].stride)
                                        : 0;
-    if (e->layer_mode[i] == 0) continue;
+    const int win = e->layer_mode[i] & 7;  // bit 3: CTA pairs
+    if (win == 0) continue;
     const int t = e->layer_t[i];
-    const int rw = 8 / t, rh = e->layer_mode[i] == 3 ? 16 / t : 1;
+    const int rw = 8 / t, rh = win == 3 ? 16 / t : 1;
     int k = 0;
     while (k < e->n_rk && !(e->rk_w[k] == rw && e->rk_h[k] == rh)) ++k;
     if (k == e->n_rk) {

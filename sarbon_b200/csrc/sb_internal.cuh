@@ -105,8 +105,9 @@ cudaError_t launch_set_mode(State* st, int mode, int reset_hyst, int64_t force_t
 
 // fp16 tcgen05 path.  Returns cudaErrorInvalidValue for shapes without an instantiation.
 bool conv_tc_supported(int cin, int cout, int t, int s);  // some mode exists for the shape
-// window mode the engine runs a layer with: 0 per-tap im2col (or first-layer gather),
-// 1 per-ky row windows over (8/t)x1-block regions, 3 full windows over (8/t)x(16/t) regions
+// mode the engine runs a layer with: window mode 0 per-tap im2col (or first-layer gather),
+// 1 per-ky row windows over (8/t)x1-block regions, 3 full windows over (8/t)x(16/t)
+// regions; plus 8 when 2-CTA clusters run M=256 cta_group::2 MMAs
 int conv_tc_pick_mode(int cin, int cout, int t, int s);
 int conv_tc_nsplit(int cin, int cout, int t, int s);   // CTA splits of cout
 size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s);  // all splits

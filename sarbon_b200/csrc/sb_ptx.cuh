@@ -184,6 +184,73 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);    // M >> 4
 }
 
+// ---------------------------------------------------------------- CTA pairs (cta_group::2)
+// A 2-CTA cluster runs one M=256 tcgen05.mma: each CTA supplies 128 rows of A and half of
+// the N rows of B from its own shared memory (same offsets), and holds its 128 rows of D
+// in its own TMEM.  Only the even CTA (rank 0) issues MMAs and commits.
+SB_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of both CTAs: release prior memory operations, wait for the other CTA.
+SB_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the variable at shared::cta address `a` in CTA `rank`.
+SB_DEV uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
+SB_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+SB_DEV void tmem_alloc2(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+SB_DEV void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+SB_DEV void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+SB_DEV void mma_f16_ss2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Arrive once on the mbarrier at shared::cluster address `bar` (this CTA's or the peer's)
+// when all prior cta_group::2 tcgen05 ops of this thread have completed.
+SB_DEV void mma_commit2(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+// Arrive once on the mbarrier at the same shared-memory offset as `bar` in both CTAs of
+// the pair when all prior cta_group::2 tcgen05 ops of this thread have completed.
+SB_DEV void mma_commit2_both(const uint64_t* bar) {
+  const uint16_t mask = 3;
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"(mask)
+               : "memory");
+}
+// Tile load into this CTA's shared memory whose completed bytes are counted on the mbarrier
+// at shared::cluster address `bar` (the pair leader's), for cta_group::2 MMAs.
+SB_DEV void tma_load_4d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- misc
 SB_DEV void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 SB_DEV void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
