@@ -140,14 +140,14 @@ class ClockSampler:
 
 
 def layer_flops(eng, counts, mode):
-    """Algorithmic conv FLOPs of one step: 2*cin*cout*9*t^2 per active tile per layer,
+    """Algorithmic conv FLOPs of one step per layer: 2*cin*cout*9*t^2 per active tile,
     counted on the real active counts k_d (dense: every block)."""
-    total = 0
+    out = []
     for l in eng.layers:
         t = eng.block // l.out_stride
         k = eng.n_blocks if mode == "dense" else counts[eng.ds.index(eng.dilation(l.radius))]
-        total += 2 * l.w_tile.shape[2] * l.w_tile.shape[3] * 9 * t * t * k
-    return total
+        out.append(2 * l.w_tile.shape[2] * l.w_tile.shape[3] * 9 * t * t * k)
+    return out
 
 
 def gate_bytes(eng, n_changed):
@@ -297,6 +297,7 @@ def run_b200(args):
     prof = {"gate": 0.0, "lists": 0.0, "copy": 0.0, "conv": 0.0, "finalize": 0.0}
     per_layer = [0.0] * len(eng.layers)
     conv_flops, gbytes, nprof = 0, 0, 0
+    flops_layer = [0] * len(eng.layers)
     eng.reset(seq[0])
     for i in range(args.profile_steps):
         f = seq[1 + i % (len(seq) - 1)]
@@ -309,7 +310,10 @@ def run_b200(args):
         for j in range(len(eng.layers)):
             per_layer[j] += kms[3 + j]
         prof["finalize"] += kms[3 + len(eng.layers)]
-        conv_flops += layer_flops(eng, counts, mode) if mode != "skip" else 0
+        if mode != "skip":
+            fl = layer_flops(eng, counts, mode)
+            conv_flops += sum(fl)
+            flops_layer = [a + b for a, b in zip(flops_layer, fl)]
         gbytes += gate_bytes(eng, int(eng.changed.sum().item()))
         nprof += 1
     peaks, src = load_peaks()
@@ -398,6 +402,8 @@ def run_b200(args):
                              f"the image cache (> 126 MB L2)"},
             "roofline": roof, "roofline_gate": roof_gate, "kernel_time_share": share,
             "conv_us_per_layer": {l.dst: round(1e3 * t / max(nprof, 1), 1) for l, t in zip(eng.layers, per_layer)},
+            "conv_tflops_per_layer": {l.dst: round(f / (t * 1e-3) / 1e12, 1) if t > 0 else None
+                                      for l, f, t in zip(eng.layers, flops_layer, per_layer)},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clock_info}
     print(json.dumps(line), flush=True)

@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
 
   // work of this launch, decided on the device (no host sync)
   const int mode = a.st->mode_cur;
-  const int listed = WIN ? a.st->rcounts[a.rkind][a.d_idx] : a.st->counts[a.d_idx];
+  const int listed = (WIN && a.rkind >= 0) ? a.st->rcounts[a.rkind][a.d_idx] : a.st->counts[a.d_idx];
   const int n_units =
       WIN ? a.n_blocks / (a.hb * a.wb) * ((a.hb + a.rh - 1) / a.rh) * ((a.wb + a.rw - 1) / a.rw) : a.n_blocks;
   int n_tiles = 0;

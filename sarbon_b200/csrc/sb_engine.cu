@@ -163,6 +163,10 @@ int launch_convs(sb_engine* e, cudaStream_t s) {
       a.rcam = e->rlists[rk] + (size_t)di * 3 * e->rk_cap[rk];
       a.rry = a.rcam + e->rk_cap[rk];
       a.rrx = a.rry + e->rk_cap[rk];
+    } else {  // window layers with one-block regions iterate over the block lists
+      a.rcam = a.lcam;
+      a.rry = a.lby;
+      a.rrx = a.lbx;
     }
     cudaError_t err;
     if (e->dtype == SB_F16) {
@@ -406,7 +410,7 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
     const size_t bytes = (size_t)e->shape[i][0] * e->shape[i][1] * e->shape[i][2] * e->shape[i][3] * e->esz;
     if ((rc = alloc_dev(e, &e->cache[i], bytes))) return bail(rc);
   }
-  e->n_chunks = (e->n_blocks + 1023) / 1024;
+  e->n_chunks = (e->n_blocks + SB_LIST_CHUNK - 1) / SB_LIST_CHUNK;
   if ((rc = alloc_dev(e, (void**)&e->changed, e->n_blocks))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->extra, e->n_blocks))) return bail(rc);
   if ((rc = alloc_dev(e, (void**)&e->masks, (size_t)e->nd * e->n_blocks))) return bail(rc);
@@ -421,6 +425,7 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
     if (win == 0) continue;
     const int t = e->layer_t[i];
     const int rw = 8 / t, rh = win == 3 ? 16 / t : 1;
+    if (rw == 1 && rh == 1) continue;  // a one-block region is a block: the layer uses the block lists
     int k = 0;
     while (k < e->n_rk && !(e->rk_w[k] == rw && e->rk_h[k] == rh)) ++k;
     if (k == e->n_rk) {

@@ -284,12 +284,14 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
 }
 
 // ---------------------------------------------------------------- dilation + ordered lists
-// One thread per block (flat index over all cameras), 1024 per CTA.  For each dilation d
-// the mask is max_pool2d(changed, 2d+1, 1, d) within the camera (fused_engine.py:151);
-// active blocks are compacted in ascending flat order (nonzero_static, :163) with a
-// warp ballot, a CTA prefix and a decoupled look-back across CTAs.  Chunks are taken by
+// One thread per block (flat index over all cameras), SB_LIST_CHUNK per CTA.  For each
+// dilation d the mask is max_pool2d(changed, 2d+1, 1, d) within the camera
+// (fused_engine.py:151); active blocks are compacted in ascending flat order
+// (nonzero_static, :163) with a warp ballot, a CTA prefix and a decoupled look-back across
+// CTAs in which a whole warp inspects 32 predecessors at a time.  Chunks are taken by
 // ticket, so a CTA only ever waits on CTAs that are already running.
-#define LIST_THREADS 1024
+#define LIST_THREADS SB_LIST_CHUNK
+#define LIST_WARPS (LIST_THREADS / 32)
 #define LB_FLAG_AGG 1ull
 #define LB_FLAG_INC 2ull
 
@@ -303,6 +305,43 @@ SB_DEV unsigned long long lb_load(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+SB_DEV uint32_t warp_sum(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// Exclusive prefix of chunk `chunk` in the look-back array `stat` (executed by a full warp;
+// the result is returned on every lane).  Lane i reads predecessor p - i; a window is
+// usable once every lane up to the nearest inclusive prefix has published.
+SB_DEV uint32_t lookback(unsigned long long* stat, uint32_t chunk, uint32_t epoch, State* st) {
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t excl = 0;
+  int p = (int)chunk - 1;
+  uint32_t spins = 0;
+  while (p >= 0) {
+    const int q = p - (int)lane;
+    unsigned long long w = q >= 0 ? lb_load(stat + q) : lb_pack(epoch, LB_FLAG_INC, 0);  // before chunk 0: 0
+    const bool ready = (uint32_t)(w >> 32) == epoch && ((w >> 30) & 3ull) != 0;
+    const bool inc = ready && ((w >> 30) & 3ull) == LB_FLAG_INC;
+    const uint32_t notready = __ballot_sync(0xFFFFFFFFu, !ready);
+    const uint32_t incm = __ballot_sync(0xFFFFFFFFu, inc);
+    const uint32_t upto = incm ? (2u << (__ffs(incm) - 1)) - 1u : 0xFFFFFFFFu;  // lanes 0..first inclusive
+    if (notready & upto) {
+      if (++spins > SB_SPIN_LIMIT) {
+        if (lane == 0) atomicOr(&st->error, SB_ERR_TIMEOUT_LOOKBK);
+        break;
+      }
+      __nanosleep(32);
+      continue;
+    }
+    const uint32_t v = (upto >> lane) & 1u ? (uint32_t)(w & 0x3FFFFFFFull) : 0u;
+    excl += warp_sum(v);
+    if (incm) break;
+    p -= 32;
+  }
+  return excl;
 }
 
 __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
@@ -319,7 +358,7 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
   constexpr int NK = 1 + SB_MAX_RKINDS;
   constexpr int ML = NK * SB_MAX_DILATIONS;
   __shared__ uint32_t s_chunk;
-  __shared__ uint32_t s_warp[ML][32];
+  __shared__ uint32_t s_warp[ML][LIST_WARPS];
   __shared__ uint32_t s_excl[ML];
   const uint32_t epoch = st->epoch;
   if (threadIdx.x == 0) s_chunk = atomicAdd(&st->ticket, 1u);
@@ -371,51 +410,32 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    for (int L = 0; L < nl; ++L) {
-      const uint32_t v = s_warp[L][lane];
-      uint32_t inc = v;
+  // warp w handles compaction lanes w, w + LIST_WARPS, ...: CTA prefix, then the look-back
+  for (int L = (int)warp; L < nl; L += LIST_WARPS) {
+    const uint32_t v = lane < LIST_WARPS ? s_warp[L][lane] : 0u;
+    uint32_t inc = v;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
-        if (lane >= (uint32_t)o) inc += t;
-      }
-      s_warp[L][lane] = inc - v;  // exclusive warp offsets
-      const uint32_t agg = __shfl_sync(0xFFFFFFFFu, inc, 31);
-      // decoupled look-back: lane 0 publishes and walks predecessors
-      if (lane == 0) {
-        unsigned long long* stat = a.status + (size_t)L * nchunks;
-        uint32_t excl = 0;
-        if (chunk == 0) {
-          lb_store(stat, lb_pack(epoch, LB_FLAG_INC, agg));
-        } else {
-          lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_AGG, agg));
-          int p = (int)chunk - 1;
-          uint32_t spins = 0;
-          while (p >= 0) {
-            const unsigned long long w = lb_load(stat + p);
-            const uint32_t we = (uint32_t)(w >> 32);
-            const unsigned long long fl = (w >> 30) & 3ull;
-            if (we != epoch || fl == 0) {
-              if (++spins > SB_SPIN_LIMIT) {
-                atomicOr(&st->error, SB_ERR_TIMEOUT_LOOKBK);
-                break;
-              }
-              __nanosleep(32);
-              continue;
-            }
-            excl += (uint32_t)(w & 0x3FFFFFFFull);
-            if (fl == LB_FLAG_INC) break;
-            --p;
-          }
-          lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_INC, excl + agg));
-        }
-        s_excl[L] = excl;
-        if ((int)chunk == nchunks - 1) {
-          const int kind = L / a.n_dil, di = L - kind * a.n_dil;
-          if (kind == 0) st->counts[di] = (int32_t)(excl + agg);
-          else st->rcounts[kind - 1][di] = (int32_t)(excl + agg);
-        }
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+      if (lane >= (uint32_t)o) inc += t;
+    }
+    if (lane < LIST_WARPS) s_warp[L][lane] = inc - v;  // exclusive warp offsets
+    const uint32_t agg = __shfl_sync(0xFFFFFFFFu, inc, 31);
+    unsigned long long* stat = a.status + (size_t)L * nchunks;
+    uint32_t excl = 0;
+    if (chunk == 0) {
+      if (lane == 0) lb_store(stat, lb_pack(epoch, LB_FLAG_INC, agg));
+    } else {
+      if (lane == 0) lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_AGG, agg));
+      excl = lookback(stat, chunk, epoch, st);
+      if (lane == 0) lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_INC, excl + agg));
+    }
+    if (lane == 0) {
+      s_excl[L] = excl;
+      if ((int)chunk == nchunks - 1) {
+        const int kind = L / a.n_dil, di = L - kind * a.n_dil;
+        if (kind == 0) st->counts[di] = (int32_t)(excl + agg);
+        else st->rcounts[kind - 1][di] = (int32_t)(excl + agg);
       }
     }
   }

@@ -14,6 +14,10 @@ namespace sb {
 // block itself is kind "blocks" and has its own lists).
 #define SB_MAX_RKINDS 3
 
+// Blocks per CTA of the list kernel (a multiple of 32); the look-back status arrays hold
+// one word per chunk = ceil(n_blocks / SB_LIST_CHUNK) per compaction lane.
+#define SB_LIST_CHUNK 256
+
 // Device-resident engine state.  Written only by the engine's own kernels (and by
 // cudaMemcpyAsync for host-set knobs), so a whole step runs without a host sync.
 struct State {
