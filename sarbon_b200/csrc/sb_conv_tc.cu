@@ -90,11 +90,14 @@ struct TcCfg {
   static constexpr int WIN_COLS = ((8 + WIN_ELEMS + 7) / 8) * 8;     // box inner extent (elements)
   static constexpr int WIN_LEAD = 8 - CIN;                            // elements before the first used one
   static constexpr int WIN_BUF = ((WIN_ROWS * WIN_COLS * 2 + 127) / 128) * 128;
-  static constexpr int NWB = 4;                                       // window ring depth
+  static constexpr int NWB = 8;                                       // window ring depth
+  static constexpr int NGW = 4;                                       // first layer: gather warps
   static constexpr int WIN_BYTES = MANUAL ? NWB * WIN_BUF : 0;
   static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
-  static constexpr int STAGES = STAGES_FIT > 24 ? 24 : STAGES_FIT;
+  // first layer: a multiple of 8 stages, so that each stage (and each window slot) is
+  // always filled by the same one of the NGW gather warps (see the gather loop)
+  static constexpr int STAGES = STAGES_FIT > 24 ? 24 : MANUAL ? (STAGES_FIT / 8) * 8 : STAGES_FIT;
   // MMA issuers: two (alternate items, one accumulator each) when the ring holds two items'
   // K-blocks; each issuer then owns a sub-ring of SUB stages that the producer fills in
   // item order, so every stage has one in-order consumer and the phase parities stay exact
@@ -107,6 +110,7 @@ struct TcCfg {
   static_assert(NCTA % 32 == 0 && NCTA >= 32 && NMMA <= 256, "UMMA N / epilogue split");
   static_assert(!PAIR || !MANUAL, "CTA pairs need TMA-loaded A stages");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
+  static_assert(!MANUAL || ((NISS * SUB) % NGW == 0 && NWB % NGW == 0), "gather warp per stage / window slot");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
   static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256), "first-layer window box");
   static_assert(!WIN || ((WIN == 1 || WIN == 3) && S == 1 && 8 % T == 0 && T <= 8 && ROWB == 128 && !MANUAL),
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
-      mbar_init(&full[i], C::MANUAL ? 128 : 1);
+      mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -207,7 +211,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
     mbar_init(wpeer, 1);
     for (int i = 0; i < C::NWB; ++i) {
       mbar_init(&winfull[i], 1);
-      mbar_init(&winempty[i], 128);
+      mbar_init(&winempty[i], 1);
     }
     for (int i = 0; i < C::CRING; ++i) {
       mbar_init(&cfull[i], 1);
@@ -264,8 +268,6 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
     if (warp == C::PROD_WARP) {
       // ------------------------------------------------ producer: the slice's weights, A stages
       // The whole warp runs the loop (warp-uniform control flow); lane 0 issues the copies.
-      // Tile coordinates are fetched one item ahead into the other of two register sets
-      // (the loop is unrolled by two, so no set is ever copied while its loads are in flight).
       const bool leader = lane == 0;
       uint32_t g = 0, nload = 0;
       struct Coords {
@@ -377,13 +379,35 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         }
         return true;
       };
+      // Lane l loads the unit coordinates of item base + l, one batch of 32 items ahead of
+      // their use (two batches alternate between the register sets ca and cb), so the
+      // list reads' latency is paid once per 32 items; items take theirs by shuffle.
+      auto fetch_lane = [&](int base, Coords& o) {
+        if (base + (int)lane < my_items) fetch(base + (int)lane, o);
+      };
+      auto run_batch = [&](int base, const Coords& cur) -> bool {
+        for (int i = 0; i < 32 && base + i < my_items; ++i) {
+          if (*abort_flag) return false;
+          Coords cc;
+#pragma unroll
+          for (int j = 0; j < C::TPM; ++j) {
+            cc.cam[j] = __shfl_sync(0xFFFFFFFFu, cur.cam[j], i);
+            cc.y0[j] = __shfl_sync(0xFFFFFFFFu, cur.y0[j], i);
+            cc.x0[j] = __shfl_sync(0xFFFFFFFFu, cur.x0[j], i);
+            cc.uy[j] = __shfl_sync(0xFFFFFFFFu, cur.uy[j], i);
+            cc.ux[j] = __shfl_sync(0xFFFFFFFFu, cur.ux[j], i);
+          }
+          if (!issue(base + i, cc)) return false;
+        }
+        return true;
+      };
       Coords ca, cb;
-      fetch(0, ca);
-      for (int it = 0; it < my_items && !*abort_flag; it += 2) {
-        if (it + 1 < my_items) fetch(it + 1, cb);
-        if (!issue(it, ca) || it + 1 >= my_items) break;
-        if (it + 2 < my_items) fetch(it + 2, ca);
-        if (!issue(it + 1, cb)) break;
+      fetch_lane(0, ca);
+      for (int base = 0; base < my_items; base += 64) {
+        if (base + 32 < my_items) fetch_lane(base + 32, cb);
+        if (!run_batch(base, ca) || base + 32 >= my_items) break;
+        if (base + 64 < my_items) fetch_lane(base + 64, ca);
+        if (!run_batch(base + 32, cb)) break;
       }
       // drain: every issued copy has landed before the CTA may exit
       volatile int never = 0;
@@ -406,54 +430,63 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       if (nload > 0) warp_wait(wfull, 0, &never);
     } else if (C::MANUAL && (int)threadIdx.x >= C::GATHER0) {
       // ------------------------------------------------ gather producers (first layer)
-      // Each thread builds one A row (one output pixel: 3x3 taps x channels, zero-padded to
-      // KPAD) from the TMA-loaded input window of its item.
-      const int r = threadIdx.x - C::GATHER0;  // A row = output pixel slot, 0..127
-      const int lr = r / T, lc = r % T;
-      uint32_t g = 0;
-      for (int it = 0; it < my_items && !*abort_flag; ++it, ++g) {
+      // Gather warp gw builds all 128 A rows (one output pixel each: 3x3 taps x channels,
+      // zero-padded to KPAD) of items gw, gw + NGW, ... from the TMA-loaded input window of
+      // the item, four rows per lane, so NGW items are in flight.  Item it uses window slot
+      // it % NWB and stage stage_of(it): both are always filled by this same warp.
+      const int gw = ((int)threadIdx.x - C::GATHER0) >> 5;
+      for (int it = gw; it < my_items && !*abort_flag; it += C::NGW) {
         const int b = it % C::NWB;
-        if (!mbar_wait(&winfull[b], (it / C::NWB) & 1u, abort_flag)) {
+        if (!warp_wait(&winfull[b], (it / C::NWB) & 1u, abort_flag)) {
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
           *abort_flag = 1;
           break;
         }
         uint32_t s, ph;
         stage_of<C>(it, 0, s, ph);
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) {
+        if (!warp_wait(&empty[s], ph ^ 1u, abort_flag)) {
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_EMPTY);
           *abort_flag = 1;
           break;
         }
-        // element (ky, kx, c) of output (lr, lc): window row S*lr+ky, column
-        // lead + (S*lc + kx)*CIN + c  (the window starts one input pixel left of the tile)
-        const uint16_t* wrow = reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(win) +
-                                                                 b * C::WIN_BUF) +
-                               (S * lr) * C::WIN_COLS + C::WIN_LEAD + (S * lc) * CIN;
-        uint16_t v[C::KPAD > 0 ? C::KPAD : 16];
+        const uint16_t* wbase =
+            reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(win) + b * C::WIN_BUF) + C::WIN_LEAD;
 #pragma unroll
-        for (int k = 0; k < C::KPAD; ++k) v[k] = 0;
+        for (int j = 0; j < 4; ++j) {
+          const int r = lane + 32 * j;  // A row = output pixel slot, 0..127
+          const int lr = r / T, lc = r % T;
+          // element (ky, kx, c) of output (lr, lc): window row S*lr+ky, column
+          // lead + (S*lc + kx)*CIN + c  (the window starts one input pixel left of the tile)
+          const uint16_t* wrow = wbase + (S * lr) * C::WIN_COLS + (S * lc) * CIN;
+          uint16_t v[C::KPAD > 0 ? C::KPAD : 16];
 #pragma unroll
-        for (int ky = 0; ky < 3; ++ky)
+          for (int k = 0; k < C::KPAD; ++k) v[k] = 0;
 #pragma unroll
-          for (int kx = 0; kx < 3; ++kx)
+          for (int ky = 0; ky < 3; ++ky)
 #pragma unroll
-            for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = wrow[ky * C::WIN_COLS + kx * CIN + c];
-        uint8_t* row = sA + s * C::A_STAGE + r * C::ROWB;
-        constexpr int NQ = C::ROWB / 16;
+            for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-          const int pq = C::SWZ == 2 ? (q ^ (r & 7)) : (q ^ ((r >> 1) & 3));
-          uint4 w4;
-          w4.x = v[q * 8 + 0] | ((uint32_t)v[q * 8 + 1] << 16);
-          w4.y = v[q * 8 + 2] | ((uint32_t)v[q * 8 + 3] << 16);
-          w4.z = v[q * 8 + 4] | ((uint32_t)v[q * 8 + 5] << 16);
-          w4.w = v[q * 8 + 6] | ((uint32_t)v[q * 8 + 7] << 16);
-          *reinterpret_cast<uint4*>(row + pq * 16) = w4;
+              for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = wrow[ky * C::WIN_COLS + kx * CIN + c];
+          uint8_t* row = sA + s * C::A_STAGE + r * C::ROWB;
+          constexpr int NQ = C::ROWB / 16;
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            const int pq = C::SWZ == 2 ? (q ^ (r & 7)) : (q ^ ((r >> 1) & 3));
+            uint4 w4;
+            w4.x = v[q * 8 + 0] | ((uint32_t)v[q * 8 + 1] << 16);
+            w4.y = v[q * 8 + 2] | ((uint32_t)v[q * 8 + 3] << 16);
+            w4.z = v[q * 8 + 4] | ((uint32_t)v[q * 8 + 5] << 16);
+            w4.w = v[q * 8 + 6] | ((uint32_t)v[q * 8 + 7] << 16);
+            *reinterpret_cast<uint4*>(row + pq * 16) = w4;
+          }
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&full[s]);
-        mbar_arrive(&winempty[b]);
+        fence_proxy_async_smem();  // these generic-proxy writes feed the MMA (async proxy)
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&full[s]);
+          mbar_arrive(&winempty[b]);
+        }
+        __syncwarp();
       }
     } else if (warp == C::MMA_WARP || warp == C::MMA_WARP + 1) {
       // ------------------------------------------------ MMA issuers
