@@ -608,7 +608,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       // unit coordinates come from the producer through the shared-memory ring, so the
       // residual prefetch below depends on no global load
       auto fetch = [&](int it, Row& o) -> bool {
-        const Item w = item_at(it, nsplit);
+        const Item w = item_of(it);
         o.n0 = PAIR ? col0 : w.split * NCTA + col0;
         int ti, p, j;
         if (WIN) { j = r / C::RPX; ti = w.m * C::TPM + j; p = r % C::RPX; }

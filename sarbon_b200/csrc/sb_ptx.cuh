@@ -114,6 +114,10 @@ SB_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned address, bytes % 16 == 0).
+SB_DEV void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 SB_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -203,9 +207,12 @@ SB_DEV uint32_t mapa_shared(uint32_t a, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
   return r;
 }
-// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
+// Arrive on an mbarrier given by its shared::cluster address (default semantics: release
+// at CTA scope).  A cluster-scope release would first wait until this thread's earlier
+// global stores are visible device-wide; the callers only need their tcgen05 accesses
+// ordered, which tcgen05.fence::before_thread_sync does, or earlier mbarrier completions.
 SB_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 SB_DEV void tmem_alloc2(uint32_t* dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
