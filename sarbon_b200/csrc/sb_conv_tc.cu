@@ -34,6 +34,7 @@
 namespace sb {
 
 constexpr int kMaxSmem = 232448;  // 227 KB opt-in shared memory per CTA on sm_100
+constexpr int kMaxCout = 128;     // widest layer of the stem (bias staged in shared memory)
 
 // WIN = 0: per-tap im2col boxes over blocks (or the first layer's gather);
 // WIN = 1: row windows -- regions of 8/T x 1 blocks (8 px x T rows), one box per (ky, chunk)
@@ -78,10 +79,9 @@ struct TcCfg {
   static constexpr int THREADS = MANUAL ? 480 : 352;
   static constexpr int W_OFF = 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
-  static constexpr int BIAS_BYTES = 256 * 4;          // every output channel (C_out <= 256)
-  static constexpr int CRING = 16;                    // item-coordinate ring (producer -> epilogue)
+  static constexpr int BIAS_BYTES = kMaxCout * 4;     // every output channel
+  static constexpr int CRING = MANUAL ? 16 : 8;       // item-coordinate ring (producer -> epilogue)
   static constexpr int CRING_BYTES = CRING * 8 * 4 * 4; // <= 8 units x (cam, row, col, pad) per item
-  static constexpr int BAR_BYTES = 1024;
   // first layer: the input window of one M-tile (BOX_ROWS output rows of one tile), loaded
   // by one 3-D TMA box from the image cache viewed as [N][H][W*CIN]; the box starts 8
   // elements (16 B) before the window's first element... rounded so x stays 16-byte aligned
@@ -93,6 +93,10 @@ struct TcCfg {
   static constexpr int NWB = 8;                                       // window ring depth
   static constexpr int NGW = 4;                                       // first layer: gather warps
   static constexpr int WIN_BYTES = MANUAL ? NWB * WIN_BUF : 0;
+  // mbarriers (sized for the most stages that could fit) + TMEM address + abort flag
+  static constexpr int STAGES_UB = (kMaxSmem - A_OFF) / A_STAGE > 24 ? 24 : (kMaxSmem - A_OFF) / A_STAGE;
+  static constexpr int N_BARS = 2 * STAGES_UB + 8 + (MANUAL ? 2 * NWB : 0) + 2 * CRING;
+  static constexpr int BAR_BYTES = ((N_BARS * 8 + 8) + 127) / 128 * 128;
   static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
   // first layer: a multiple of 8 stages, so that each stage (and each window slot) is
@@ -185,9 +189,9 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   uint64_t* wfull = acce + 2;
   uint64_t* dbar = wfull + 1;            // [2]: drain of each MMA issuer
   uint64_t* wpeer = dbar + 2;            // pairs: the odd CTA's weights have landed
-  uint64_t* winfull = dbar + 3;          // first-layer window ring
+  uint64_t* winfull = dbar + 3;          // first-layer window ring (MANUAL only)
   uint64_t* winempty = winfull + C::NWB;
-  uint64_t* cfull = winempty + C::NWB;   // item-coordinate ring
+  uint64_t* cfull = C::MANUAL ? winempty + C::NWB : winfull;  // item-coordinate ring
   uint64_t* cempty = cfull + C::CRING;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(cempty + C::CRING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
@@ -209,9 +213,11 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
     mbar_init(&dbar[0], 1);
     mbar_init(&dbar[1], 1);
     mbar_init(wpeer, 1);
-    for (int i = 0; i < C::NWB; ++i) {
-      mbar_init(&winfull[i], 1);
-      mbar_init(&winempty[i], 1);
+    if (C::MANUAL) {
+      for (int i = 0; i < C::NWB; ++i) {
+        mbar_init(&winfull[i], 1);
+        mbar_init(&winempty[i], 1);
+      }
     }
     for (int i = 0; i < C::CRING; ++i) {
       mbar_init(&cfull[i], 1);
@@ -670,8 +676,11 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
 #pragma unroll
           for (int j = 0; j < C::NCOL / 8; ++j) {
             float f[8];
+            const float4 b0 = *reinterpret_cast<const float4*>(sBias + cu.n0 + j * 8);  // one broadcast
+            const float4 b1 = *reinterpret_cast<const float4*>(sBias + cu.n0 + j * 8 + 4);
+            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + sBias[cu.n0 + j * 8 + e];
+            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + bb[e];
             if (res != nullptr) {
               const __half2* h = reinterpret_cast<const __half2*>(&cu.rr[j]);
 #pragma unroll
@@ -916,7 +925,7 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
 
 cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, int grid_x, cudaStream_t st) {
   const Variant* v = find_variant(a.cin, a.cout, a.t, a.s, mode);
-  if (!v || map == nullptr) return cudaErrorInvalidValue;  // every variant loads through TMA
+  if (!v || map == nullptr || a.cout > kMaxCout) return cudaErrorInvalidValue;  // every variant loads through TMA
   static bool attr_done[32] = {};
   const int idx = (int)(v - variants().data());
   if (!attr_done[idx]) {
