@@ -70,11 +70,16 @@ struct TcCfg {
   static constexpr int B_KB = NCTA * ROWB;
   static constexpr int W_BYTES = NWKB * B_KB;
   static constexpr int NMMA = PAIR ? 2 * NCTA : NCTA;  // MMA N = accumulator columns per CTA
-  static constexpr int TMEM_COLS = (2 * NMMA) <= 32 ? 32 : (2 * NMMA) <= 64 ? 64 : (2 * NMMA) <= 128 ? 128 : (2 * NMMA) <= 256 ? 256 : 512;
+  // narrow layers: two epilogue groups of four warps take alternate items (each warp all
+  // NMMA columns of its 32 rows) and four accumulator buffers let the MMAs run further
+  // ahead; wide layers: all eight warps on every item (half the columns each), two buffers
+  static constexpr int EPG = NMMA <= 64 ? 2 : 1;
+  static constexpr int NACC = EPG == 2 ? 4 : 2;
+  static constexpr int TMEM_COLS = (NACC * NMMA) <= 32 ? 32 : (NACC * NMMA) <= 64 ? 64 : (NACC * NMMA) <= 128 ? 128 : (NACC * NMMA) <= 256 ? 256 : 512;
   // roles: warps 0-7 epilogue (two per TMEM lane quadrant, half the columns each),
   // warp 8 TMA producer, warps 9-10 MMA issuers (warp 9 owns TMEM), warps 11-14 first-layer gather
-  static constexpr int EPI_THREADS = 256;
-  static constexpr int NCOL = NMMA / 2;               // accumulator columns per epilogue warp
+  static constexpr int NCOL = EPG == 2 ? NMMA : NMMA / 2;  // accumulator columns per epilogue warp
+  static constexpr int EPI_WARPS_PER_ITEM = 8 / EPG;
   static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 352;  // MMA issuers: warps 9, 10
   static constexpr int THREADS = MANUAL ? 480 : 352;
   static constexpr int W_OFF = 0;
@@ -95,7 +100,7 @@ struct TcCfg {
   static constexpr int WIN_BYTES = MANUAL ? NWB * WIN_BUF : 0;
   // mbarriers (sized for the most stages that could fit) + TMEM address + abort flag
   static constexpr int STAGES_UB = (kMaxSmem - A_OFF) / A_STAGE > 24 ? 24 : (kMaxSmem - A_OFF) / A_STAGE;
-  static constexpr int N_BARS = 2 * STAGES_UB + 8 + (MANUAL ? 2 * NWB : 0) + 2 * CRING;
+  static constexpr int N_BARS = 2 * STAGES_UB + 2 * NACC + 4 + (MANUAL ? 2 * NWB : 0) + 2 * CRING;
   static constexpr int BAR_BYTES = ((N_BARS * 8 + 8) + 127) / 128 * 128;
   static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
@@ -184,9 +189,9 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sBias) + C::BIAS_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::STAGES;
-  uint64_t* accf = bars + 2 * C::STAGES;
-  uint64_t* acce = accf + 2;
-  uint64_t* wfull = acce + 2;
+  uint64_t* accf = bars + 2 * C::STAGES;  // [NACC] accumulator full / empty
+  uint64_t* acce = accf + C::NACC;
+  uint64_t* wfull = acce + C::NACC;
   uint64_t* dbar = wfull + 1;            // [2]: drain of each MMA issuer
   uint64_t* wpeer = dbar + 2;            // pairs: the odd CTA's weights have landed
   uint64_t* winfull = dbar + 3;          // first-layer window ring (MANUAL only)
@@ -205,9 +210,10 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < C::NACC; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], PAIR ? 16 : C::EPI_THREADS);  // pairs: one arrival per epilogue warp of both CTAs
+      // one arrival per epilogue warp on the item (of both CTAs of a pair)
+      mbar_init(&acce[i], C::EPI_WARPS_PER_ITEM * (PAIR ? 2 : 1));
     }
     mbar_init(wfull, 1);
     mbar_init(&dbar[0], 1);
@@ -221,7 +227,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
     }
     for (int i = 0; i < C::CRING; ++i) {
       mbar_init(&cfull[i], 1);
-      mbar_init(&cempty[i], 8);  // one arrival per epilogue warp
+      mbar_init(&cempty[i], C::EPI_WARPS_PER_ITEM);  // one arrival per epilogue warp on the item
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -518,8 +524,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           ok = false;
         }
         for (int it = u; ok && it < my_items; it += C::NISS) {
-          const int ab = it & 1;
-          if (!mbar_wait(&acce[ab], ((it >> 1) & 1) ^ 1, abort_flag)) {
+          const int ab = it % C::NACC;
+          if (!mbar_wait(&acce[ab], ((it / C::NACC) & 1) ^ 1, abort_flag)) {
             atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
             *abort_flag = 1;
             break;
@@ -597,10 +603,12 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       __syncwarp();
     } else if (warp < 8) {
       // ------------------------------------------------ epilogue: TMEM -> bias/res/ReLU -> cache
-      // Warp w reads TMEM lanes 32*(w%4).. (its accumulator rows) and columns
-      // (w/4)*NCOL.. of them.  The residual is fetched before the accumulator wait and the
-      // TMEM buffer is released as soon as it sits in registers.
-      const int q = warp & 3, col0 = (warp >> 2) * C::NCOL;
+      // Warp w reads TMEM lanes 32*(w%4).. (its accumulator rows); with two groups (EPG = 2)
+      // warps 0-3 take the even and warps 4-7 the odd items with all NCOL = NMMA columns,
+      // else every warp takes every item with columns (w/4)*NCOL...  The residual is fetched
+      // one item ahead and the TMEM buffer is released as soon as it sits in registers.
+      const int q = warp & 3, eg = C::EPG == 2 ? (warp >> 2) : 0;  // lane quadrant, group
+      const int col0 = C::EPG == 2 ? 0 : (warp >> 2) * C::NCOL;
       const int r = q * 32 + lane;  // accumulator row = TMEM lane
       __half* y = static_cast<__half*>(a.y);
       const __half* res = static_cast<const __half*>(a.res);
@@ -646,8 +654,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       // one item: wait for the accumulator, move it to registers, release TMEM, prefetch the
       // next item into `nx`, then bias / residual / ReLU / store item `it` from `cu`
       auto step = [&](int it, const Row& cu, Row& nx) -> bool {
-        const int ab = it & 1;
-        const bool got = mbar_wait(&accf[ab], (it >> 1) & 1, abort_flag);
+        const int ab = it % C::NACC;
+        const bool got = mbar_wait(&accf[ab], (it / C::NACC) & 1, abort_flag);
         if (!got) {
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
           *abort_flag = 1;
@@ -662,13 +670,13 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           tmem_ld16(taddr + j * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[j * 16]));
         tmem_ld_wait();
         tc_fence_before();
-        if (PAIR) {  // one arrival per warp on the leader's barrier
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[ab]), 0));
-        } else {
-          mbar_arrive(&acce[ab]);  // the MMA may overwrite this buffer now
+        // one arrival per warp (on the pair leader's barrier): the MMA may overwrite it now
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[ab]), 0));
+          else mbar_arrive(&acce[ab]);
         }
-        if (it + 1 < my_items && !fetch(it + 1, nx)) {
+        if (it + C::EPG < my_items && !fetch(it + C::EPG, nx)) {
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
           *abort_flag = 1;
         }
@@ -703,14 +711,15 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         }
         return true;
       };
+      // this group's items: eg, eg + EPG, ...
       Row ra, rb;
-      if (!fetch(0, ra)) {
+      if (eg < my_items && !fetch(eg, ra)) {
         atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
         *abort_flag = 1;
       }
-      for (int it = 0; it < my_items; it += 2) {
-        if (!step(it, ra, rb) || it + 1 >= my_items) break;
-        if (!step(it + 1, rb, ra)) break;
+      for (int it = eg; it < my_items; it += 2 * C::EPG) {
+        if (!step(it, ra, rb) || it + C::EPG >= my_items) break;
+        if (!step(it + C::EPG, rb, ra)) break;
       }
     }
   }
