@@ -164,10 +164,14 @@ def build_net(seed):
     return LocalBackbone().eval()
 
 
-def make_frames(args, rank, dev):
+def make_frames(args, rank, dev, world=1):
+    """This rank's shard of the job's world x S streams (contiguous global stream ids),
+    seeded by its first global stream id so that no two ranks share a camera."""
     from sarbon_b200 import scenes
+    from sarbon_b200.multi import shard_streams, stream_seed
     rects = args.rects or auto_rects(args.height, args.width)
-    src = scenes.Streams(args.streams, args.height, args.width, seed=1000 * rank + args.seed + 1,
+    shard = shard_streams(world * args.streams, world, rank)
+    src = scenes.Streams(len(shard), args.height, args.width, seed=stream_seed(args.seed, shard.start),
                          n_rects=rects, device=dev)
     u8 = torch.stack([src.next() for _ in range(args.frames)])  # [F, S, H, W, 3] RGB
     return u8, rects
@@ -234,6 +238,7 @@ def run_reference(args):
 def run_b200(args):
     import torch.distributed as dist
     from sarbon_b200 import FusedSparseEngine, scenes
+    from sarbon_b200.multi import job_rate, max_over_ranks
     rank, world, local = dist_env()
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
@@ -244,7 +249,7 @@ def run_b200(args):
     net = build_net(args.seed).to(dev)
     S, H, W = args.streams, args.height, args.width
     eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev)
-    u8, rects = make_frames(args, rank, dev)
+    u8, rects = make_frames(args, rank, dev, world)
     staged = torch.stack([scenes.normalise(u8[i]) for i in range(u8.shape[0])])  # [F,S,H,W,3] fp16
     order = pingpong(args.frames)
     seq = [staged[i] for i in order]
@@ -284,11 +289,9 @@ def run_b200(args):
     clock_info = clocks.stop()
     launches = eng.launch_count() * args.steps
     ms = start.elapsed_time(end)
-    t = torch.tensor([ms], device=dev, dtype=torch.float64)
     if world > 1:
         dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = t.item()
+    ms_max = max_over_ranks(ms, dev)
     st = eng.device_stats()
     if st.error:
         raise RuntimeError(f"device error flags {st.error} after the timed region")
@@ -365,10 +368,7 @@ def run_b200(args):
         e1.record()
         torch.cuda.synchronize()
         ems = e0.elapsed_time(e1)
-        te = torch.tensor([ems], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": world * S * args.e2e_steps / (te.item() * 1e-3), "unit": UNIT,
+        e2e = {"value": job_rate(world, S, args.e2e_steps, max_over_ranks(ems, dev)), "unit": UNIT,
                "h2d_bytes_per_step": int(host[0].numel()), "d2h_bytes_per_step": 16,
                "steps": args.e2e_steps, "input": "pinned host uint8 BGR, normalisation fused into the gate",
                "modes_seen": sorted({int(m) for m in ring[:, 0].tolist()})}
@@ -387,7 +387,7 @@ def run_b200(args):
         dist.destroy_process_group()
     if rank != 0:
         return
-    value = world * S * args.steps / (ms_max * 1e-3)
+    value = job_rate(world, S, args.steps, ms_max)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
