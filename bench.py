@@ -83,6 +83,22 @@ def pingpong(n):
     return list(range(n)) + list(range(n - 2, 0, -1))
 
 
+def load_traffic(streams):
+    """DRAM bytes per launch measured by ncu (profiles/dram_traffic_8x1080p_5pct.md), scaled
+    from its 8-stream capture to `streams` (traffic grows with the active blocks); None
+    when the summary is absent."""
+    p = ROOT / "profiles" / "dram_traffic_8x1080p_5pct.md"
+    out = {}
+    if p.exists():
+        for line in p.read_text().splitlines():
+            line = line.strip()
+            for key in ("conv", "gate"):
+                tag = f"{key}_traffic_bytes_per_launch_8_streams:"
+                if line.startswith(tag):
+                    out[key] = float(line[len(tag):]) * streams / 8
+    return out
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -320,16 +336,20 @@ def run_b200(args):
         gbytes += gate_bytes(eng, int(eng.changed.sum().item()))
         nprof += 1
     peaks, src = load_peaks()
+    traffic = load_traffic(S)
     n_conv = nprof * len(eng.layers)
     conv_tflops = conv_flops / (prof["conv"] * 1e-3) / 1e12
     gate_gbs = gbytes / (prof["gate"] * 1e-3) / 1e9
     roof = {"bound": "tensor", "kernel": "sb::conv_tc_kernel (tile conv, all 11 layers)",
             "achieved": conv_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
             "frac": conv_tflops / peaks["bf16_tflops_sustained"],
-            "traffic": None, "peak_source": f"{src} bf16_tflops_sustained (fp16 dense = bf16 rate)",
+            "traffic": traffic.get("conv"), "traffic_source": "ncu dram__bytes_read+write per conv launch, "
+            "8-stream capture scaled to this stream count (profiles/dram_traffic_8x1080p_5pct.md)",
+            "peak_source": f"{src} bf16_tflops_sustained (fp16 dense = bf16 rate)",
             "flops_per_launch": conv_flops / n_conv, "ms_per_launch": prof["conv"] / n_conv}
     roof_gate = {"bound": "hbm", "kernel": "sb::gate_kernel<0>", "achieved": gate_gbs, "peak": peaks["hbm_gbs"],
                  "unit": "GB/s", "frac": gate_gbs / peaks["hbm_gbs"], "bytes_per_launch": gbytes / nprof,
+                 "traffic": traffic.get("gate"),
                  "ms_per_launch": prof["gate"] / nprof}
     share = {k: v / sum(prof.values()) for k, v in prof.items()}
 
