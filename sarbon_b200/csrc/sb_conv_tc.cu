@@ -41,6 +41,11 @@ constexpr int kMaxCout = 128;     // widest layer of the stem (bias staged in sh
 //          feeds the three kx taps;
 // WIN = 3: full windows -- regions of 8/T x 16/T blocks (8 px x 16 rows), one 10 x 18 px box
 //          per chunk feeds all nine taps.  Both window modes are for stride-1 layers.
+// WIN = 2: pair windows for stride-2 layers with 32 input channels: the input is viewed as
+//          pixel pairs (2 px x 32 ch = one 128-byte row); regions as WIN = 1 (8 output px x T
+//          rows); per ky one box of 10 pairs x T rows (row element stride 2) feeds two pair
+//          taps: pair offset -1 carries kx = 0 (odd pixel of the pair), offset 0 carries kx = 1
+//          (even) and kx = 2 (odd); the unused half of the offset -1 tap has zero weights.
 // PAIR = 1: a 2-CTA cluster runs M=256 cta_group::2 MMAs; each CTA holds NCTA of the
 //           2*NCTA output channels as its half of B and all 2*NCTA accumulator columns of
 //           its own 128 pixels.
@@ -48,10 +53,11 @@ template <int CIN, int NCTA, int T, int S, int WIN, int PAIR = 0>
 struct TcCfg {
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
-  static constexpr int CH = MANUAL ? KPAD : (CIN % 64 == 0 ? 64 : 32);  // K elements per K-block
-  static constexpr int NCH = MANUAL ? 1 : CIN / CH;
-  static constexpr int NKB = MANUAL ? 1 : (WIN == 3 ? 1 : WIN == 1 ? 3 : 9) * NCH;  // K-blocks per M-tile
-  static constexpr int NWKB = MANUAL ? 1 : 9 * NCH;   // weight K-blocks (tap-major)
+  // K elements per K-block (WIN = 2: a pair of input pixels x channels)
+  static constexpr int CH = MANUAL ? KPAD : WIN == 2 ? 2 * CIN : (CIN % 64 == 0 ? 64 : 32);
+  static constexpr int NCH = (MANUAL || WIN == 2) ? 1 : CIN / CH;
+  static constexpr int NKB = MANUAL ? 1 : (WIN == 3 ? 1 : (WIN == 1 || WIN == 2) ? 3 : 9) * NCH;  // per M-tile
+  static constexpr int NWKB = MANUAL ? 1 : WIN == 2 ? 6 : 9 * NCH;  // weight K-blocks
   static constexpr int ROWB = CH * 2;                 // bytes per operand row
   static constexpr int SWZ = ROWB == 128 ? 2 : 4;     // 128B / 64B swizzle
   static constexpr int SBO = 8 * ROWB;
@@ -122,7 +128,8 @@ struct TcCfg {
   static_assert(!MANUAL || ((NISS * SUB) % NGW == 0 && NWB % NGW == 0), "gather warp per stage / window slot");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
   static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256), "first-layer window box");
-  static_assert(!WIN || ((WIN == 1 || WIN == 3) && S == 1 && 8 % T == 0 && T <= 8 && ROWB == 128 && !MANUAL),
+  static_assert(!WIN || ((((WIN == 1 || WIN == 3) && S == 1) || (WIN == 2 && S == 2 && 2 * CIN == 64)) &&
+                         8 % T == 0 && T <= 8 && ROWB == 128 && !MANUAL),
                 "window mode geometry");
 };
 
@@ -296,7 +303,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           o.uy[j] = p.by;
           o.ux[j] = p.bx;
           o.cam[j] = p.cam;
-          o.y0[j] = (WIN ? p.by * C::RROWS : (p.by * T + sub * C::BOX_ROWS) * S) - 1;
+          o.y0[j] = (WIN ? p.by * C::RROWS * S : (p.by * T + sub * C::BOX_ROWS) * S) - 1;
           o.x0[j] = (WIN ? p.bx * 8 : p.bx * T * S) - 1;
         }
       };
@@ -549,16 +556,17 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
               // window taps: A = the window shifted by (ky*10 + kx) pixels (128 B rows; the
               // hardware swizzle follows absolute smem addresses), B = that tap's weights.
               // Row windows hold one ky per K-block, full windows all three.
-              constexpr int NKY = WIN == 3 ? 3 : 1;
+              // Pair windows: two pair taps per ky (weight blocks ky*2 + tap).
+              constexpr int NKY = WIN == 3 ? 3 : 1, NTX = WIN == 2 ? 2 : 3;
               const int ch = kb % C::NCH, ky0 = WIN == 3 ? 0 : kb / C::NCH;
 #pragma unroll
               for (int dy = 0; dy < NKY; ++dy)
 #pragma unroll
-                for (int kx = 0; kx < 3; ++kx)
+                for (int kx = 0; kx < NTX; ++kx)
 #pragma unroll
                   for (int kk = 0; kk < C::CH / 16; ++kk) {
                     const uint32_t a_off = ((WIN == 3 ? dy * 10 : 0) + kx) * C::ROWB + kk * 32;
-                    const uint32_t b_off = (((ky0 + dy) * 3 + kx) * C::NCH + ch) * C::B_KB + kk * 32;
+                    const uint32_t b_off = (WIN == 2 ? kb * 2 + kx : ((ky0 + dy) * 3 + kx) * C::NCH + ch) * C::B_KB + kk * 32;
                     if (PAIR)
                       mma_f16_ss2(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
                                   (kb | dy | kx | kk) != 0 ? 1u : 0u);
@@ -758,6 +766,7 @@ const std::vector<Variant>& variants() {
   static const std::vector<Variant> v = {
       // block 32
       make_variant<3, 32, 16, 2>(32),
+      make_variant<32, 64, 8, 2, 2>(64),       // pair windows over blocks
       make_variant<32, 64, 8, 2>(64),
       make_variant<64, 64, 8, 1, 1>(64),       // row windows over blocks
       make_variant<64, 64, 8, 1, 3>(64),       // full windows over 1x2-block regions
@@ -847,6 +856,33 @@ int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s) {
 void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_t* out) {
   const Variant* v = picked(cin, cout, t, s);
   if (!v) return;
+  if (v->win == 2) {
+    // pair windows: block ky*2 + tap; K element k = (dx, c) of a pixel pair; tap 0 (pair
+    // offset -1) holds kx = 0 in its odd half, tap 1 (offset 0) kx = 1 / kx = 2 in its halves
+    const int ncta = v->ncta, nsplit = cout / ncta, rowb = v->ch * 2;
+    const size_t split_elems = (size_t)v->w_bytes / 2;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      uint16_t* img = out + sp * split_elems;
+      std::memset(img, 0, (size_t)v->w_bytes);
+      for (int kb = 0; kb < 6; ++kb) {
+        const int ky = kb / 2, tap = kb % 2;
+        for (int n = 0; n < ncta; ++n) {
+          const int co = sp * ncta + n;
+          for (int k = 0; k < v->ch; ++k) {
+            const int dx = k / cin, c = k % cin;
+            const int kx = tap == 0 ? (dx == 1 ? 0 : -1) : 1 + dx;
+            const float val = kx < 0 ? 0.f : w[((size_t)(ky * 3 + kx) * cin + c) * cout + co];
+            const int q = (k * 2) / 16, within = (k * 2) % 16;
+            const int pq = q ^ (n & 7);
+            const size_t byte = (size_t)kb * ncta * rowb + (size_t)n * rowb + pq * 16 + within;
+            __half h = __float2half_rn(val);
+            img[byte / 2] = *reinterpret_cast<uint16_t*>(&h);
+          }
+        }
+      }
+    }
+    return;
+  }
   const bool manual = cin < 16;
   const int ch = v->ch, rowb = ch * 2, ncta = v->ncta, nsplit = cout / ncta;
   const int nch = manual ? 1 : cin / ch, nkb = manual ? 1 : 9 * nch;
@@ -920,6 +956,18 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
   }
   PFN_encodeTiled enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
+  if (v->win == 2) {
+    // pixel pairs: [pair = 2 px x cin][wx/2][hx][n]; rows taken with element stride 2
+    if (wx % 2 != 0 || 2 * cin != v->ch) return cudaErrorInvalidValue;
+    cuuint64_t pd[4] = {(cuuint64_t)2 * cin, (cuuint64_t)wx / 2, (cuuint64_t)hx, (cuuint64_t)n};
+    cuuint64_t ps[3] = {(cuuint64_t)cin * 4, (cuuint64_t)wx * cin * 2, (cuuint64_t)hx * wx * cin * 2};
+    cuuint32_t pb[4] = {(cuuint32_t)v->ch, 10u, (cuuint32_t)(v->box_rows * 2), 1};
+    cuuint32_t pe[4] = {1, 1, 2, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(src), pd, ps, pb, pe,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+  }
   cuuint64_t dims[4] = {(cuuint64_t)cin, (cuuint64_t)wx, (cuuint64_t)hx, (cuuint64_t)n};
   cuuint64_t strides[3] = {(cuuint64_t)cin * 2, (cuuint64_t)wx * cin * 2, (cuuint64_t)hx * wx * cin * 2};
   // window mode: 10 input px (8 output px + halo) x T rows; im2col: the strided tile itself
