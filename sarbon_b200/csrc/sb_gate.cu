@@ -6,6 +6,7 @@
 //   img update      _sparse      :155-160 (fused into the gate here)
 //   block lists     _sparse      :161-165 (nonzero_static: ascending flat order)
 //   dispatch        step         :214-240 (skip / sparse / dense + hysteresis)
+#include <algorithm>
 #include <cstdint>
 
 #include "sb_internal.cuh"
@@ -61,9 +62,9 @@ SB_DEV float absdiff2(uint32_t x, uint32_t y) {
   return f.x + f.y;
 }
 
-// Per-block change statistic.  One CTA per (block row, camera): reads the block row of
-// the new frames and of the image cache with 16-byte coalesced loads and sums |diff| per
-// block in fp32.  The fp32 sum of n non-negative terms is within (n-1)*2^-24 relative of
+// Per-block change statistic.  One CTA per (segment of a block row, camera): reads the
+// segment of the new frames and of the image cache with 16-byte coalesced loads (about one
+// 16-byte column per thread, all rows of the block) and sums |diff| per block in fp32.  The fp32 sum of n non-negative terms is within (n-1)*2^-24 relative of
 // the exact sum, so it decides `sum > thr` exactly unless it falls inside that band
 // around the threshold; only those (rare) blocks are re-summed exactly, in integer
 // multiples of 2^-24.  The result equals an exact comparison (the reference sums in fp32
@@ -72,16 +73,18 @@ SB_DEV float absdiff2(uint32_t x, uint32_t y) {
 template <int KIND>  // 0: fp16 frames, 1: fp32 frames, 2: uint8 BGR frames (fused prep)
 __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
   if (in_hysteresis(a.st)) return;  // hysteresis dense step: the gate is not looked at (:222-226)
-  const int by = blockIdx.x, cam = blockIdx.y;
+  // CTA = blocks [bx0, bx0 + nblk) of block row `by` of camera `cam` (a segment of the row)
+  const int by = blockIdx.x, cam = blockIdx.y, bx0 = blockIdx.z * a.seg;
+  const int nblk = min(a.seg, a.wb - bx0);
   const int B = a.block;
   extern __shared__ __align__(16) uint8_t gsm[];
   unsigned long long* s_sx = reinterpret_cast<unsigned long long*>(gsm);  // [wb] exact sums (or double)
-  float* s_sf = reinterpret_cast<float*>(s_sx + a.wb);                    // [wb] fp32 sums
-  uint32_t* s_flag = reinterpret_cast<uint32_t*>(s_sf + a.wb);           // [wb]
-  int* s_amb = reinterpret_cast<int*>(s_flag + a.wb);                    // [wb] ambiguous blocks
-  __half* s_lut = reinterpret_cast<__half*>(s_amb + a.wb);               // [3][256] (u8 path)
+  float* s_sf = reinterpret_cast<float*>(s_sx + a.seg);                   // [seg] fp32 sums
+  uint32_t* s_flag = reinterpret_cast<uint32_t*>(s_sf + a.seg);          // [seg]
+  int* s_amb = reinterpret_cast<int*>(s_flag + a.seg);                   // [seg] ambiguous blocks
+  __half* s_lut = reinterpret_cast<__half*>(s_amb + a.seg);              // [3][256] (u8 path)
   __shared__ int s_namb;
-  for (int i = threadIdx.x; i < a.wb; i += blockDim.x) {
+  for (int i = threadIdx.x; i < nblk; i += blockDim.x) {
     s_sx[i] = 0ull;
     s_sf[i] = 0.f;
     s_flag[i] = 0u;
@@ -98,13 +101,14 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
   __syncthreads();
 
   const size_t row_px = (size_t)a.w;
-  const size_t img_row0 = ((size_t)cam * a.h + (size_t)by * B) * row_px * 3;  // element index
+  // element index of the segment's first pixel; rows stay row_px * 3 elements apart
+  const size_t img_row0 = (((size_t)cam * a.h + (size_t)by * B) * row_px + (size_t)bx0 * B) * 3;
   if (KIND == 0) {
     // 16 B = 8 halves; a block row-segment is B*3*2/16 vectors
-    const int vpb = B * 3 / 8, vpr = vpb * a.wb;
+    const int vpb = B * 3 / 8, vpr = vpb * a.wb;  // vectors per block, per image row
     const uint4* f = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.frames) + img_row0);
     const uint4* g = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.img) + img_row0);
-    for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+    for (int v = threadIdx.x; v < vpb * nblk; v += blockDim.x) {
       float acc = 0.f;
 #pragma unroll 8
       for (int r = 0; r < B; ++r) {
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
     const float4* f = reinterpret_cast<const float4*>(static_cast<const float*>(a.frames) + img_row0);
     const float4* g = reinterpret_cast<const float4*>(static_cast<const float*>(a.img) + img_row0);
     double* s_d = reinterpret_cast<double*>(s_sx);
-    for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+    for (int v = threadIdx.x; v < vpb * nblk; v += blockDim.x) {
       double acc = 0.0;
 #pragma unroll 4
       for (int r = 0; r < B; ++r) {
@@ -133,10 +137,10 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
     }
   } else {
     // uint8 BGR: units of 16 pixels = 48 bytes of frame, 96 bytes of fp16 cache
-    const int upb = B / 16, upr = upb * a.wb;
+    const int upb = B / 16;
     const uint8_t* f = static_cast<const uint8_t*>(a.frames) + img_row0;
     const __half* g = static_cast<const __half*>(a.img) + img_row0;
-    for (int u = threadIdx.x; u < upr; u += blockDim.x) {
+    for (int u = threadIdx.x; u < upb * nblk; u += blockDim.x) {
       float acc = 0.f;
 #pragma unroll 2
       for (int r = 0; r < B; ++r) {
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
   __syncthreads();
 
   // classify with the fp32 sums; collect the blocks inside the rounding band
-  for (int bx = threadIdx.x; bx < a.wb; bx += blockDim.x) {
+  for (int bx = threadIdx.x; bx < nblk; bx += blockDim.x) {
     uint32_t cls;  // 0 unchanged, 1 changed, 2 ambiguous
     if (KIND == 1) {
       cls = reinterpret_cast<double*>(s_sx)[bx] > a.thr ? 1u : 0u;
@@ -236,8 +240,8 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
 
   // extra + refresh (fused_engine.py:144-148)
   const int64_t tick = a.st->tick;
-  for (int bx = threadIdx.x; bx < a.wb; bx += blockDim.x) {
-    const int64_t lin = ((int64_t)cam * a.hb + by) * a.wb + bx;
+  for (int bx = threadIdx.x; bx < nblk; bx += blockDim.x) {
+    const int64_t lin = ((int64_t)cam * a.hb + by) * a.wb + bx0 + bx;
     bool ch = s_flag[bx] == 1u;
     ch = ch || a.extra[lin] != 0;
     if (a.refresh) ch = ch || (lin % a.refresh) == (tick % a.refresh);
@@ -248,10 +252,10 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
 
   // image-cache update for changed blocks (fused_engine.py:157-160)
   if (KIND == 2) {
-    const int upb = B / 16, upr = upb * a.wb;
+    const int upb = B / 16;
     const uint8_t* f = static_cast<const uint8_t*>(a.frames) + img_row0;
     __half* g = static_cast<__half*>(a.img) + img_row0;
-    for (int u = threadIdx.x; u < upr; u += blockDim.x) {
+    for (int u = threadIdx.x; u < upb * nblk; u += blockDim.x) {
       if (!s_flag[u / upb]) continue;
       for (int r = 0; r < B; ++r) {
         const uint4* fp = reinterpret_cast<const uint4*>(f + (size_t)r * row_px * 3 + (size_t)u * 48);
@@ -275,7 +279,7 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
     const int vpb = B * 3 * esz / 16, vpr = vpb * a.wb;
     const uint4* f = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.frames) + img_row0 * esz);
     uint4* g = reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.img) + img_row0 * esz);
-    for (int v = threadIdx.x; v < vpr; v += blockDim.x) {
+    for (int v = threadIdx.x; v < vpb * nblk; v += blockDim.x) {
       if (!s_flag[v / vpb]) continue;
 #pragma unroll 4
       for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
@@ -545,9 +549,14 @@ __global__ void set_mode_kernel(State* st, int mode, int reset_hyst, int64_t for
 }
 
 // ---------------------------------------------------------------- launchers
-cudaError_t launch_gate(const GateArgs& a, int kind, cudaStream_t s) {
-  dim3 grid(a.hb, a.n);
-  const size_t smem = (size_t)a.wb * (8 + 4 + 4 + 4) + 768 * 2 + 16;
+cudaError_t launch_gate(const GateArgs& a_in, int kind, cudaStream_t s) {
+  // row segments of about one 16-byte column per thread (fp16 / fp32 frames); the uint8
+  // path keeps whole block rows (its 48-byte units give few threads per block)
+  GateArgs a = a_in;
+  const int per_block = kind == 0 ? a.block * 3 / 8 : kind == 1 ? a.block * 3 / 4 : a.wb * a.block;
+  a.seg = kind == 2 ? a.wb : std::max(1, std::min(a.wb, 256 / std::max(1, per_block)));
+  dim3 grid(a.hb, a.n, (a.wb + a.seg - 1) / a.seg);
+  const size_t smem = (size_t)a.seg * (8 + 4 + 4 + 4) + 768 * 2 + 16;
   switch (kind) {
     case 0: gate_kernel<0><<<grid, 256, smem, s>>>(a); break;
     case 1: gate_kernel<1><<<grid, 256, smem, s>>>(a); break;

@@ -48,6 +48,7 @@ struct GateArgs {
   uint8_t* changed;        // [N][Hb][Wb]
   State* st;
   int n, h, w, hb, wb, block;
+  int seg;                 // blocks per CTA along the block row (set by launch_gate)
   int64_t thr_fx;          // floor(threshold * 2^24) (fp16/u8 paths); -1: always; INT64_MAX: never
   double thr;              // threshold as a double (fp32 path)
   double band_lo, band_hi; // fp32 sums outside [band_lo, band_hi] decide `sum > thr` exactly
