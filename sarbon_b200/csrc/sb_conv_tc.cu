@@ -41,11 +41,14 @@ constexpr int kMaxCout = 128;     // widest layer of the stem (bias staged in sh
 //          feeds the three kx taps;
 // WIN = 3: full windows -- regions of 8/T x 16/T blocks (8 px x 16 rows), one 10 x 18 px box
 //          per chunk feeds all nine taps.  Both window modes are for stride-1 layers.
-// WIN = 2: pair windows for stride-2 layers with 32 input channels: the input is viewed as
-//          pixel pairs (2 px x 32 ch = one 128-byte row); regions as WIN = 1 (8 output px x T
-//          rows); per ky one box of 10 pairs x T rows (row element stride 2) feeds two pair
+// WIN = 2: strided windows for stride-2 layers; regions as WIN = 1 (8 output px x T rows).
+//          32 input channels: the input is viewed as pixel pairs (2 px x 32 ch = one 128-byte
+//          row); per ky one box of 10 pairs x T rows (row element stride 2) feeds two pair
 //          taps: pair offset -1 carries kx = 0 (odd pixel of the pair), offset 0 carries kx = 1
 //          (even) and kx = 2 (odd); the unused half of the offset -1 tap has zero weights.
+//          64 input channels: per ky two boxes of 10 px x T rows with element stride 2 in x
+//          and y, starting at the odd (2*x0 - 1) and even (2*x0 - 2) input column: the odd box
+//          feeds kx = 0 (offset 0) and kx = 2 (offset 1), the even box kx = 1 (offset 1).
 // PAIR = 1: a 2-CTA cluster runs M=256 cta_group::2 MMAs; each CTA holds NCTA of the
 //           2*NCTA output channels as its half of B and all 2*NCTA accumulator columns of
 //           its own 128 pixels.
@@ -54,10 +57,12 @@ struct TcCfg {
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
   // K elements per K-block (WIN = 2: a pair of input pixels x channels)
-  static constexpr int CH = MANUAL ? KPAD : WIN == 2 ? 2 * CIN : (CIN % 64 == 0 ? 64 : 32);
+  static constexpr int CH = MANUAL ? KPAD : WIN == 2 ? 64 : (CIN % 64 == 0 ? 64 : 32);
   static constexpr int NCH = (MANUAL || WIN == 2) ? 1 : CIN / CH;
+  // WIN = 2 with 64 channels: two boxes per K-block (odd and even input columns)
+  static constexpr int NBOX = (WIN == 2 && CIN == 64) ? 2 : 1;
   static constexpr int NKB = MANUAL ? 1 : (WIN == 3 ? 1 : (WIN == 1 || WIN == 2) ? 3 : 9) * NCH;  // per M-tile
-  static constexpr int NWKB = MANUAL ? 1 : WIN == 2 ? 6 : 9 * NCH;  // weight K-blocks
+  static constexpr int NWKB = MANUAL ? 1 : WIN == 2 ? (CIN == 32 ? 6 : 9) : 9 * NCH;  // weight K-blocks
   static constexpr int ROWB = CH * 2;                 // bytes per operand row
   static constexpr int SWZ = ROWB == 128 ? 2 : 4;     // 128B / 64B swizzle
   static constexpr int SBO = 8 * ROWB;
@@ -71,7 +76,7 @@ struct TcCfg {
   static constexpr int BOX_ROWS = WIN == 3 ? 18 : WIN ? T : (TT >= 128 ? 128 / T : T);
   static constexpr int BOX_BYTES = WIN ? 10 * BOX_ROWS * ROWB : T * BOX_ROWS * ROWB;
   static constexpr int WSBO = 10 * ROWB;                // window modes: stride between output rows
-  static constexpr int A_BYTES = WIN ? TPM * BOX_BYTES : 128 * ROWB;  // bytes the TMA boxes of a stage deliver
+  static constexpr int A_BYTES = WIN ? NBOX * TPM * BOX_BYTES : 128 * ROWB;  // bytes a stage's boxes deliver
   static constexpr int A_STAGE = ((A_BYTES + 1023) / 1024) * 1024;     // stage stride (1024-aligned)
   static constexpr int B_KB = NCTA * ROWB;
   static constexpr int W_BYTES = NWKB * B_KB;
@@ -128,7 +133,7 @@ struct TcCfg {
   static_assert(!MANUAL || ((NISS * SUB) % NGW == 0 && NWB % NGW == 0), "gather warp per stage / window slot");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
   static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256), "first-layer window box");
-  static_assert(!WIN || ((((WIN == 1 || WIN == 3) && S == 1) || (WIN == 2 && S == 2 && 2 * CIN == 64)) &&
+  static_assert(!WIN || ((((WIN == 1 || WIN == 3) && S == 1) || (WIN == 2 && S == 2 && (CIN == 32 || CIN == 64))) &&
                          8 % T == 0 && T <= 8 && ROWB == 128 && !MANUAL),
                 "window mode geometry");
 };
@@ -383,15 +388,19 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
               const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
               if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::A_BYTES);
 #pragma unroll
-              for (int j = 0; j < C::TPM; ++j)
-                tma_load_4d_pair(dst + j * C::BOX_BYTES, &tmap, fb, ch * C::CH, cc.x0[j] + kx, cc.y0[j] + ky,
-                                 cc.cam[j]);
+              for (int bs = 0; bs < C::NBOX; ++bs)
+#pragma unroll
+                for (int j = 0; j < C::TPM; ++j)
+                  tma_load_4d_pair(dst + (bs * C::TPM + j) * C::BOX_BYTES, &tmap, fb, ch * C::CH,
+                                   C::NBOX == 2 ? 2 * cc.x0[j] + 1 - bs : cc.x0[j] + kx, cc.y0[j] + ky, cc.cam[j]);
             } else {
               mbar_arrive_expect_tx(&full[s], C::A_BYTES);
 #pragma unroll
-              for (int j = 0; j < C::TPM; ++j)
-                tma_load_4d(dst + j * C::BOX_BYTES, &tmap, &full[s], ch * C::CH, cc.x0[j] + kx, cc.y0[j] + ky,
-                            cc.cam[j]);
+              for (int bs = 0; bs < C::NBOX; ++bs)
+#pragma unroll
+                for (int j = 0; j < C::TPM; ++j)
+                  tma_load_4d(dst + (bs * C::TPM + j) * C::BOX_BYTES, &tmap, &full[s], ch * C::CH,
+                              C::NBOX == 2 ? 2 * cc.x0[j] + 1 - bs : cc.x0[j] + kx, cc.y0[j] + ky, cc.cam[j]);
             }
           }
           __syncwarp();
@@ -557,7 +566,9 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
               // hardware swizzle follows absolute smem addresses), B = that tap's weights.
               // Row windows hold one ky per K-block, full windows all three.
               // Pair windows: two pair taps per ky (weight blocks ky*2 + tap).
-              constexpr int NKY = WIN == 3 ? 3 : 1, NTX = WIN == 2 ? 2 : 3;
+              // 64-channel strided windows: taps t = 0, 1, 2 are (odd box, offset 0) kx = 0,
+              // (odd box, offset 1) kx = 2 and (even box, offset 1) kx = 1.
+              constexpr int NKY = WIN == 3 ? 3 : 1, NTX = WIN == 2 ? (C::NBOX == 2 ? 3 : 2) : 3;
               const int ch = kb % C::NCH, ky0 = WIN == 3 ? 0 : kb / C::NCH;
 #pragma unroll
               for (int dy = 0; dy < NKY; ++dy)
@@ -565,8 +576,13 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
                 for (int kx = 0; kx < NTX; ++kx)
 #pragma unroll
                   for (int kk = 0; kk < C::CH / 16; ++kk) {
-                    const uint32_t a_off = ((WIN == 3 ? dy * 10 : 0) + kx) * C::ROWB + kk * 32;
-                    const uint32_t b_off = (WIN == 2 ? kb * 2 + kx : ((ky0 + dy) * 3 + kx) * C::NCH + ch) * C::B_KB + kk * 32;
+                    constexpr int SLOT = C::TPM * C::BOX_BYTES;
+                    const uint32_t a_off = C::NBOX == 2
+                                               ? (kx == 2 ? SLOT : 0) + (kx == 0 ? 0 : 1) * C::ROWB + kk * 32
+                                               : ((WIN == 3 ? dy * 10 : 0) + kx) * C::ROWB + kk * 32;
+                    const int wk = C::NBOX == 2 ? kb * 3 + (kx == 0 ? 0 : kx == 1 ? 2 : 1)
+                                   : WIN == 2 ? kb * 2 + kx : ((ky0 + dy) * 3 + kx) * C::NCH + ch;
+                    const uint32_t b_off = wk * C::B_KB + kk * 32;
                     if (PAIR)
                       mma_f16_ss2(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
                                   (kb | dy | kx | kk) != 0 ? 1u : 0u);
@@ -770,6 +786,7 @@ const std::vector<Variant>& variants() {
       make_variant<32, 64, 8, 2>(64),
       make_variant<64, 64, 8, 1, 1>(64),       // row windows over blocks
       make_variant<64, 64, 8, 1, 3>(64),       // full windows over 1x2-block regions
+      make_variant<64, 64, 4, 2, 2, 1>(128),   // CTA pairs, strided windows over 2x1-block regions
       make_variant<64, 64, 4, 2, 0, 1>(128),   // CTA pairs: M=256, N=128
       make_variant<64, 128, 4, 2>(128),
       make_variant<128, 64, 4, 1, 1, 1>(128),  // CTA pairs, row windows over horizontal block pairs
@@ -780,6 +797,7 @@ const std::vector<Variant>& variants() {
       make_variant<3, 32, 32, 2>(32),
       make_variant<32, 64, 16, 2>(64),
       make_variant<64, 64, 16, 1>(64),
+      make_variant<64, 64, 8, 2, 2, 1>(128),
       make_variant<64, 64, 8, 2, 0, 1>(128),
       make_variant<64, 128, 8, 2>(128),
       make_variant<128, 64, 8, 1, 3, 1>(128),  // CTA pairs, full windows over 1x2-block regions
@@ -856,7 +874,7 @@ int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s) {
 void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_t* out) {
   const Variant* v = picked(cin, cout, t, s);
   if (!v) return;
-  if (v->win == 2) {
+  if (v->win == 2 && cin == 32) {
     // pair windows: block ky*2 + tap; K element k = (dx, c) of a pixel pair; tap 0 (pair
     // offset -1) holds kx = 0 in its odd half, tap 1 (offset 0) kx = 1 / kx = 2 in its halves
     const int ncta = v->ncta, nsplit = cout / ncta, rowb = v->ch * 2;
@@ -956,6 +974,17 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
   }
   PFN_encodeTiled enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
+  if (v->win == 2 && cin == 64) {
+    // strided windows: plain pixels, element stride 2 in x and y, 10 px x box_rows per box
+    cuuint64_t pd[4] = {(cuuint64_t)cin, (cuuint64_t)wx, (cuuint64_t)hx, (cuuint64_t)n};
+    cuuint64_t ps[3] = {(cuuint64_t)cin * 2, (cuuint64_t)wx * cin * 2, (cuuint64_t)hx * wx * cin * 2};
+    cuuint32_t pb[4] = {(cuuint32_t)v->ch, 20u, (cuuint32_t)(v->box_rows * 2), 1};
+    cuuint32_t pe[4] = {1, 2, 2, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(src), pd, ps, pb, pe,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+  }
   if (v->win == 2) {
     // pixel pairs: [pair = 2 px x cin][wx/2][hx][n]; rows taken with element stride 2
     if (wx % 2 != 0 || 2 * cin != v->ch) return cudaErrorInvalidValue;
