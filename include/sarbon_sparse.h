@@ -134,6 +134,10 @@ SB_API int sb_set_extra(sb_engine* e, const uint8_t* mask_dev, void* stream);
 /* Set the dense-fallback crossover (fused_engine.py:89, written by calibrate
  * :242-275) and the hysteresis period (:91). */
 SB_API int sb_set_fallback(sb_engine* e, int64_t fallback, void* stream);
+/* Change threshold `tau` (mean |diff| per block) for the steps launched after this call;
+ * host-side only.  Replaces the per-call `tau` of the M0 engine's step
+ * (block_sparse.py:253,323-326) and `update`'s given mask (tau = +inf, block_sparse.py:213). */
+SB_API int sb_set_tau(sb_engine* e, double tau);
 SB_API int sb_set_dense_check_every(sb_engine* e, int n, void* stream);
 
 /* Calibration support (fused_engine.py:261-264): run the conv sequence over

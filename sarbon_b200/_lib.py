@@ -59,6 +59,7 @@ PROTOTYPES = {
     "sb_result_ptr": (_I, [_P, C.POINTER(_P)]),
     "sb_set_extra": (_I, [_P, _P, _P]),
     "sb_set_fallback": (_I, [_P, _I64, _P]),
+    "sb_set_tau": (_I, [_P, C.c_double]),
     "sb_set_dense_check_every": (_I, [_P, _I, _P]),
     "sb_run_sparse_forced": (_I, [_P, _P, _I64, _P]),
     "sb_cache_ptr": (_I, [_P, _I, C.POINTER(_P), C.POINTER(_I64)]),

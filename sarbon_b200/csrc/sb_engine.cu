@@ -126,6 +126,30 @@ int alloc_dev(sb_engine* e, void** p, size_t bytes) {
   return SB_OK;
 }
 
+// Gate threshold from tau: float32(tau * block * block * 3), compared as torch does
+// (fused_engine.py:144), as an exact fixed-point value and as the fp32 rounding band.
+void set_threshold(sb_engine* e, double tau) {
+  e->tau = tau;
+  const float thr32 = (float)(tau * e->block * e->block * 3);
+  e->thr = (double)thr32;
+  if (std::isnan(thr32)) e->thr_fx = INT64_MAX;
+  else if (thr32 < 0.f) e->thr_fx = -1;
+  else if (std::isinf(thr32) || (double)thr32 * 16777216.0 >= 9.0e18) e->thr_fx = INT64_MAX;
+  else e->thr_fx = (int64_t)std::floor((double)thr32 * 16777216.0);
+  if (std::isnan(thr32)) e->thr = INFINITY;  // sum > NaN is false for every block
+  // A recursive fp32 sum of n non-negative fp16 terms is within (n-1)*2^-24 relative of the
+  // exact sum (any order); twice that margin decides the comparison from the fp32 sum.
+  const double gam = 2.0 * 3.0 * e->block * e->block * std::ldexp(1.0, -24);
+  if (std::isnan(thr32) || std::isinf(thr32) && thr32 > 0) {
+    e->band_lo = e->band_hi = INFINITY;                // only inf / NaN sums reach the exact path
+  } else if (thr32 < 0.f) {
+    e->band_lo = e->band_hi = -1.0;                    // every block changes
+  } else {
+    e->band_lo = (double)thr32 * (1.0 - gam);
+    e->band_hi = (double)thr32 * (1.0 + gam);
+  }
+}
+
 int launch_convs(sb_engine* e, cudaStream_t s) {
   for (int i = 0; i < e->n_layers; ++i) {
     const sb_layer_desc& L = e->layers[i];
@@ -341,25 +365,7 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
   e->tau = tau;
   e->refresh = refresh;
   e->n_layers = n_layers;
-  // threshold = float32(tau * block * block * 3), compared as torch does (fused_engine.py:144)
-  const float thr32 = (float)(tau * block * block * 3);
-  e->thr = (double)thr32;
-  if (std::isnan(thr32)) e->thr_fx = INT64_MAX;
-  else if (thr32 < 0.f) e->thr_fx = -1;
-  else if (std::isinf(thr32) || (double)thr32 * 16777216.0 >= 9.0e18) e->thr_fx = INT64_MAX;
-  else e->thr_fx = (int64_t)std::floor((double)thr32 * 16777216.0);
-  if (std::isnan(thr32)) e->thr = INFINITY;  // sum > NaN is false for every block
-  // A recursive fp32 sum of n non-negative fp16 terms is within (n-1)*2^-24 relative of the
-  // exact sum (any order); twice that margin decides the comparison from the fp32 sum.
-  const double gam = 2.0 * 3.0 * block * block * std::ldexp(1.0, -24);
-  if (std::isnan(thr32) || std::isinf(thr32) && thr32 > 0) {
-    e->band_lo = e->band_hi = INFINITY;                // only inf / NaN sums reach the exact path
-  } else if (thr32 < 0.f) {
-    e->band_lo = e->band_hi = -1.0;                    // every block changes
-  } else {
-    e->band_lo = (double)thr32 * (1.0 - gam);
-    e->band_hi = (double)thr32 * (1.0 + gam);
-  }
+  set_threshold(e, tau);
   // caches: id 0 = image, id i+1 = layer i output
   e->shape[0][0] = n_streams;
   e->shape[0][1] = height;
@@ -562,6 +568,12 @@ int sb_set_fallback(sb_engine* e, int64_t fallback, void* stream) {
   if (!e) return fail(SB_EINVAL, "null engine");
   set_i64_kernel<<<1, 1, 0, (cudaStream_t)stream>>>(&e->st->fallback, fallback);
   SB_CUDA(cudaGetLastError());
+  return SB_OK;
+}
+
+int sb_set_tau(sb_engine* e, double tau) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  set_threshold(e, tau);
   return SB_OK;
 }
 

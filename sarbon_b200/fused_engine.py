@@ -195,6 +195,12 @@ class FusedSparseEngine:
         self._fallback = int(v)
         check(lib().sb_set_fallback(self._h.ptr, int(v), self._stream()), "sb_set_fallback")
 
+    def set_tau(self, tau):
+        """Change threshold for the steps launched after this call (mean |diff| per block;
+        an extension: the reference fixes `tau` at construction)."""
+        self.tau = float(tau)
+        check(lib().sb_set_tau(self._h.ptr, float(tau)), "sb_set_tau")
+
     @property
     def dense_check_every(self):
         return self._dense_check_every

@@ -250,3 +250,28 @@ def test_multistream_equals_single_streams():
     for i, e in enumerate(singles):
         for o in ("t7", "t14"):
             assert torch.equal(big.cache[o][i], e.cache[o][0]), (i, o)
+
+
+def test_calibrate_restores_caches_and_sets_crossover():
+    """calibrate() (fused_engine.py:242-275): times every budget bucket against the dense
+    pass, sets `fallback` to the last bucket before two slower-than-dense buckets in a row,
+    and leaves the caches exactly as they were."""
+    from sarbon_b200 import FusedSparseEngine, LocalBackbone, scenes
+    torch.manual_seed(3)
+    net = LocalBackbone().eval()
+    eng = FusedSparseEngine(net, 2, 256, 384, dtype=torch.float16, tau=0.05)
+    src = scenes.Streams(2, 256, 384, seed=4, n_rects=2, device="cuda")
+    eng.reset(scenes.normalise(src.next()))
+    eng.step(scenes.normalise(src.next()))
+    before = {k: v.clone() for k, v in eng.cache.items()}
+    table = eng.calibrate(reps=3)
+    buckets = [b for b, _, _ in table]
+    assert buckets == sorted(buckets) and len(buckets) >= 1
+    assert set(buckets) <= {eng._bucket(x) for x in eng.buckets}
+    assert all(ms > 0 and ratio > 0 for _, ms, ratio in table)
+    assert eng.fallback == 0 or eng.fallback in buckets
+    for k, v in eng.cache.items():
+        assert torch.equal(v, before[k]), k
+    # the engine still steps normally with the calibrated crossover
+    mode, k = eng.step(scenes.normalise(src.next()))
+    assert mode in ("skip", "sparse", "dense")

@@ -133,3 +133,27 @@ def test_normalise_matches_prep_formula():
     std = np.array([0.229, 0.224, 0.225], np.float32) * 255
     ref = ((u.numpy().astype(np.float32) - mean) / std).astype(np.float16).astype(np.float32)
     np.testing.assert_array_equal(got, ref)
+
+
+def test_m0_helpers_on_cpu():
+    """BlockSparseEngine's host helpers (block_sparse.py:115-119,181-192,323-326)."""
+    import math
+    import torch
+    from sarbon_b200 import LocalBackbone
+    from sarbon_b200.block_sparse import BlockSparseEngine, _bucket
+    assert [_bucket(n) for n in (0, 1, 16, 17, 33, 100, 1024)] == [16, 16, 16, 32, 64, 128, 1024]
+    eng = BlockSparseEngine(LocalBackbone(), 32)
+    assert eng.dilation(1) == 1 and eng.dilation(32) == 1 and eng.dilation(33) == 2 and eng.dilation(0) == 0
+    g = torch.Generator().manual_seed(0)
+    prev = torch.rand(3, 64, 96, generator=g)
+    cur = prev.clone()
+    cur[:, 0:32, 32:64] += 0.25           # block (0, 1) changes by mean 0.25
+    ch = eng.changed_blocks(cur, prev, tau=0.2)
+    assert ch.tolist() == [[False, True, False], [False, False, False]]
+    assert not eng.changed_blocks(cur, prev, tau=0.3).any()
+    act = eng.active_blocks(ch, 33)       # d = 2: the whole 2x3 grid
+    assert bool(act.all())
+    act1 = eng.active_blocks(ch, 10)      # d = 1: 3x3 neighbourhood of (0, 1)
+    assert act1.tolist() == [[True, True, True], [True, True, True]]
+    act0 = eng.active_blocks(ch, 0)       # d = 0: the block itself
+    assert act0.tolist() == ch.tolist()
