@@ -262,6 +262,20 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   const uint32_t tmem_base = *tmem_holder;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
 
+  // This CTA's weight slice is constant during a step: its bulk copy starts before the wait
+  // for the previous kernel of the stream (programmatic dependent launch).  Everything the
+  // earlier kernels write -- device state, lists, caches -- is read only after the wait.
+  if (warp == C::PROD_WARP && lane == 0) {
+    const int wsplit = PAIR ? (int)rank : (int)blockIdx.x % (a.cout / NCTA);
+    const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)wsplit * C::W_BYTES;
+    mbar_arrive_expect_tx(wfull, C::W_BYTES);
+    for (int off = 0; off < C::W_BYTES; off += 32768) {
+      const int len = C::W_BYTES - off < 32768 ? C::W_BYTES - off : 32768;
+      bulk_load(sW + off, wsrc + off, len, wfull);
+    }
+  }
+  grid_dep_wait();
+
   // work of this launch, decided on the device (no host sync)
   const int mode = a.st->mode_cur;
   const int listed = (WIN && a.rkind >= 0) ? a.st->rcounts[a.rkind][a.d_idx] : a.st->counts[a.d_idx];
@@ -330,16 +344,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           }
           __syncwarp();
         }
-        if (nload == 0) {  // the CTA's C_out slice never changes: weights are loaded once
-          const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)w.split * C::W_BYTES;
-          if (leader) {
-            mbar_arrive_expect_tx(wfull, C::W_BYTES);
-            for (int off = 0; off < C::W_BYTES; off += 32768) {
-              const int len = C::W_BYTES - off < 32768 ? C::W_BYTES - off : 32768;
-              bulk_load(sW + off, wsrc + off, len, wfull);
-            }
-          }
-          __syncwarp();
+        if (nload == 0) {  // the weights were issued in the prologue
           ++nload;
           if (PAIR && rank == 1) {  // tell the leader that this CTA's half of B is resident
             if (!warp_wait(wfull, 0, abort_flag)) {
@@ -747,6 +752,12 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       }
     }
   }
+  // the weight copy has landed before the CTA may exit (also when it had no items)
+  if (warp == C::PROD_WARP) {
+    volatile int never = 0;
+    warp_wait(wfull, 0, &never);
+  }
+  grid_dep_launch();  // the next kernel of the stream may start its prologue on free SMs
   tc_fence_before();
   __syncthreads();
   if (PAIR) cluster_sync();  // both CTAs are done with TMEM and with each other's barriers
@@ -1028,17 +1039,19 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
   if (v->pair) {
     // 2-CTA clusters, as many as can be resident at once (the loop over M-tile pairs is
     // persistent, so every cluster must be running)
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(v->threads, 1, 1);
     cfg.dynamicSmemBytes = v->smem;
     cfg.stream = st;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1;  // occupancy query with the cluster shape only
     static int max_clusters[32] = {};
     if (max_clusters[idx] == 0) {
       cfg.gridDim = dim3(2 * (grid_x / 2 > 0 ? grid_x / 2 : 1), 1, 1);
@@ -1050,6 +1063,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
     if (pairs > max_clusters[idx]) pairs = max_clusters[idx];
     if (pairs < 1) pairs = 1;
     cfg.gridDim = dim3(2 * pairs, 1, 1);
+    cfg.numAttrs = 2;  // + programmatic dependent launch
     return cudaLaunchKernelEx(&cfg, v->fn, a, *map);
   }
   // each CTA keeps one C_out slice: the grid is a multiple of the number of slices
@@ -1057,9 +1071,19 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
   int gx = grid_x * occ[idx];
   gx -= gx % nsplit;
   if (gx < nsplit) gx = nsplit;
-  dim3 grid(gx, 1);
-  v->fn<<<grid, v->threads, v->smem, st>>>(a, *map);
-  return cudaGetLastError();
+  // programmatic dependent launch: the kernel's prologue and weight copy overlap the tail of
+  // the previous kernel of the stream (the kernel waits for it before reading its outputs)
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(gx, 1, 1);
+  cfg.blockDim = dim3(v->threads, 1, 1);
+  cfg.dynamicSmemBytes = v->smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, v->fn, a, *map);
 }
 
 }  // namespace sb
