@@ -72,6 +72,7 @@ SB_DEV float absdiff2(uint32_t x, uint32_t y) {
 // changed blocks of the new frames are copied into the image cache.
 template <int KIND>  // 0: fp16 frames, 1: fp32 frames, 2: uint8 BGR frames (fused prep)
 __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
+  grid_dep_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   if (in_hysteresis(a.st)) return;  // hysteresis dense step: the gate is not looked at (:222-226)
   // CTA = blocks [bx0, bx0 + nblk) of block row `by` of camera `cam` (a segment of the row)
   const int by = blockIdx.x, cam = blockIdx.y, bx0 = blockIdx.z * a.seg;
@@ -285,6 +286,7 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
       for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
     }
   }
+  grid_dep_launch();
 }
 
 // ---------------------------------------------------------------- dilation + ordered lists
@@ -349,6 +351,7 @@ SB_DEV uint32_t lookback(unsigned long long* stat, uint32_t chunk, uint32_t epoc
 }
 
 __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
+  grid_dep_wait();
   State* st = a.st;
   if (in_hysteresis(st)) {  // hysteresis dense step: no gate, count -1 (fused_engine.py:222-226)
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -462,12 +465,14 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
     st->count_cur = k;
     st->mode_cur = k == 0 ? SB_MODE_SKIP : (k <= st->fallback ? SB_MODE_SPARSE : SB_MODE_DENSE);
   }
+  grid_dep_launch();
 }
 
 // ---------------------------------------------------------------- img copies
 // Dense: img <- frames for every block when this step is dense (fused_engine.py:173).
 // Masked (calibration replays): img <- frames where `changed` (:157-160).
 __global__ void __launch_bounds__(256) copy_kernel(CopyArgs a) {
+  grid_dep_wait();
   const int mode = a.st->mode_cur;
   if (a.changed == nullptr && mode != SB_MODE_DENSE) return;
   const int by = blockIdx.x, cam = blockIdx.y, B = a.block;
@@ -512,11 +517,13 @@ __global__ void __launch_bounds__(256) copy_kernel(CopyArgs a) {
       for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
     }
   }
+  grid_dep_launch();
 }
 
 // ---------------------------------------------------------------- state machine
 // End of a step (fused_engine.py:222-240): tick, hysteresis, stats, result slot.
 __global__ void finalize_kernel(State* st, int refresh, int32_t* host_out) {
+  grid_dep_wait();
   if (threadIdx.x != 0) return;
   const int mode = st->mode_cur;
   if (in_hysteresis(st)) {
@@ -538,6 +545,7 @@ __global__ void finalize_kernel(State* st, int refresh, int32_t* host_out) {
     host_out[2] = st->error;
     host_out[3] = 1;  // written
   }
+  grid_dep_launch();
 }
 
 // Reset / dense replay / calibration: force the mode of the conv sequence.
@@ -549,6 +557,25 @@ __global__ void set_mode_kernel(State* st, int mode, int reset_hyst, int64_t for
 }
 
 // ---------------------------------------------------------------- launchers
+namespace {
+// Launch with programmatic stream serialisation: the kernel may be scheduled before the
+// previous kernel of the stream completes and waits for it with griddepcontrol.wait.
+template <typename... Args>
+cudaError_t launch_pdl(void (*k)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+}  // namespace
+
 cudaError_t launch_gate(const GateArgs& a_in, int kind, cudaStream_t s) {
   // row segments of about one 16-byte column per thread (fp16 / fp32 frames); the uint8
   // path keeps whole block rows (its 48-byte units give few threads per block)
@@ -558,26 +585,22 @@ cudaError_t launch_gate(const GateArgs& a_in, int kind, cudaStream_t s) {
   dim3 grid(a.hb, a.n, (a.wb + a.seg - 1) / a.seg);
   const size_t smem = (size_t)a.seg * (8 + 4 + 4 + 4) + 768 * 2 + 16;
   switch (kind) {
-    case 0: gate_kernel<0><<<grid, 256, smem, s>>>(a); break;
-    case 1: gate_kernel<1><<<grid, 256, smem, s>>>(a); break;
-    default: gate_kernel<2><<<grid, 256, smem, s>>>(a); break;
+    case 0: return launch_pdl(gate_kernel<0>, grid, dim3(256), smem, s, a);
+    case 1: return launch_pdl(gate_kernel<1>, grid, dim3(256), smem, s, a);
+    default: return launch_pdl(gate_kernel<2>, grid, dim3(256), smem, s, a);
   }
-  return cudaGetLastError();
 }
 
 cudaError_t launch_lists(const ListArgs& a, int n_chunks, cudaStream_t s) {
-  lists_kernel<<<n_chunks, LIST_THREADS, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(lists_kernel, dim3(n_chunks), dim3(LIST_THREADS), 0, s, a);
 }
 
 cudaError_t launch_copy(const CopyArgs& a, cudaStream_t s) {
-  copy_kernel<<<dim3(a.hb, a.n), 256, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(copy_kernel, dim3(a.hb, a.n), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_finalize(State* st, int refresh, int32_t* host_out, cudaStream_t s) {
-  finalize_kernel<<<1, 32, 0, s>>>(st, refresh, host_out);
-  return cudaGetLastError();
+  return launch_pdl(finalize_kernel, dim3(1), dim3(32), 0, s, st, refresh, host_out);
 }
 
 cudaError_t launch_set_mode(State* st, int mode, int reset_hyst, int64_t force_tiles, cudaStream_t s) {
