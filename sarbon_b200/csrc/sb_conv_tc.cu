@@ -96,6 +96,17 @@ struct TcCfg {
   static constexpr int W_OFF = 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
   static constexpr int BIAS_BYTES = kMaxCout * 4;     // every output channel
+  // Epilogue output through shared memory: each epilogue warp writes its 32 output pixels
+  // (NCOL channels each) into its own staging buffer and stores them with one TMA tile
+  // store, a box of OBW px x 32/OBW rows of one unit.  Written directly, every 16-byte
+  // store instruction of a warp touches 32 different lines; the tile store writes whole
+  // lines.  Used where a warp's pixels form such a box of one unit (window modes); CTA
+  // pairs store directly (their shared memory holds the weights and the stages), and so
+  // does the first layer, whose per-item epilogue latency the staging would lengthen.
+  static constexpr bool TSTORE = !PAIR && WIN != 0;
+  static constexpr int OBW = 8;                                    // staged box width (px)
+  static constexpr int EPI_WARP_BYTES = TSTORE ? 32 * NCOL * 2 : 0;  // one warp's buffer
+  static constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;
   static constexpr int CRING = MANUAL ? 16 : 8;       // item-coordinate ring (producer -> epilogue)
   static constexpr int CRING_BYTES = CRING * 8 * 4 * 4; // <= 8 units x (cam, row, col, pad) per item
   // first layer: the input window of one M-tile (BOX_ROWS output rows of one tile), loaded
@@ -113,7 +124,7 @@ struct TcCfg {
   static constexpr int STAGES_UB = (kMaxSmem - A_OFF) / A_STAGE > 24 ? 24 : (kMaxSmem - A_OFF) / A_STAGE;
   static constexpr int N_BARS = 2 * STAGES_UB + 2 * NACC + 4 + (MANUAL ? 2 * NWB : 0) + 2 * CRING;
   static constexpr int BAR_BYTES = ((N_BARS * 8 + 8) + 127) / 128 * 128;
-  static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES;
+  static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES + EPI_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
   // first layer: a multiple of 8 stages, so that each stage (and each window slot) is
   // always filled by the same one of the NGW gather warps (see the gather loop)
@@ -127,6 +138,8 @@ struct TcCfg {
   static constexpr uint32_t IDESC = idesc_f16(PAIR ? 256 : 128, NMMA);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(TPM <= 8, "coordinate ring holds up to 8 units per item");
+  static_assert(!TSTORE || (EPG == 2 && (NCOL == 32 || NCOL == 64) && RPX % 32 == 0),
+                "staged output: a warp's 32 pixels are one box of one unit");
   static_assert(NCTA % 32 == 0 && NCTA >= 32 && NMMA <= 256, "UMMA N / epilogue split");
   static_assert(!PAIR || !MANUAL, "CTA pairs need TMA-loaded A stages");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
@@ -191,13 +204,15 @@ SB_DEV void stage_of(int it, int kb, uint32_t& s, uint32_t& ph) {
 
 template <int CIN, int NCTA, int T, int S, int WIN, int PAIR>
 __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
-    conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmap) {
+    conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmap,
+                   const __grid_constant__ CUtensorMap tmap_y) {
   using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem + C::W_OFF;
   uint8_t* sA = smem + C::A_OFF;
-  float* sBias = reinterpret_cast<float*>(sA + C::STAGES * C::A_STAGE);
+  uint8_t* sEpi = sA + C::STAGES * C::A_STAGE;  // [8 epilogue warps][EPI_WARP_BYTES], 1024-aligned
+  float* sBias = reinterpret_cast<float*>(sEpi + C::EPI_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sBias) + C::BIAS_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::STAGES;
@@ -255,6 +270,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   }
   for (int i = threadIdx.x; i < a.cout; i += blockDim.x) sBias[i] = a.bias[i];
   if (!C::MANUAL && warp == C::PROD_WARP && lane == 0) prefetch_tmap(&tmap);
+  if (C::TSTORE && warp == 0 && lane == 0) prefetch_tmap(&tmap_y);
   tc_fence_before();
   if (PAIR) cluster_sync();  // the leader's barriers are initialised before the odd CTA uses them
   else __syncthreads();
@@ -646,6 +662,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         size_t pix;
         int n0;
         bool st;
+        bool ovalid;     // staged output: the warp's box belongs to a listed unit
+        int ox, oy, oc;  // staged output: box origin (pixel column, row, camera)
         uint4 rr[C::NCOL / 8];
       };
       // unit coordinates come from the producer through the shared-memory ring, so the
@@ -674,9 +692,18 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         if (valid && !origin_ok) atomicOr(&a.st->error, SB_ERR_BAD_TILE);
         o.st = valid && inb;
         o.pix = (((size_t)tc.cam * a.ho + gy) * a.wo + gx) * a.cout + o.n0;
-        if (res != nullptr && o.st) {
+        if (C::TSTORE) {
+          // the warp's 32 pixels: rows p0/OBW .. of the unit (p0 = this warp's first pixel)
+          const int p0 = p - lane;
+          o.ovalid = valid && origin_ok;
+          o.ox = tc.bx * 8;
+          o.oy = tc.by * C::RROWS + p0 / C::OBW;
+          o.oc = tc.cam;
+        }
+        if (res != nullptr) {
 #pragma unroll
-          for (int q2 = 0; q2 < C::NCOL / 8; ++q2) o.rr[q2] = __ldg(reinterpret_cast<const uint4*>(res + o.pix) + q2);
+          for (int q2 = 0; q2 < C::NCOL / 8; ++q2)
+            o.rr[q2] = o.st ? __ldg(reinterpret_cast<const uint4*>(res + o.pix) + q2) : make_uint4(0, 0, 0, 0);
         }
         return true;
       };
@@ -709,7 +736,12 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
           *abort_flag = 1;
         }
-        if (cu.st) {
+        uint8_t* ebuf = sEpi + warp * C::EPI_WARP_BYTES;
+        if (C::TSTORE) {
+          if (lane == 0) bulk_wait_read0();  // the previous item's store has read the buffer
+          __syncwarp();
+        }
+        if (C::TSTORE || cu.st) {
 #pragma unroll
           for (int j = 0; j < C::NCOL / 8; ++j) {
             float f[8];
@@ -735,7 +767,23 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
             __half2* ph = reinterpret_cast<__half2*>(&o);
 #pragma unroll
             for (int e = 0; e < 4; ++e) ph[e] = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
-            reinterpret_cast<uint4*>(y + cu.pix)[j] = o;
+            if (C::TSTORE) {
+              // box layout [pixel][NCOL channels] with the tensor map's swizzle (128-byte rows:
+              // 16-byte chunk j at j ^ (pixel & 7); 64-byte rows: j ^ ((pixel >> 1) & 3)), so
+              // the 32 lanes' writes spread over all banks
+              const int pj = C::NCOL == 64 ? (j ^ (lane & 7)) : (j ^ ((lane >> 1) & 3));
+              *reinterpret_cast<uint4*>(ebuf + lane * (C::NCOL * 2) + pj * 16) = o;
+            } else {
+              reinterpret_cast<uint4*>(y + cu.pix)[j] = o;
+            }
+          }
+        }
+        if (C::TSTORE) {
+          fence_proxy_async_smem();  // generic-proxy writes -> the TMA store (async proxy)
+          __syncwarp();
+          if (lane == 0 && cu.ovalid) {  // pixels outside the image are clipped by the store
+            tma_store_4d(&tmap_y, ebuf, cu.n0, cu.ox, cu.oy, cu.oc);
+            bulk_commit_group();
           }
         }
         return true;
@@ -750,6 +798,10 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         if (!step(it, ra, rb) || it + C::EPG >= my_items) break;
         if (!step(it + C::EPG, rb, ra)) break;
       }
+      // the staged stores are complete (global writes performed) before the CTA signals
+      // its dependents or exits
+      if (C::TSTORE && lane == 0) bulk_wait0();
+      __syncwarp();
     }
   }
   // the weight copy has landed before the CTA may exit (also when it had no items)
@@ -774,8 +826,9 @@ namespace {
 
 struct Variant {
   int cin, cout, t, s, win, ncta, pair;
-  void (*fn)(const ConvArgs, const CUtensorMap);
+  void (*fn)(const ConvArgs, const CUtensorMap, const CUtensorMap);
   int smem, threads, w_bytes, ch, box_rows, win_cols, win_rows;
+  int tstore, ncol, obw;  // staged output stores: flag, channels and width of a warp's box
   int mode() const { return win | (pair << 3); }
 };
 
@@ -784,7 +837,7 @@ Variant make_variant(int cout) {
   using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
   return Variant{CIN,       cout,       T,         S,         WIN,       NCTA,      PAIR,
                  conv_tc_kernel<CIN, NCTA, T, S, WIN, PAIR>,  C::SMEM,   C::THREADS, C::W_BYTES,
-                 C::CH,     C::BOX_ROWS, C::WIN_COLS, C::WIN_ROWS};
+                 C::CH,     C::BOX_ROWS, C::WIN_COLS, C::WIN_ROWS, C::TSTORE ? 1 : 0, C::NCOL, C::OBW};
 }
 
 // Sarbon stem shapes (widths 32/64/128, Res blocks) at block 32 and block 64.  The first
@@ -1020,9 +1073,31 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, int grid_x, cudaStream_t st) {
+cudaError_t conv_tc_make_tmap_out(CUtensorMap* map, void* dst, int n, int ho, int wo, int cin, int cout, int t, int s,
+                                  int mode) {
+  const Variant* v = find_variant(cin, cout, t, s, mode);
+  if (!v) return cudaErrorInvalidValue;
+  std::memset(map, 0, sizeof(*map));
+  if (!v->tstore) return cudaSuccess;  // this variant stores directly; the map is not read
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) return cudaErrorNotSupported;
+  // the destination cache [n][ho][wo][cout]; one box = one epilogue warp's 32 pixels
+  cuuint64_t dims[4] = {(cuuint64_t)cout, (cuuint64_t)wo, (cuuint64_t)ho, (cuuint64_t)n};
+  cuuint64_t strides[3] = {(cuuint64_t)cout * 2, (cuuint64_t)wo * cout * 2, (cuuint64_t)ho * wo * cout * 2};
+  cuuint32_t box[4] = {(cuuint32_t)v->ncol, (cuuint32_t)v->obw, (cuuint32_t)(32 / v->obw), 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapSwizzle swz = v->ncol * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, dst, dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, const CUtensorMap* map_y, int grid_x,
+                           cudaStream_t st) {
   const Variant* v = find_variant(a.cin, a.cout, a.t, a.s, mode);
-  if (!v || map == nullptr || a.cout > kMaxCout) return cudaErrorInvalidValue;  // every variant loads through TMA
+  // every variant loads through TMA; staged-output variants also store through map_y
+  if (!v || map == nullptr || map_y == nullptr || a.cout > kMaxCout) return cudaErrorInvalidValue;
   static bool attr_done[32] = {};
   const int idx = (int)(v - variants().data());
   if (!attr_done[idx]) {
@@ -1064,7 +1139,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
     if (pairs < 1) pairs = 1;
     cfg.gridDim = dim3(2 * pairs, 1, 1);
     cfg.numAttrs = 2;  // + programmatic dependent launch
-    return cudaLaunchKernelEx(&cfg, v->fn, a, *map);
+    return cudaLaunchKernelEx(&cfg, v->fn, a, *map, *map_y);
   }
   // each CTA keeps one C_out slice: the grid is a multiple of the number of slices
   const int nsplit = a.cout / v->ncta;
@@ -1083,7 +1158,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, v->fn, a, *map);
+  return cudaLaunchKernelEx(&cfg, v->fn, a, *map, *map_y);
 }
 
 }  // namespace sb

@@ -93,6 +93,7 @@ struct sb_engine {
   void* wdev[SB_MAX_LAYERS] = {};
   bool wok[SB_MAX_LAYERS] = {};
   CUtensorMap tmap[SB_MAX_LAYERS];
+  CUtensorMap tmap_y[SB_MAX_LAYERS];  // destination cache (staged-output variants)
   bool has_tmap[SB_MAX_LAYERS] = {};
   int32_t* host_out = nullptr;      // mapped pinned: mode, count, error, written
   int32_t* host_out_dev = nullptr;
@@ -194,7 +195,8 @@ int launch_convs(sb_engine* e, cudaStream_t s) {
     }
     cudaError_t err;
     if (e->dtype == SB_F16) {
-      err = launch_conv_tc(a, e->layer_mode[i], e->has_tmap[i] ? &e->tmap[i] : nullptr, e->n_sms, s);
+      err = launch_conv_tc(a, e->layer_mode[i], e->has_tmap[i] ? &e->tmap[i] : nullptr,
+                           e->has_tmap[i] ? &e->tmap_y[i] : nullptr, e->n_sms, s);
     } else {
       err = launch_conv_simt(a, e->n_sms * 4, s);
     }
@@ -472,6 +474,10 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
       cudaError_t err = conv_tc_make_tmap(&e->tmap[i], e->cache[L.src], n_streams, (int)e->shape[L.src][1],
                                           (int)e->shape[L.src][2], L.cin, e->layer_t[i], L.stride,
                                           e->layer_mode[i]);
+      if (err == cudaSuccess)
+        err = conv_tc_make_tmap_out(&e->tmap_y[i], e->cache[i + 1], n_streams, (int)e->shape[i + 1][1],
+                                    (int)e->shape[i + 1][2], L.cin, L.cout, e->layer_t[i], L.stride,
+                                    e->layer_mode[i]);
       if (err != cudaSuccess) return bail(fail(SB_ECUDA, std::string("tensor map: ") + cudaGetErrorString(err)));
       e->has_tmap[i] = true;
     }

@@ -120,7 +120,12 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w /*[3][3]
                         uint16_t* out /* fp16 bits */);
 cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s,
                               int mode);
-cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, int grid_x, cudaStream_t s);
+// the destination cache's map for the variants whose epilogue stages its output in shared
+// memory and writes it with TMA tile stores (zero-filled and unused for the others)
+cudaError_t conv_tc_make_tmap_out(CUtensorMap* map, void* dst, int n, int ho, int wo, int cin, int cout, int t, int s,
+                                  int mode);
+cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, const CUtensorMap* map_y, int grid_x,
+                           cudaStream_t s);
 int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s);
 
 // Sets the message sb_last_error() returns on this thread; returns `code`.

@@ -114,6 +114,20 @@ SB_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Tile store shared -> global through a tensor map (bulk async-group of the issuing thread).
+// Elements of the box outside the tensor's extent are not written.
+SB_DEV void tma_store_4d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+SB_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The issuing thread's bulk groups have finished reading their shared-memory sources.
+SB_DEV void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// The issuing thread's bulk groups are complete (their global writes performed).
+SB_DEV void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned address, bytes % 16 == 0).
 SB_DEV void prefetch_l2(const void* src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
