@@ -278,9 +278,14 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   const uint32_t tmem_base = *tmem_holder;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
 
-  // This CTA's weight slice is constant during a step: its bulk copy starts before the wait
-  // for the previous kernel of the stream (programmatic dependent launch).  Everything the
-  // earlier kernels write -- device state, lists, caches -- is read only after the wait.
+  // Programmatic dependent launch: this kernel may start while the previous kernel of the
+  // stream (the previous layer, or the frame copy) still runs.  That kernel began its item
+  // loop only after the kernel before it had completed, and it writes nothing but its
+  // output cache and error flags; so the step's device state and unit lists (written by
+  // the gate / list / mode kernels, two or more launches back) and this CTA's weight slice
+  // are read before griddepcontrol.wait.  Only the threads that read caches written by
+  // earlier layers wait: the producer before its first input copy, the epilogue before its
+  // first residual read.
   if (warp == C::PROD_WARP && lane == 0) {
     const int wsplit = PAIR ? (int)rank : (int)blockIdx.x % (a.cout / NCTA);
     const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)wsplit * C::W_BYTES;
@@ -290,7 +295,6 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       bulk_load(sW + off, wsrc + off, len, wfull);
     }
   }
-  grid_dep_wait();
 
   // work of this launch, decided on the device (no host sync)
   const int mode = a.st->mode_cur;
@@ -452,6 +456,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       };
       Coords ca, cb;
       fetch_lane(0, ca);
+      grid_dep_wait();  // the input cache (previous layer / frame copy) is complete
       for (int base = 0; base < my_items; base += 64) {
         if (base + 32 < my_items) fetch_lane(base + 32, cb);
         if (!run_batch(base, ca) || base + 32 >= my_items) break;
@@ -647,6 +652,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       }
       __syncwarp();
     } else if (warp < 8) {
+      grid_dep_wait();  // residual caches of earlier layers are complete
       // ------------------------------------------------ epilogue: TMEM -> bias/res/ReLU -> cache
       // Warp w reads TMEM lanes 32*(w%4).. (its accumulator rows); with two groups (EPG = 2)
       // warps 0-3 take the even and warps 4-7 the odd items with all NCOL = NMMA columns,
