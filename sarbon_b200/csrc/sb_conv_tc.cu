@@ -708,8 +708,14 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         }
         if (res != nullptr) {
 #pragma unroll
-          for (int q2 = 0; q2 < C::NCOL / 8; ++q2)
-            o.rr[q2] = o.st ? __ldg(reinterpret_cast<const uint4*>(res + o.pix) + q2) : make_uint4(0, 0, 0, 0);
+          for (int q2 = 0; q2 < C::NCOL / 16; ++q2) {  // 32-byte loads: one sector per lane
+            if (o.st) {
+              ld_global_nc_v8(res + o.pix + q2 * 16, o.rr[2 * q2], o.rr[2 * q2 + 1]);
+            } else {
+              o.rr[2 * q2] = make_uint4(0, 0, 0, 0);
+              o.rr[2 * q2 + 1] = make_uint4(0, 0, 0, 0);
+            }
+          }
         }
         return true;
       };
@@ -748,6 +754,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           __syncwarp();
         }
         if (C::TSTORE || cu.st) {
+          uint4 prev = make_uint4(0, 0, 0, 0);
 #pragma unroll
           for (int j = 0; j < C::NCOL / 8; ++j) {
             float f[8];
@@ -779,8 +786,10 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
               // the 32 lanes' writes spread over all banks
               const int pj = C::NCOL == 64 ? (j ^ (lane & 7)) : (j ^ ((lane >> 1) & 3));
               *reinterpret_cast<uint4*>(ebuf + lane * (C::NCOL * 2) + pj * 16) = o;
+            } else if (j & 1) {
+              st_global_v8(y + cu.pix + (j - 1) * 8, prev, o);  // 32-byte stores: one sector per lane
             } else {
-              reinterpret_cast<uint4*>(y + cu.pix)[j] = o;
+              prev = o;
             }
           }
         }
