@@ -82,17 +82,15 @@ struct TcCfg {
   static constexpr int W_BYTES = NWKB * B_KB;
   static constexpr int NMMA = PAIR ? 2 * NCTA : NCTA;  // MMA N = accumulator columns per CTA
   // narrow layers: two epilogue groups of four warps take alternate items (each warp all
-  // NMMA columns of its 32 rows) and four accumulator buffers let the MMAs run further
-  // ahead; wide layers: all eight warps on every item (half the columns each), two buffers
+  // NMMA columns of its 32 rows); wide layers: all eight warps on every item (half the
+  // columns each).  Accumulator buffers: see NACC below.
   static constexpr int EPG = NMMA <= 64 ? 2 : 1;
-  static constexpr int NACC = EPG == 2 ? 4 : 2;
-  static constexpr int TMEM_COLS = (NACC * NMMA) <= 32 ? 32 : (NACC * NMMA) <= 64 ? 64 : (NACC * NMMA) <= 128 ? 128 : (NACC * NMMA) <= 256 ? 256 : 512;
   // roles: warps 0-7 epilogue (two per TMEM lane quadrant, half the columns each),
-  // warp 8 TMA producer, warps 9-10 MMA issuers (warp 9 owns TMEM), warps 11-14 first-layer gather
+  // warp 8 TMA producer, warps 9-10 MMA issuers (warp 9 owns TMEM), warps 11-14 first-layer
+  // gather, or warp 11 the second TMA producer (see NPROD)
   static constexpr int NCOL = EPG == 2 ? NMMA : NMMA / 2;  // accumulator columns per epilogue warp
   static constexpr int EPI_WARPS_PER_ITEM = 8 / EPG;
-  static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 352;  // MMA issuers: warps 9, 10
-  static constexpr int THREADS = MANUAL ? 480 : 352;
+  static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 352, PROD_WARP2 = 11;  // MMA issuers: warps 9, 10
   static constexpr int W_OFF = 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
   static constexpr int BIAS_BYTES = kMaxCout * 4;     // every output channel
@@ -122,22 +120,35 @@ struct TcCfg {
   static constexpr int WIN_BYTES = MANUAL ? NWB * WIN_BUF : 0;
   // mbarriers (sized for the most stages that could fit) + TMEM address + abort flag
   static constexpr int STAGES_UB = (kMaxSmem - A_OFF) / A_STAGE > 24 ? 24 : (kMaxSmem - A_OFF) / A_STAGE;
-  static constexpr int N_BARS = 2 * STAGES_UB + 2 * NACC + 4 + (MANUAL ? 2 * NWB : 0) + 2 * CRING;
+  static constexpr int N_BARS = 2 * STAGES_UB + 2 * 4 /*NACC <= 4*/ + 4 + (MANUAL ? 2 * NWB : 0) + 2 * CRING;
   static constexpr int BAR_BYTES = ((N_BARS * 8 + 8) + 127) / 128 * 128;
   static constexpr int FIXED = 1024 /*align slack*/ + BIAS_BYTES + BAR_BYTES + WIN_BYTES + CRING_BYTES + EPI_BYTES;
   static constexpr int STAGES_FIT = (kMaxSmem - FIXED - A_OFF) / A_STAGE;
   // first layer: a multiple of 8 stages, so that each stage (and each window slot) is
   // always filled by the same one of the NGW gather warps (see the gather loop)
   static constexpr int STAGES = STAGES_FIT > 24 ? 24 : MANUAL ? (STAGES_FIT / 8) * 8 : STAGES_FIT;
-  // MMA issuers: two (alternate items, one accumulator each) when the ring holds two items'
-  // K-blocks; each issuer then owns a sub-ring of SUB stages that the producer fills in
-  // item order, so every stage has one in-order consumer and the phase parities stay exact
-  static constexpr int NISS = STAGES >= 2 * NKB ? 2 : 1;
+  // MMA issuers: two (alternate items) when the ring holds two items' K-blocks, or for CTA
+  // pairs whenever it holds four stages; each issuer owns a sub-ring of SUB stages used in
+  // the order of its K-blocks, so every stage has one in-order consumer and the phase
+  // parities stay exact.  An issuer's mbarrier wait costs ~200 cycles in which the tensor
+  // pipe would run dry; with two, one keeps it fed while the other waits.
+  static constexpr int NISS = (STAGES >= 2 * NKB || (PAIR && STAGES >= 4)) ? 2 : 1;
   static constexpr int SUB = STAGES / NISS;
+  // TMA producers: with two issuers (TMA-loaded layers) each sub-ring has its own producer
+  // warp filling its issuer's items, so neither issuer waits behind the other's loads when
+  // a sub-ring holds less than an item
+  static constexpr int NPROD = (!MANUAL && NISS == 2) ? 2 : 1;
+  static constexpr int THREADS = MANUAL ? 480 : NPROD == 2 ? 384 : 352;
+  // accumulator buffers: four for narrow layers (two epilogue groups) and for two issuers,
+  // so the MMAs can run ahead of the epilogue
+  static constexpr int NACC = (EPG == 2 || NISS == 2) ? 4 : 2;
+  static constexpr int TMEM_COLS = (NACC * NMMA) <= 32 ? 32 : (NACC * NMMA) <= 64 ? 64 : (NACC * NMMA) <= 128 ? 128 : (NACC * NMMA) <= 256 ? 256 : 512;
   static constexpr int SMEM = FIXED + A_OFF + STAGES * A_STAGE;
   static constexpr uint32_t IDESC = idesc_f16(PAIR ? 256 : 128, NMMA);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(TPM <= 8, "coordinate ring holds up to 8 units per item");
+  static_assert(NACC * NMMA <= 512, "accumulators exceed TMEM");
+  static_assert(NPROD == 1 || (CRING % 2 == 0 && SUB >= 1), "two producers: ring slots alternate between them");
   static_assert(!TSTORE || (EPG == 2 && (NCOL == 32 || NCOL == 64) && RPX % 32 == 0),
                 "staged output: a warp's 32 pixels are one box of one unit");
   static_assert(NCTA % 32 == 0 && NCTA >= 32 && NMMA <= 256, "UMMA N / epilogue split");
@@ -323,10 +334,13 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   };
 
   if (my_items > 0) {
-    if (warp == C::PROD_WARP) {
+    if (warp == C::PROD_WARP || (C::NPROD == 2 && warp == C::PROD_WARP2)) {
       // ------------------------------------------------ producer: the slice's weights, A stages
       // The whole warp runs the loop (warp-uniform control flow); lane 0 issues the copies.
+      // With two producers, producer pu fills the items pu, pu + 2, ... (issuer pu's sub-ring).
       const bool leader = lane == 0;
+      const int pu = warp == C::PROD_WARP ? 0 : 1;
+      const int n_loc = (my_items - pu + C::NPROD - 1) / C::NPROD;  // this producer's items
       uint32_t g = 0, nload = 0;
       struct Coords {
         int cam[C::TPM], y0[C::TPM], x0[C::TPM], uy[C::TPM], ux[C::TPM];
@@ -366,7 +380,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         }
         if (nload == 0) {  // the weights were issued in the prologue
           ++nload;
-          if (PAIR && rank == 1) {  // tell the leader that this CTA's half of B is resident
+          if (PAIR && rank == 1 && pu == 0) {  // tell the leader that this CTA's half of B is resident
             if (!warp_wait(wfull, 0, abort_flag)) {
               atomicOr(&a.st->error, SB_ERR_TIMEOUT_WGT);
               *abort_flag = 1;
@@ -432,14 +446,14 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         }
         return true;
       };
-      // Lane l loads the unit coordinates of item base + l, one batch of 32 items ahead of
-      // their use (two batches alternate between the register sets ca and cb), so the
-      // list reads' latency is paid once per 32 items; items take theirs by shuffle.
+      // Lane l loads the unit coordinates of this producer's item base + l, one batch of 32
+      // items ahead of their use (two batches alternate between the register sets ca and cb),
+      // so the list reads' latency is paid once per 32 items; items take theirs by shuffle.
       auto fetch_lane = [&](int base, Coords& o) {
-        if (base + (int)lane < my_items) fetch(base + (int)lane, o);
+        if (base + (int)lane < n_loc) fetch(pu + (base + (int)lane) * C::NPROD, o);
       };
       auto run_batch = [&](int base, const Coords& cur) -> bool {
-        for (int i = 0; i < 32 && base + i < my_items; ++i) {
+        for (int i = 0; i < 32 && base + i < n_loc; ++i) {
           if (*abort_flag) return false;
           Coords cc;
 #pragma unroll
@@ -450,17 +464,17 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
             cc.uy[j] = __shfl_sync(0xFFFFFFFFu, cur.uy[j], i);
             cc.ux[j] = __shfl_sync(0xFFFFFFFFu, cur.ux[j], i);
           }
-          if (!issue(base + i, cc)) return false;
+          if (!issue(pu + (base + i) * C::NPROD, cc)) return false;
         }
         return true;
       };
       Coords ca, cb;
       fetch_lane(0, ca);
       grid_dep_wait();  // the input cache (previous layer / frame copy) is complete
-      for (int base = 0; base < my_items; base += 64) {
-        if (base + 32 < my_items) fetch_lane(base + 32, cb);
-        if (!run_batch(base, ca) || base + 32 >= my_items) break;
-        if (base + 64 < my_items) fetch_lane(base + 64, ca);
+      for (int base = 0; base < n_loc; base += 64) {
+        if (base + 32 < n_loc) fetch_lane(base + 32, cb);
+        if (!run_batch(base, ca) || base + 32 >= n_loc) break;
+        if (base + 64 < n_loc) fetch_lane(base + 64, ca);
         if (!run_batch(base + 32, cb)) break;
       }
       // drain: every issued copy has landed before the CTA may exit
@@ -473,6 +487,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         // odd CTA of a pair has no full barriers of its own: it waits until the leader's
         // MMAs have released its last stages (no copy or commit into it is then pending)
         for (int u = 0; u < C::NISS; ++u) {
+          if (C::NPROD == 2 && u != pu) continue;  // the other producer drains its own sub-ring
           const uint32_t uses = (uint32_t)((my_items - u + C::NISS - 1) / C::NISS) * C::NKB;
           const uint32_t first = uses > (uint32_t)C::SUB ? uses - C::SUB : 0u;
           for (uint32_t q = first; q < uses; ++q) {
