@@ -156,7 +156,7 @@ struct TcCfg {
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
   static_assert(!MANUAL || ((NISS * SUB) % NGW == 0 && NWB % NGW == 0), "gather warp per stage / window slot");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
-  static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256), "first-layer window box");
+  static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256 && WIN_COLS % 2 == 0), "first-layer window box");
   static_assert(!WIN || ((((WIN == 1 || WIN == 3) && S == 1) || (WIN == 2 && S == 2 && (CIN == 32 || CIN == 64))) &&
                          8 % T == 0 && T <= 8 && ROWB == 128 && !MANUAL),
                 "window mode geometry");
@@ -526,16 +526,28 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           const int lr = r / T, lc = r % T;
           // element (ky, kx, c) of output (lr, lc): window row S*lr+ky, column
           // lead + (S*lc + kx)*CIN + c  (the window starts one input pixel left of the tile)
-          const uint16_t* wrow = wbase + (S * lr) * C::WIN_COLS + (S * lc) * CIN;
+          // The 3*CIN elements (kx, c) of one ky are contiguous in the window row and in the
+          // A row; they are read as 32-bit words (S = 2 puts every pixel's run at the same
+          // parity: it starts at an odd element when WIN_LEAD is odd) and shifted into place.
+          constexpr int RUN = 3 * CIN;
+          constexpr int ODD = C::WIN_LEAD & 1;
+          constexpr int NWD = (RUN + ODD + 1) / 2;
+          const uint32_t* wrow32 =
+              reinterpret_cast<const uint32_t*>(wbase + (S * lr) * C::WIN_COLS + (S * lc) * CIN - ODD);
           uint16_t v[C::KPAD > 0 ? C::KPAD : 16];
 #pragma unroll
           for (int k = 0; k < C::KPAD; ++k) v[k] = 0;
 #pragma unroll
-          for (int ky = 0; ky < 3; ++ky)
+          for (int ky = 0; ky < 3; ++ky) {
+            uint32_t w[NWD];
 #pragma unroll
-            for (int kx = 0; kx < 3; ++kx)
+            for (int i = 0; i < NWD; ++i) w[i] = wrow32[ky * (C::WIN_COLS / 2) + i];
 #pragma unroll
-              for (int c = 0; c < CIN; ++c) v[(ky * 3 + kx) * CIN + c] = wrow[ky * C::WIN_COLS + kx * CIN + c];
+            for (int t = 0; t < RUN; ++t) {
+              const int h = t + ODD;
+              v[ky * RUN + t] = (uint16_t)(w[h >> 1] >> ((h & 1) * 16));
+            }
+          }
           uint8_t* row = sA + s * C::A_STAGE + r * C::ROWB;
           constexpr int NQ = C::ROWB / 16;
 #pragma unroll

@@ -71,7 +71,7 @@ SB_DEV float absdiff2(uint32_t x, uint32_t y) {
 // in torch's order, fused_engine.py:142-144).  Then `| extra`, the refresh phase, and the
 // changed blocks of the new frames are copied into the image cache.
 template <int KIND>  // 0: fp16 frames, 1: fp32 frames, 2: uint8 BGR frames (fused prep)
-__global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
+__global__ void __launch_bounds__(256, 4) gate_kernel(GateArgs a) {
   grid_dep_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   if (in_hysteresis(a.st)) return;  // hysteresis dense step: the gate is not looked at (:222-226)
   // CTA = blocks [bx0, bx0 + nblk) of block row `by` of camera `cam` (a segment of the row)
@@ -111,11 +111,20 @@ __global__ void __launch_bounds__(256) gate_kernel(GateArgs a) {
     const uint4* g = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.img) + img_row0);
     for (int v = threadIdx.x; v < vpb * nblk; v += blockDim.x) {
       float acc = 0.f;
-#pragma unroll 8
-      for (int r = 0; r < B; ++r) {
-        const uint4 x = __ldg(f + (size_t)r * vpr + v);
-        const uint4 y = g[(size_t)r * vpr + v];
-        acc += (absdiff2(x.x, y.x) + absdiff2(x.y, y.y)) + (absdiff2(x.z, y.z) + absdiff2(x.w, y.w));
+      // eight rows of both images in flight per thread (the image cache is written only by
+      // the copy below, after every read of this kernel, so it is read through the
+      // non-coherent path too)
+      for (int r0 = 0; r0 < B; r0 += 8) {
+        uint4 xs[8], ys[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          xs[k] = __ldg(f + (size_t)(r0 + k) * vpr + v);
+          ys[k] = __ldg(g + (size_t)(r0 + k) * vpr + v);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          acc += (absdiff2(xs[k].x, ys[k].x) + absdiff2(xs[k].y, ys[k].y)) +
+                 (absdiff2(xs[k].z, ys[k].z) + absdiff2(xs[k].w, ys[k].w));
       }
       atomicAdd(&s_sf[v / vpb], acc);
     }
