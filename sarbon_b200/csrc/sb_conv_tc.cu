@@ -34,7 +34,7 @@
 namespace sb {
 
 constexpr int kMaxSmem = 232448;  // 227 KB opt-in shared memory per CTA on sm_100
-constexpr int kMaxCout = 128;     // widest layer of the stem (bias staged in shared memory)
+constexpr int kMaxCout = 128;     // widest layer of the stem (ConvArgs::bias_v holds its bias)
 
 // WIN = 0: per-tap im2col boxes over blocks (or the first layer's gather);
 // WIN = 1: row windows -- regions of 8/T x 1 blocks (8 px x T rows), one box per (ky, chunk)
@@ -92,8 +92,11 @@ struct TcCfg {
   static constexpr int EPI_WARPS_PER_ITEM = 8 / EPG;
   static constexpr int PROD_WARP = 8, MMA_WARP = 9, GATHER0 = 352, PROD_WARP2 = 11;  // MMA issuers: warps 9, 10
   static constexpr int W_OFF = 0;
+  // bias: CTA pairs stage it in shared memory; the other layers read it from the kernel
+  // parameters (ConvArgs::bias_v, warp-uniform constant-cache reads) -- measured faster there
+  static constexpr bool BIAS_SMEM = PAIR != 0;
+  static constexpr int BIAS_BYTES = BIAS_SMEM ? kMaxCout * 4 : 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
-  static constexpr int BIAS_BYTES = kMaxCout * 4;     // every output channel
   // Epilogue output through shared memory: each epilogue warp writes its 32 output pixels
   // (NCOL channels each) into its own staging buffer and stores them with one TMA tile
   // store, a box of OBW px x 32/OBW rows of one unit.  Written directly, every 16-byte
@@ -215,7 +218,7 @@ SB_DEV void stage_of(int it, int kb, uint32_t& s, uint32_t& ph) {
 
 template <int CIN, int NCTA, int T, int S, int WIN, int PAIR>
 __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
-    conv_tc_kernel(const ConvArgs a, const __grid_constant__ CUtensorMap tmap,
+    conv_tc_kernel(const __grid_constant__ ConvArgs a, const __grid_constant__ CUtensorMap tmap,
                    const __grid_constant__ CUtensorMap tmap_y) {
   using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   uint8_t* sW = smem + C::W_OFF;
   uint8_t* sA = smem + C::A_OFF;
   uint8_t* sEpi = sA + C::STAGES * C::A_STAGE;  // [8 epilogue warps][EPI_WARP_BYTES], 1024-aligned
-  float* sBias = reinterpret_cast<float*>(sEpi + C::EPI_BYTES);
+  float* sBias = reinterpret_cast<float*>(sEpi + C::EPI_BYTES);  // BIAS_SMEM only
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sBias) + C::BIAS_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + C::STAGES;
@@ -279,7 +282,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       tmem_relinquish();
     }
   }
-  for (int i = threadIdx.x; i < a.cout; i += blockDim.x) sBias[i] = a.bias[i];
+  if (C::BIAS_SMEM)
+    for (int i = threadIdx.x; i < a.cout; i += blockDim.x) sBias[i] = a.bias_v[i];
   if (!C::MANUAL && warp == C::PROD_WARP && lane == 0) prefetch_tmap(&tmap);
   if (C::TSTORE && warp == 0 && lane == 0) prefetch_tmap(&tmap_y);
   tc_fence_before();
@@ -785,8 +789,9 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
 #pragma unroll
           for (int j = 0; j < C::NCOL / 8; ++j) {
             float f[8];
-            const float4 b0 = *reinterpret_cast<const float4*>(sBias + cu.n0 + j * 8);  // one broadcast
-            const float4 b1 = *reinterpret_cast<const float4*>(sBias + cu.n0 + j * 8 + 4);
+            const float* bsrc = C::BIAS_SMEM ? sBias : a.bias_v;  // warp-uniform index either way
+            const float4 b0 = *reinterpret_cast<const float4*>(bsrc + cu.n0 + j * 8);
+            const float4 b1 = *reinterpret_cast<const float4*>(bsrc + cu.n0 + j * 8 + 4);
             const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
             for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + bb[e];

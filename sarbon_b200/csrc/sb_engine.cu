@@ -90,6 +90,7 @@ struct sb_engine {
   int n_chunks = 0;
   State* st = nullptr;
   float* bias[SB_MAX_LAYERS] = {};
+  float bias_h[SB_MAX_LAYERS][128] = {};  // host copy, passed by value to the fp16 conv kernels
   void* wdev[SB_MAX_LAYERS] = {};
   bool wok[SB_MAX_LAYERS] = {};
   CUtensorMap tmap[SB_MAX_LAYERS];
@@ -160,6 +161,7 @@ int launch_convs(sb_engine* e, cudaStream_t s) {
     a.y = e->cache[i + 1];
     a.res = L.res >= 0 ? e->cache[L.res] : nullptr;
     a.bias = e->bias[i];
+    std::memcpy(a.bias_v, e->bias_h[i], sizeof(a.bias_v));
     a.wimg = e->wdev[i];
     const int di = e->layer_di[i];
     a.lcam = e->lists + (size_t)di * 3 * e->n_blocks;
@@ -492,6 +494,7 @@ int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias
   const sb_layer_desc& L = e->layers[layer];
   SB_CUDA(cudaSetDevice(e->dev));
   SB_CUDA(cudaMemcpy(e->bias[layer], bias, (size_t)L.cout * 4, cudaMemcpyHostToDevice));
+  for (int c = 0; c < L.cout && c < 128; ++c) e->bias_h[layer][c] = bias[c];
   if (e->dtype == SB_F16) {
     const size_t bytes = conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[layer], L.stride);
     std::vector<uint16_t> img(bytes / 2);

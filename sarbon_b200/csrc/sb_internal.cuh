@@ -99,6 +99,9 @@ struct ConvArgs {
   const int32_t* rcam;     // region lists of this layer's dilation
   const int32_t* rry;
   const int32_t* rrx;
+  // bias by value (kernel parameter space): epilogue reads are warp-uniform and go through
+  // the constant cache, off the shared-memory path the tensor pipe saturates
+  alignas(16) float bias_v[128];
 };
 
 // ---------------------------------------------------------------- launchers
