@@ -150,6 +150,7 @@ struct TcCfg {
   static constexpr uint32_t IDESC = idesc_f16(PAIR ? 256 : 128, NMMA);
   static_assert(STAGES >= 2, "shared memory too small for two stages");
   static_assert(TPM <= 8, "coordinate ring holds up to 8 units per item");
+  static_assert(!PAIR || NCOL == 64, "pair epilogue: 16x256b fragments of 64 columns per warp");
   static_assert(NACC * NMMA <= 512, "accumulators exceed TMEM");
   static_assert(NPROD == 1 || (CRING % 2 == 0 && SUB >= 1), "two producers: ring slots alternate between them");
   static_assert(!TSTORE || (EPG == 2 && (NCOL == 32 || NCOL == 64) && RPX % 32 == 0),
@@ -682,6 +683,200 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         mbar_wait(&dbar[u], 0, &never);
       }
       __syncwarp();
+    } else if (PAIR && warp < 8) {
+      grid_dep_wait();  // residual caches of earlier layers are complete
+      // ------------------------------------------------ epilogue of CTA pairs: TMEM fragments -> cache
+      // Warp w reads TMEM lane quadrant q = w % 4 (32 accumulator rows = pixels); with two
+      // groups (EPG = 2) warps 0-3 take the even and warps 4-7 the odd items with all
+      // NCOL = NMMA columns, else every warp takes every item with columns (w / 4) * NCOL...
+      // The accumulator is read as 16x256b fragments (two loads, lanes 32q and 32q + 16):
+      // thread t (k = t / 4, m = t % 4) gets, for the pixels k, k + 8, k + 16, k + 24 of the
+      // quadrant, the columns 8j + 2m + b.  The weight image orders the output channels so
+      // that column 8j + 2m + b of a group of NCOL columns holds channel CPT * m + 2j + b
+      // (CPT = NCOL / 4): each thread then owns CPT consecutive channels of four pixels and
+      // the four threads of a pixel store its NCOL channels as whole 32-byte sectors that
+      // together fill complete lines.  The residual is read the same way one item ahead;
+      // the TMEM buffer is released as soon as it sits in registers.
+      constexpr int G = C::NCOL, CPT = G / 4, REP = G / 8;  // CPT channels per thread and pixel
+      const int q = warp & 3, eg = C::EPG == 2 ? (warp >> 2) : 0;  // lane quadrant, group
+      const int col0 = C::EPG == 2 ? 0 : (warp >> 2) * C::NCOL;
+      const int k = lane >> 2, m = lane & 3;
+      __half* y = static_cast<__half*>(a.y);
+      const __half* res = static_cast<const __half*>(a.res);
+      // this thread's output channels are the same for every item of the launch
+      const int n0 = (PAIR ? 0 : ((int)blockIdx.x % (a.cout / NCTA)) * NCTA) + col0 + CPT * m;
+      float bias[CPT];
+#pragma unroll
+      for (int t = 0; t < CPT; ++t) bias[t] = C::BIAS_SMEM ? sBias[n0 + t] : a.bias_v[n0 + t];
+      // Pixel sr (0..3) of this thread is accumulator row q*32 + k + 8*sr.  When a warp's 32
+      // rows lie in one unit (ONEUNIT) its pixels sit at fixed offsets from the first one.
+      constexpr int UPX = WIN ? C::RPX : (C::TT >= 128 ? 128 : C::TT);  // rows of one unit in an M-tile
+      constexpr bool ONEUNIT = UPX >= 32;
+      constexpr int UW = WIN ? 8 : T;                                    // unit width (px)
+      // destinations and residual of one item (this thread's four pixels), fetched one item ahead
+      struct Row {
+        size_t pix[ONEUNIT ? 1 : 4];  // element of channel n0: pixel 0 (ONEUNIT) or each pixel
+        int p;                        // pixel 0's index within its unit (ONEUNIT)
+        unsigned okm;                 // bit sr: pixel sr is stored
+        uint4 rr[4][CPT / 8];         // residual: CPT channels of each pixel
+      };
+      const size_t rowstride = (size_t)a.wo * a.cout;
+      // offset of pixel sr from pixel 0 (ONEUNIT): unit pixel p + 8 sr, UW pixels per row
+      auto pix_of = [&](const Row& o, int sr) -> size_t {
+        if constexpr (ONEUNIT) {
+          const int p1 = o.p + 8 * sr;
+          return o.pix[0] + (size_t)(p1 / UW - o.p / UW) * rowstride + (ptrdiff_t)(p1 % UW - o.p % UW) * a.cout;
+        } else {
+          return o.pix[sr];
+        }
+      };
+      // unit coordinates come from the producer through the shared-memory ring, so the
+      // residual prefetch below depends on no global load
+      auto fetch = [&](int it, Row& o) -> bool {
+        const Item w = item_of(it);
+        const int slot = it % C::CRING;
+        if (!mbar_wait(&cfull[slot], (it / C::CRING) & 1, abort_flag)) return false;
+        int4 u[4];
+        int ti[4], pp[4];
+#pragma unroll
+        for (int sr = 0; sr < 4; ++sr) {
+          const int r = q * 32 + k + 8 * sr;  // accumulator row of pixel sr
+          int j;
+          if (WIN) { j = r / C::RPX; ti[sr] = w.m * C::TPM + j; pp[sr] = r % C::RPX; }
+          else if (C::TT >= 128) { j = 0; ti[sr] = w.m / C::MPT; pp[sr] = (w.m % C::MPT) * 128 + r; }
+          else { j = r / C::TT; ti[sr] = w.m * C::TPM + j; pp[sr] = r % C::TT; }
+          if (!ONEUNIT || sr == 0) u[sr] = sCoord[slot * 8 + j];
+          else u[sr] = u[0];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cempty[slot]);
+        o.okm = 0u;
+        o.p = pp[0];
+#pragma unroll
+        for (int sr = 0; sr < 4; ++sr) {
+          const int p = pp[sr];
+          const bool valid = ti[sr] < n_tiles;
+          const TileXY tc{u[sr].x, u[sr].y, u[sr].z};
+          const int gy = WIN ? tc.by * C::RROWS + p / 8 : tc.by * T + p / T;
+          const int gx = WIN ? tc.bx * 8 + p % 8 : tc.bx * T + p % T;
+          const bool inb = tc.cam < a.n && gy < a.ho && gx < a.wo;
+          // a region may overhang the image's right / bottom edge (those pixels are skipped);
+          // only a unit whose origin lies outside the image is a corrupt list entry
+          if (sr == 0 || !ONEUNIT) {
+            const bool origin_ok = tc.cam < a.n && (WIN ? tc.by * C::RROWS : tc.by * T) < a.ho &&
+                                   (WIN ? tc.bx * 8 : tc.bx * T) < a.wo;
+            if (valid && !origin_ok) atomicOr(&a.st->error, SB_ERR_BAD_TILE);
+            o.pix[ONEUNIT ? 0 : sr] = (((size_t)tc.cam * a.ho + gy) * a.wo + gx) * a.cout + n0;
+          }
+          const bool st = valid && inb;
+          if (st) o.okm |= 1u << sr;
+          if (res != nullptr) {
+            const size_t px = pix_of(o, sr);
+            if constexpr (CPT == 16) {
+              if (st) ld_global_nc_v8(res + px, o.rr[sr][0], o.rr[sr][1]);
+              else o.rr[sr][0] = o.rr[sr][1] = make_uint4(0, 0, 0, 0);
+            } else {
+              o.rr[sr][0] = st ? __ldg(reinterpret_cast<const uint4*>(res + px)) : make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+        return true;
+      };
+      // bias / residual / ReLU / store of pixel sr from its fragment registers f
+      // (registers 4j + b hold channels CPT*m + 2j + b)
+      auto out_pixel = [&](const Row& cu, int sr, const uint32_t* f) {
+        if (!((cu.okm >> sr) & 1u)) return;
+        const uint32_t* rw = reinterpret_cast<const uint32_t*>(&cu.rr[sr][0]);
+        uint32_t o[CPT / 2];
+#pragma unroll
+        for (int jj = 0; jj < REP; ++jj) {
+          float f0 = __uint_as_float(f[4 * jj]) + bias[2 * jj];
+          float f1 = __uint_as_float(f[4 * jj + 1]) + bias[2 * jj + 1];
+          if (res != nullptr) {
+            const float2 t2 = __half22float2(*reinterpret_cast<const __half2*>(&rw[jj]));
+            f0 += t2.x;
+            f1 += t2.y;
+          }
+          if (a.act) {
+            f0 = fmaxf(f0, 0.0f);
+            f1 = fmaxf(f1, 0.0f);
+          }
+          __half2 h2 = __floats2half2_rn(f0, f1);
+          o[jj] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        __half* dst = y + pix_of(cu, sr);
+        if constexpr (CPT == 16)
+          st_global_v8(dst, make_uint4(o[0], o[1], o[2], o[3]), make_uint4(o[4], o[5], o[6], o[7]));
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+      };
+      // one item: wait for the accumulator, move its fragments to registers, release TMEM and
+      // prefetch the next item into `nx`, bias / residual / ReLU / store the four pixels
+      auto step = [&](int it, const Row& cu, Row& nx) -> bool {
+        const int ab = it % C::NACC;
+        const bool got = mbar_wait(&accf[ab], (it / C::NACC) & 1, abort_flag);
+        if (!got) {
+          atomicOr(&a.st->error, SB_ERR_TIMEOUT_ACC);
+          *abort_flag = 1;
+        }
+        // warp-uniform exit: tcgen05.ld below is .sync.aligned
+        if (__any_sync(0xFFFFFFFFu, !got || *abort_flag != 0)) return false;
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + ab * C::NMMA + col0;
+        auto ld_frag = [&](int hh, uint32_t* v) {
+          if constexpr (REP == 8)
+            tmem_ld16x256b8(taddr + ((uint32_t)(16 * hh) << 16), *reinterpret_cast<uint32_t(*)[32]>(v));
+          else
+            tmem_ld16x256b4(taddr + ((uint32_t)(16 * hh) << 16), *reinterpret_cast<uint32_t(*)[16]>(v));
+        };
+        auto release = [&]() {
+          tc_fence_before();
+          // one arrival per warp (on the pair leader's barrier): the MMA may overwrite it now
+          __syncwarp();
+          if (lane == 0) {
+            if (PAIR) mbar_arrive_cluster(mapa_shared(smem_u32(&acce[ab]), 0));
+            else mbar_arrive(&acce[ab]);
+          }
+          if (it + C::EPG < my_items && !fetch(it + C::EPG, nx)) {
+            atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+            *abort_flag = 1;
+          }
+        };
+        if constexpr (!PAIR) {
+          // both fragments to registers, release the buffer at once, then the four pixels
+          uint32_t v[2][4 * REP];
+          ld_frag(0, v[0]);
+          ld_frag(1, v[1]);
+          tmem_ld_wait();
+          release();
+#pragma unroll
+          for (int sr = 0; sr < 4; ++sr) out_pixel(cu, sr, &v[sr >> 1][2 * (sr & 1)]);
+        } else {
+          // CTA pairs (fewer registers to spare): lanes 32q.. -> pixels 0, 1 first, then
+          // lanes 32q + 16.., release, pixels 2, 3
+          uint32_t v[4 * REP];
+          ld_frag(0, v);
+          tmem_ld_wait();
+          out_pixel(cu, 0, &v[0]);
+          out_pixel(cu, 1, &v[2]);
+          ld_frag(1, v);
+          tmem_ld_wait();
+          release();
+          out_pixel(cu, 2, &v[0]);
+          out_pixel(cu, 3, &v[2]);
+        }
+        return true;
+      };
+      // this group's items: eg, eg + EPG, ...
+      Row ra, rb;
+      if (eg < my_items && !fetch(eg, ra)) {
+        atomicOr(&a.st->error, SB_ERR_TIMEOUT_FULL);
+        *abort_flag = 1;
+      }
+      for (int it = eg; it < my_items; it += 2 * C::EPG) {
+        if (!step(it, ra, rb) || it + C::EPG >= my_items) break;
+        if (!step(it + C::EPG, rb, ra)) break;
+      }
     } else if (warp < 8) {
       grid_dep_wait();  // residual caches of earlier layers are complete
       // ------------------------------------------------ epilogue: TMEM -> bias/res/ReLU -> cache
@@ -982,6 +1177,16 @@ int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s) {
 // Weight image for the tcgen05 B operand: per C_out slice, per K-block (tap-major,
 // then channel chunk), NCTA rows of ROWB bytes, K-major, with the 128B/64B swizzle
 // applied exactly as the MMA reads it from a 1024-byte-aligned shared buffer.
+// Output-channel order of the weight image of CTA-pair variants (B rows = accumulator
+// columns): within each group of g = 64 columns (one epilogue warp's), column 8j + 2m + b
+// holds channel (g / 4) * m + 2j + b, so that a 16x256b TMEM fragment gives each thread g / 4
+// consecutive channels of its pixels (see the pair epilogue).  Other variants keep the
+// natural order.
+int out_channel_of_column(int n, int g) {
+  const int c = n % g, j = c / 8, m = (c % 8) / 2, b = c % 2;
+  return (n / g) * g + (g / 4) * m + 2 * j + b;
+}
+
 void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_t* out) {
   const Variant* v = picked(cin, cout, t, s);
   if (!v) return;
@@ -996,7 +1201,7 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_
       for (int kb = 0; kb < 6; ++kb) {
         const int ky = kb / 2, tap = kb % 2;
         for (int n = 0; n < ncta; ++n) {
-          const int co = sp * ncta + n;
+          const int co = sp * ncta + (v->pair ? out_channel_of_column(n, v->ncol) : n);
           for (int k = 0; k < v->ch; ++k) {
             const int dx = k / cin, c = k % cin;
             const int kx = tap == 0 ? (dx == 1 ? 0 : -1) : 1 + dx;
@@ -1021,7 +1226,7 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_
     std::memset(img, 0, (size_t)v->w_bytes);
     for (int kb = 0; kb < nkb; ++kb) {
       for (int n = 0; n < ncta; ++n) {
-        const int co = sp * ncta + n;
+        const int co = sp * ncta + (v->pair ? out_channel_of_column(n, v->ncol) : n);
         for (int k = 0; k < ch; ++k) {
           float val = 0.f;
           if (manual) {
