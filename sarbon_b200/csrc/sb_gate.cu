@@ -414,9 +414,14 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
         // blocks: max_pool(2d+1) of `changed` (fused_engine.py:151); regions: any of their blocks
         const int y0 = max(0, ry * rh - d), y1 = min(a.hb - 1, ry * rh + rh - 1 + d);
         const int x0 = max(0, rx * rw - d), x1 = min(a.wb - 1, rx * rw + rw - 1 + d);
-        for (int y = y0; y <= y1 && !on; ++y)
-          for (int x = x0; x <= x1; ++x)
-            if (__ldg(cm + y * a.wb + x)) { on = true; break; }
+        // OR of the window's bytes, no early exit: the loads are independent and overlap
+        uint32_t acc = 0;
+        for (int y = y0; y <= y1; ++y) {
+          const uint8_t* rowp = cm + y * a.wb;
+#pragma unroll 4
+          for (int x = x0; x <= x1; ++x) acc |= __ldg(rowp + x);
+        }
+        on = acc != 0;
         if (kind == 0) a.masks[(size_t)di * a.n_blocks + f] = on ? 1 : 0;
       }
       act[L] = on;

@@ -16,7 +16,7 @@ namespace sb {
 
 // Blocks per CTA of the list kernel (a multiple of 32); the look-back status arrays hold
 // one word per chunk = ceil(n_blocks / SB_LIST_CHUNK) per compaction lane.
-#define SB_LIST_CHUNK 256
+#define SB_LIST_CHUNK 1024
 
 // Device-resident engine state.  Written only by the engine's own kernels (and by
 // cudaMemcpyAsync for host-set knobs), so a whole step runs without a host sync.

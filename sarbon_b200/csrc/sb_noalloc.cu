@@ -29,7 +29,8 @@ constexpr size_t kStatusOffset = (sizeof(State) + 255) / 256 * 256;
 constexpr size_t kScratchBytes = kStatusOffset + (size_t)SB_MAX_DILATIONS * kMaxChunks * 8;
 static_assert(kMaxBlocks % kChunk == 0, "the block limit is a whole number of list chunks");
 
-// 128 KB of look-back words + one State: [State | pad to 256 | status[n_dil][n_chunks]].
+// Look-back words (SB_MAX_DILATIONS x SB_STATIC_LISTS_MAX_BLOCKS / SB_LIST_CHUNK x 8 bytes) + one
+// State: [State | pad to 256 | status[n_dil][n_chunks]].
 static __device__ __align__(256) unsigned char g_lists_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
