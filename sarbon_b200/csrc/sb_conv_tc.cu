@@ -1077,9 +1077,10 @@ struct Variant {
 template <int CIN, int NCTA, int T, int S, int WIN = 0, int PAIR = 0>
 Variant make_variant(int cout) {
   using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
-  return Variant{CIN,       cout,       T,         S,         WIN,       NCTA,      PAIR,
+  Variant v{CIN,       cout,       T,         S,         WIN,       NCTA,      PAIR,
                  conv_tc_kernel<CIN, NCTA, T, S, WIN, PAIR>,  C::SMEM,   C::THREADS, C::W_BYTES,
                  C::CH,     C::BOX_ROWS, C::WIN_COLS, C::WIN_ROWS, C::TSTORE ? 1 : 0, C::NCOL, C::OBW};
+  return v;
 }
 
 // Sarbon stem shapes (widths 32/64/128, Res blocks) at block 32 and block 64.  The first
@@ -1090,6 +1091,7 @@ const std::vector<Variant>& variants() {
       make_variant<3, 32, 16, 2>(32),
       make_variant<32, 64, 8, 2, 2>(64),       // pair windows over blocks
       make_variant<32, 64, 8, 2>(64),
+      make_variant<64, 32, 8, 1, 1, 1>(64),    // CTA pairs (M=256, N=64), row windows over blocks
       make_variant<64, 64, 8, 1, 1>(64),       // row windows over blocks
       make_variant<64, 64, 8, 1, 3>(64),       // full windows over 1x2-block regions
       make_variant<64, 64, 4, 2, 2, 1>(128),   // CTA pairs, strided windows over 2x1-block regions
@@ -1149,46 +1151,45 @@ int conv_tc_pick_mode(int cin, int cout, int t, int s) {
 }
 
 namespace {
-// The variant the engine runs (and whose weight image it builds) for a shape.
-const Variant* picked(int cin, int cout, int t, int s) {
-  const int m = conv_tc_pick_mode(cin, cout, t, s);
-  return m < 0 ? nullptr : find_variant(cin, cout, t, s, m);
+// The variant the engine runs (and whose weight image it builds) for a layer of mode `mode`.
+const Variant* picked(int cin, int cout, int t, int s, int mode) {
+  return mode < 0 ? nullptr : find_variant(cin, cout, t, s, mode);
 }
 }  // namespace
 
 bool conv_tc_supported(int cin, int cout, int t, int s) { return find_variant(cin, cout, t, s) != nullptr; }
 
-int conv_tc_nsplit(int cin, int cout, int t, int s) {
-  const Variant* v = picked(cin, cout, t, s);
+int conv_tc_nsplit(int cin, int cout, int t, int s, int mode) {
+  const Variant* v = picked(cin, cout, t, s, mode);
   return v ? v->cout / v->ncta : 0;
 }
 
-size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s) {
-  const Variant* v = picked(cin, cout, t, s);
+size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode) {
+  const Variant* v = picked(cin, cout, t, s, mode);
   return v ? (size_t)v->w_bytes * (v->cout / v->ncta) : 0;
 }
 
-int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s) {
-  const Variant* v = picked(cin, cout, t, s);
+int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s, int mode) {
+  const Variant* v = picked(cin, cout, t, s, mode);
   if (!v) return 0;
   return 1;
 }
 
-// Weight image for the tcgen05 B operand: per C_out slice, per K-block (tap-major,
-// then channel chunk), NCTA rows of ROWB bytes, K-major, with the 128B/64B swizzle
-// applied exactly as the MMA reads it from a 1024-byte-aligned shared buffer.
 // Output-channel order of the weight image of CTA-pair variants (B rows = accumulator
-// columns): within each group of g = 64 columns (one epilogue warp's), column 8j + 2m + b
-// holds channel (g / 4) * m + 2j + b, so that a 16x256b TMEM fragment gives each thread g / 4
-// consecutive channels of its pixels (see the pair epilogue).  Other variants keep the
-// natural order.
+// columns of the pair, both CTAs' halves together): within each group of g = 64 columns
+// (one epilogue warp's), column 8j + 2m + b holds channel (g / 4) * m + 2j + b, so that a
+// 16x256b TMEM fragment gives each thread g / 4 consecutive channels of its pixels (see the
+// pair epilogue).  Other variants keep the natural order.
 int out_channel_of_column(int n, int g) {
   const int c = n % g, j = c / 8, m = (c % 8) / 2, b = c % 2;
   return (n / g) * g + (g / 4) * m + 2 * j + b;
 }
 
-void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_t* out) {
-  const Variant* v = picked(cin, cout, t, s);
+// Weight image for the tcgen05 B operand: per C_out slice, per K-block (tap-major,
+// then channel chunk), NCTA rows of ROWB bytes, K-major, with the 128B/64B swizzle
+// applied exactly as the MMA reads it from a 1024-byte-aligned shared buffer.
+void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w, uint16_t* out) {
+  const Variant* v = picked(cin, cout, t, s, mode);
   if (!v) return;
   if (v->win == 2 && cin == 32) {
     // pair windows: block ky*2 + tap; K element k = (dx, c) of a pixel pair; tap 0 (pair
@@ -1201,7 +1202,7 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_
       for (int kb = 0; kb < 6; ++kb) {
         const int ky = kb / 2, tap = kb % 2;
         for (int n = 0; n < ncta; ++n) {
-          const int co = sp * ncta + (v->pair ? out_channel_of_column(n, v->ncol) : n);
+          const int co = v->pair ? out_channel_of_column(sp * ncta + n, v->ncol) : sp * ncta + n;
           for (int k = 0; k < v->ch; ++k) {
             const int dx = k / cin, c = k % cin;
             const int kx = tap == 0 ? (dx == 1 ? 0 : -1) : 1 + dx;
@@ -1226,7 +1227,7 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w, uint16_
     std::memset(img, 0, (size_t)v->w_bytes);
     for (int kb = 0; kb < nkb; ++kb) {
       for (int n = 0; n < ncta; ++n) {
-        const int co = sp * ncta + (v->pair ? out_channel_of_column(n, v->ncol) : n);
+        const int co = v->pair ? out_channel_of_column(sp * ncta + n, v->ncol) : sp * ncta + n;
         for (int k = 0; k < ch; ++k) {
           float val = 0.f;
           if (manual) {

@@ -469,7 +469,7 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
   for (int i = 0; i < n_layers; ++i) {
     const sb_layer_desc& L = layers[i];
     if ((rc = alloc_dev(e, (void**)&e->bias[i], (size_t)L.cout * 4))) return bail(rc);
-    const size_t wbytes = dtype == SB_F16 ? conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[i], L.stride)
+    const size_t wbytes = dtype == SB_F16 ? conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[i], L.stride, e->layer_mode[i])
                                           : (size_t)9 * L.cin * L.cout * 4;
     if ((rc = alloc_dev(e, &e->wdev[i], wbytes))) return bail(rc);
     if (dtype == SB_F16) {  // every fp16 layer loads its input by TMA (the first layer: window boxes)
@@ -496,9 +496,9 @@ int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias
   SB_CUDA(cudaMemcpy(e->bias[layer], bias, (size_t)L.cout * 4, cudaMemcpyHostToDevice));
   for (int c = 0; c < L.cout && c < 128; ++c) e->bias_h[layer][c] = bias[c];
   if (e->dtype == SB_F16) {
-    const size_t bytes = conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[layer], L.stride);
+    const size_t bytes = conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer]);
     std::vector<uint16_t> img(bytes / 2);
-    conv_tc_build_wimg(L.cin, L.cout, e->layer_t[layer], L.stride, w, img.data());
+    conv_tc_build_wimg(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer], w, img.data());
     SB_CUDA(cudaMemcpy(e->wdev[layer], img.data(), bytes, cudaMemcpyHostToDevice));
   } else {
     SB_CUDA(cudaMemcpy(e->wdev[layer], w, (size_t)9 * L.cin * L.cout * 4, cudaMemcpyHostToDevice));

@@ -117,9 +117,9 @@ bool conv_tc_supported(int cin, int cout, int t, int s);  // some mode exists fo
 // 1 per-ky row windows over (8/t)x1-block regions, 3 full windows over (8/t)x(16/t)
 // regions; plus 8 when 2-CTA clusters run M=256 cta_group::2 MMAs
 int conv_tc_pick_mode(int cin, int cout, int t, int s);
-int conv_tc_nsplit(int cin, int cout, int t, int s);   // CTA splits of cout
-size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s);  // all splits
-void conv_tc_build_wimg(int cin, int cout, int t, int s, const float* w /*[3][3][cin][cout]*/,
+int conv_tc_nsplit(int cin, int cout, int t, int s, int mode);   // CTA splits of cout
+size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode);  // all splits
+void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w /*[3][3][cin][cout]*/,
                         uint16_t* out /* fp16 bits */);
 cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s,
                               int mode);
@@ -129,7 +129,7 @@ cudaError_t conv_tc_make_tmap_out(CUtensorMap* map, void* dst, int n, int ho, in
                                   int mode);
 cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, const CUtensorMap* map_y, int grid_x,
                            cudaStream_t s);
-int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s);
+int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s, int mode);
 
 // Sets the message sb_last_error() returns on this thread; returns `code`.
 int record_error(int code, const char* msg);
