@@ -150,6 +150,12 @@ SB_API int sb_run_sparse_forced(sb_engine* e, const void* frames_dev, int64_t n_
  * cache id (0 = image, i+1 = layer i output). */
 SB_API int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]);
 
+/* Which tile-conv kernel variant layer `layer` runs: *mode = window mode (0 per-tap boxes or
+ * first-layer gather, 1 row windows, 2 strided windows, 3 full windows) + 8 for CTA pairs;
+ * -1 for an fp32 engine (CUDA-core kernel).  Introspection only; no reference counterpart
+ * (the reference has a single Triton tile kernel, triton_conv.py:15-86). */
+SB_API int sb_layer_variant(sb_engine* e, int layer, int* mode);
+
 /* Gate buffers (uint8 device pointers, engine-owned): `changed` [N][Hb][Wb], masks
  * [n_dil][N][Hb][Wb] (fused_engine.py:74-77) and the `extra` mask [N][Hb][Wb] the
  * next step ORs into the change mask (writing it directly equals sb_set_extra). */

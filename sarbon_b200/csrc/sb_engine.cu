@@ -628,6 +628,13 @@ int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]) {
   return SB_OK;
 }
 
+int sb_layer_variant(sb_engine* e, int layer, int* mode) {
+  if (!e || !mode) return fail(SB_EINVAL, "null argument");
+  if (layer < 0 || layer >= e->n_layers) return fail(SB_EINVAL, "layer out of range");
+  *mode = e->dtype == SB_F16 ? e->layer_mode[layer] : -1;
+  return SB_OK;
+}
+
 int sb_gate_buffers(sb_engine* e, uint8_t** changed, uint8_t** masks, uint8_t** extra, int* n_dilations,
                     int dilations[SB_MAX_DILATIONS]) {
   if (!e) return fail(SB_EINVAL, "null engine");

@@ -318,6 +318,16 @@ class FusedSparseEngine:
     def launch_count(self):
         return lib().sb_last_launch_count(self._h.ptr)
 
+    def layer_variants(self):
+        """Per layer, the tile-conv variant it runs: window mode (0 per-tap boxes / first-layer
+        gather, 1 row, 2 strided, 3 full windows) + 8 for CTA pairs; -1 on fp32 engines."""
+        out = []
+        for i in range(len(self.layers)):
+            m = C.c_int()
+            check(lib().sb_layer_variant(self._h.ptr, i, C.byref(m)), "sb_layer_variant")
+            out.append(int(m.value))
+        return out
+
     @torch.no_grad()
     def calibrate(self, reps=15, margin=0.95, dense_ref=None):
         """Time every budget bucket against the dense pass; set the crossover (:242-275).
