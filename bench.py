@@ -257,8 +257,19 @@ def run_b200(args):
     from sarbon_b200.multi import job_rate, max_over_ranks
     rank, world, local = dist_env()
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
+        # NCCL prints its version banner on stdout when a communicator starts; send it to
+        # stderr so that rank 0's stdout stays the single JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                    device_id=torch.device("cuda", local))
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     tau = 8 / float(scenes.STD.mean())
