@@ -139,10 +139,6 @@ SB_DEV void ld_global_nc_v8(const void* p, uint4& lo, uint4& hi) {
                : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
                : "l"(p));
 }
-// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned address, bytes % 16 == 0).
-SB_DEV void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 SB_DEV void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
