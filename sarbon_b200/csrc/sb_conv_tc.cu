@@ -7,21 +7,24 @@
 // padding only at the image border, epilogue writing straight into the output cache.
 //
 // B200 design (not a translation of the Triton kernel):
-//   * persistent CTAs (one per SM) loop over 128-pixel M-tiles of the active-tile list;
-//     the list length and the skip/sparse/dense mode are read from device memory, so the
-//     launch needs no host sync;
-//   * the whole weight matrix of the CTA's C_out slice stays resident in shared memory
-//     (one bulk copy of a pre-swizzled image per CTA);
-//   * the im2col A operand of each (tap, 64-channel chunk) is fetched by TMA: one
-//     4-D tiled box per tile, [chunk][t px][t rows][cam] with element strides = conv
-//     stride, so the hardware does the strided gather and the image-border zero fill;
-//   * one elected thread issues tcgen05.mma (M=128, N=C_out slice, K=16 steps) from the
-//     swizzled smem stages into a double-buffered TMEM accumulator;
-//   * four epilogue warps read TMEM (tcgen05.ld 32x32b), add bias and residual, apply
-//     ReLU and store 16-byte vectors into the destination cache while the next M-tile's
-//     MMAs run.
+//   * persistent CTAs (one per SM, or one 2-CTA cluster per SM pair) loop over 128-pixel
+//     M-tiles of the step's unit list; the list length and the skip/sparse/dense mode are
+//     read from device memory, so the launch needs no host sync;
+//   * the weights of the CTA's output channels stay resident in shared memory (one bulk
+//     copy of a pre-swizzled image, started before the programmatic-launch wait);
+//   * A tiles come by TMA from the NHWC cache: row windows (one box per ky feeds the three
+//     kx taps through shifted descriptors), strided windows for stride 2, full windows or
+//     per-tap im2col boxes as selectable variants; out-of-image coordinates zero-fill;
+//   * one TMA producer warp and one MMA issuer thread per stage sub-ring (two of each when
+//     the ring holds enough stages) keep tcgen05.mma fed; CTA pairs run cta_group::2 M=256
+//     MMAs with each CTA holding half the output channels;
+//   * epilogue warps read the TMEM accumulator, add bias and residual, apply ReLU, round
+//     once to fp16 and write the destination cache: CTA pairs read 16x256b fragments of a
+//     permuted channel order (whole-line stores), window layers stage each warp's pixels
+//     for one TMA tile store, the first layer stores 32-byte sectors per pixel;
 //   * the 3-channel first layer cannot be fetched by TMA (6-byte pixels); its A rows
-//     (27 taps x channels, zero-padded to K=32) are gathered by four producer warps.
+//     (27 taps x channels, zero-padded to K=32) are gathered by producer warps from a
+//     TMA-loaded input window.
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
