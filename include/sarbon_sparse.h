@@ -150,6 +150,16 @@ SB_API int sb_run_sparse_forced(sb_engine* e, const void* frames_dev, int64_t n_
  * cache id (0 = image, i+1 = layer i output). */
 SB_API int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]);
 
+/* Cell-level gating (gating.py:42-43, `active_blocks_cell_level`): from a change mask of
+ * cell x cell-pixel cells, `cells_dev` uint8 [n_cams][hc][wc] (nonzero = changed), write for
+ * each receptive radius radii[i] (image pixels) the active blocks of block x block pixels:
+ * out_dev uint8 [n_radii][n_cams][hc*cell/block][wc*cell/block], a block being active when
+ * the cells dilated by ceil(radii[i] / cell) cells reach it.  block must be a multiple of
+ * cell and hc, wc multiples of block / cell; 1 <= n_radii <= 16.  One kernel on `stream`,
+ * no allocation. */
+SB_API int sb_cell_active_blocks(const uint8_t* cells_dev, int n_cams, int hc, int wc, int cell, int block,
+                                 const int* radii, int n_radii, uint8_t* out_dev, void* stream);
+
 /* Which tile-conv kernel variant layer `layer` runs: *mode = window mode (0 per-tap boxes or
  * first-layer gather, 1 row windows, 2 strided windows, 3 full windows) + 8 for CTA pairs;
  * -1 for an fp32 engine (CUDA-core kernel).  Introspection only; no reference counterpart

@@ -16,6 +16,7 @@ kernel ``sarbon/sparse/triton_conv.py`` (``_tile_conv_kernel``):
 * dense pass      fused_engine.py:172-185
 * dispatch        fused_engine.py:214-240   (skip / sparse / dense, hysteresis)
 * buckets         fused_engine.py:44-51, 188-193; triton_conv.py:64-69
+* cell gating     gating.py:31-43           (cells dilated, then any-pooled into blocks)
 
 Number semantics (pinned against the reference by ``tests/golden``):
 
@@ -155,6 +156,24 @@ def dilate(mask, d):
         for dx in range(2 * d + 1):
             out |= p[:, dy:dy + hb, dx:dx + wb]
     return out
+
+
+def cells_to_blocks(mask, k):
+    """Any-pool k x k cells of a bool [N, Hc, Wc] mask into [N, Hc/k, Wc/k] blocks
+    (gating.py:31-34)."""
+    n, hc, wc = mask.shape
+    return mask.reshape(n, hc // k, k, wc // k, k).any(axis=(2, 4))
+
+
+def active_blocks_cell_level(cells, radius, cell, block):
+    """Blocks whose cells, dilated by ceil(radius / cell) cells, hold a change
+    (gating.py:42-43)."""
+    return cells_to_blocks(dilate(cells, -(-radius // cell)), block // cell)
+
+
+def active_blocks_block_level(cells, radius, cell, block):
+    """Changed blocks dilated by ceil(radius / block) blocks (gating.py:37-39)."""
+    return dilate(cells_to_blocks(cells, block // cell), -(-radius // block))
 
 
 def block_lists(mask, cap=None):

@@ -5,13 +5,15 @@ Public API (mirrors ``sarbon.sparse``):
 * :class:`FusedSparseEngine` -- the engine (CUDA library ``libsarbon_sparse.so``).
 * :class:`LocalBackbone`, :func:`stem_to_local`, :func:`fold` -- stem topology and BN folding.
 * :func:`budget_buckets` -- the reference's budget schedule.
+* :func:`cell_active_blocks` -- cell-level gating (``gating.py``) on the GPU.
 
 Importing the package does not load the CUDA library; constructing an engine does, and
 raises :class:`SarbonLibraryError` when it is missing.
 """
 from ._lib import SarbonLibraryError
 from .fused_engine import FusedSparseEngine, budget_buckets, fuse_layers
+from .gating import cell_active_blocks
 from .local import LocalBackbone, Node, fold, stem_to_local
 
-__all__ = ["FusedSparseEngine", "LocalBackbone", "Node", "SarbonLibraryError", "budget_buckets", "fold",
-           "fuse_layers", "stem_to_local"]
+__all__ = ["FusedSparseEngine", "LocalBackbone", "Node", "SarbonLibraryError", "budget_buckets",
+           "cell_active_blocks", "fold", "fuse_layers", "stem_to_local"]
