@@ -160,6 +160,19 @@ SB_API int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]
 SB_API int sb_cell_active_blocks(const uint8_t* cells_dev, int n_cams, int hc, int wc, int cell, int block,
                                  const int* radii, int n_radii, uint8_t* out_dev, void* stream);
 
+/* Track-steered block masks (video.py:26-34 `boxes_to_block_mask`, as `SarbonVideo._steer`
+ * uses it at video.py:139-147): out_dev uint8 [n_cams][hb][wb] = 1 where a block of
+ * block x block pixels lies in a box's block range, rows max(0, floor(y0/block) - margin) ..
+ * min(hb-1, floor(y1/block) + margin) and likewise for columns; 0 elsewhere (the mask is
+ * overwritten).  boxes_dev: float64 [n_boxes][4] xyxy in engine pixels; offsets_dev: int32
+ * [n_cams + 1], camera c owning rows offsets[c] .. offsets[c+1]-1 (clamped to
+ * [0, n_boxes]).  Boxes with a non-finite coordinate mark nothing (the reference raises on
+ * them; the Python wrapper does too).  boxes_dev may be null when n_boxes == 0.  Writing
+ * into the engine's `extra` mask (sb_gate_buffers) steers its next step.  One kernel on
+ * `stream`, no allocation. */
+SB_API int sb_boxes_to_block_mask(const double* boxes_dev, const int* offsets_dev, int n_boxes, int n_cams,
+                                  int hb, int wb, int block, int margin, uint8_t* out_dev, void* stream);
+
 /* Which tile-conv kernel variant layer `layer` runs: *mode = window mode (0 per-tap boxes or
  * first-layer gather, 1 row windows, 2 strided windows, 3 full windows) + 8 for CTA pairs;
  * -1 for an fp32 engine (CUDA-core kernel).  Introspection only; no reference counterpart

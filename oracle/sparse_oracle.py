@@ -17,6 +17,7 @@ kernel ``sarbon/sparse/triton_conv.py`` (``_tile_conv_kernel``):
 * dispatch        fused_engine.py:214-240   (skip / sparse / dense, hysteresis)
 * buckets         fused_engine.py:44-51, 188-193; triton_conv.py:64-69
 * cell gating     gating.py:31-43           (cells dilated, then any-pooled into blocks)
+* steered masks   video.py:26-34            (track boxes -> blocks, widened by a margin)
 
 Number semantics (pinned against the reference by ``tests/golden``):
 
@@ -174,6 +175,21 @@ def active_blocks_cell_level(cells, radius, cell, block):
 def active_blocks_block_level(cells, radius, cell, block):
     """Changed blocks dilated by ceil(radius / block) blocks (gating.py:37-39)."""
     return dilate(cells_to_blocks(cells, block // cell), -(-radius // block))
+
+
+def boxes_to_block_mask(boxes, hb, wb, block, margin=0):
+    """Track-steered mask of one camera (video.py:26-34): for each xyxy box in engine
+    pixels, the block range from floor(lo / block) - margin to floor(hi / block) + margin,
+    clipped to the grid, set when it is non-empty on both axes.  Python's float floor
+    division is the exact floor of the real quotient; NaN and +-inf coordinates give a
+    NaN quotient, whose ``int`` raises ValueError, as in the reference."""
+    mask = np.zeros((hb, wb), bool)
+    for x0, y0, x1, y1 in boxes:
+        lo_r, hi_r = max(0, int(y0 // block) - margin), min(hb - 1, int(y1 // block) + margin)
+        lo_c, hi_c = max(0, int(x0 // block) - margin), min(wb - 1, int(x1 // block) + margin)
+        if lo_r <= hi_r and lo_c <= hi_c:
+            mask[lo_r:hi_r + 1, lo_c:hi_c + 1] = True
+    return mask
 
 
 def block_lists(mask, cap=None):

@@ -12,8 +12,8 @@ raises :class:`SarbonLibraryError` when it is missing.
 """
 from ._lib import SarbonLibraryError
 from .fused_engine import FusedSparseEngine, budget_buckets, fuse_layers
-from .gating import cell_active_blocks
+from .gating import boxes_to_block_mask, boxes_to_block_masks, cell_active_blocks
 from .local import LocalBackbone, Node, fold, stem_to_local
 
 __all__ = ["FusedSparseEngine", "LocalBackbone", "Node", "SarbonLibraryError", "budget_buckets",
-           "cell_active_blocks", "fold", "fuse_layers", "stem_to_local"]
+           "boxes_to_block_mask", "boxes_to_block_masks", "cell_active_blocks", "fold", "fuse_layers", "stem_to_local"]

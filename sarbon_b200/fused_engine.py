@@ -9,6 +9,8 @@ unchanged:
   tau=0.0, refresh=0, dense_check_every=4, device="cuda")``  (:55-56)
 * ``reset(frames)``, ``step(frames) -> (mode, k)``, ``calibrate(...)``,
   ``set_extra(mask)``, ``outputs_nchw()``, ``dilation(radius)``  (:121-275)
+* added: ``steer(boxes_per_cam, margin=1)``, the caller's track steering
+  (``sarbon/inference/video.py:139-147``) as one kernel writing ``extra``
 * attributes ``n, h, w, block, hb, wb, n_blocks, dtype, tau, refresh, layers, ds,
   outputs, cache, frames, changed, extra, masks, buckets, fallback,
   dense_check_every, dense_graph, stats``.
@@ -242,6 +244,15 @@ class FusedSparseEngine:
     def set_extra(self, mask):
         """Blocks [N, Hb, Wb] recomputed next step regardless of pixel change (:201-205)."""
         self.extra.copy_(mask)  # a view of the engine's mask: the next gate reads it
+
+    def steer(self, boxes_per_cam, margin=1):
+        """Track steering (video.py:139-147): the blocks each camera's predicted boxes
+        (xyxy, engine pixels) touch, widened by ``margin`` blocks, become the ``extra`` mask
+        of the next step.  One kernel writes the engine's mask from the uploaded boxes."""
+        from .gating import boxes_to_block_masks
+        if len(boxes_per_cam) != self.n:
+            raise ValueError(f"need one box list per camera ({self.n}), got {len(boxes_per_cam)}")
+        boxes_to_block_masks(boxes_per_cam, self.hb, self.wb, self.block, margin, out=self.extra)
 
     def block_lists(self, d):
         """Active (cam, by, bx) int32 lists of dilation d from the last gated step."""
