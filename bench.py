@@ -64,6 +64,7 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-stats", action="store_true", help="skip the untimed statistics cycle")
+    p.add_argument("--no-masks", action="store_true", help="skip timing the mask utility kernels")
     p.add_argument("--cpu-seconds", type=float, default=20.0)
     return p.parse_args()
 
@@ -224,6 +225,82 @@ def cpu_run(net, frames_seq, tau, max_steps, seconds):
             break
     dt = time.perf_counter() - t0
     return n / dt, n, os.cpu_count()
+
+
+def time_mask_kernels(dev, S, H, W, block, seconds=2.0):
+    """Per-call times of the two mask utilities beside the step, at the bench's grid:
+    track-steered masks (100 predicted boxes a camera, margin 1; the reference's
+    ``_steer``, video.py:139-147) and cell-level masks (8 px cells, 1 % changed, the 11
+    receptive radii of the stem; gating.py:42-43).  ``kernel_us``: back-to-back launches
+    through the C ABI on device-resident inputs (CUDA events); ``api_us``: the Python call
+    a user makes, synchronised, including the box upload; ``cpu_us``: the host restatement
+    of the reference's loop (one thread), the cost that the kernel replaces."""
+    import ctypes as C
+    from oracle import sparse_oracle as so
+    from sarbon_b200 import boxes_to_block_masks, cell_active_blocks
+    from sarbon_b200._lib import check, lib
+    hb, wb = H // block, W // block
+    rng = np.random.default_rng(3)
+    per = []
+    for _ in range(S):
+        xy = rng.uniform(0, [W, H], (100, 2))
+        wh = rng.uniform(8, 240, (100, 2))
+        per.append(np.concatenate([xy, xy + wh], 1))
+    out = torch.empty((S, hb, wb), dtype=torch.bool, device=dev)
+    boxes = torch.from_numpy(np.concatenate(per)).to(dev)
+    offsets = torch.arange(0, 100 * S + 1, 100, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    L = lib()
+
+    def events(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return 1e3 * e0.elapsed_time(e1) / n
+
+    def wall(fn, budget):
+        fn()
+        torch.cuda.synchronize(dev)
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < budget:
+            fn()
+            n += 1
+        torch.cuda.synchronize(dev)
+        return 1e6 * (time.perf_counter() - t0) / n
+
+    args_b = (C.c_void_p(boxes.data_ptr()), C.c_void_p(offsets.data_ptr()), 100 * S, S, hb, wb, block, 1,
+              C.c_void_p(out.data_ptr()), C.c_void_p(stream.cuda_stream))
+    k_box = events(lambda: check(L.sb_boxes_to_block_mask(*args_b), "sb_boxes_to_block_mask"), 500)
+    a_box = wall(lambda: boxes_to_block_masks(per, hb, wb, block, 1, out=out), seconds / 4)
+    c_box = wall(lambda: np.stack([so.boxes_to_block_mask(b, hb, wb, block, 1) for b in per]), seconds / 4)
+
+    cell = 8
+    radii = [1, 3, 7, 11, 15, 19, 23, 31, 39, 47, 55]
+    g = torch.Generator(device=dev).manual_seed(4)
+    cells = (torch.rand(S, H // cell, W // cell, device=dev, generator=g) < 0.01).view(torch.uint8)
+    cout = torch.empty((len(radii), S, hb, wb), dtype=torch.uint8, device=dev)
+    r_arr = (C.c_int * len(radii))(*radii)
+    args_c = (C.c_void_p(cells.data_ptr()), S, H // cell, W // cell, cell, block, r_arr, len(radii),
+              C.c_void_p(cout.data_ptr()), C.c_void_p(stream.cuda_stream))
+    k_cell = events(lambda: check(L.sb_cell_active_blocks(*args_c), "sb_cell_active_blocks"), 500)
+    a_cell = wall(lambda: cell_active_blocks(cells, radii, cell, block), seconds / 4)
+    ch = cells.bool().cpu().numpy()
+    c_cell = wall(lambda: [so.active_blocks_cell_level(ch, r, cell, block) for r in radii], seconds / 4)
+    return {"boxes_to_block_mask": {"kernel_us": round(k_box, 2), "api_us": round(a_box, 1),
+                                    "cpu_us": round(c_box, 1), "boxes": 100 * S, "cameras": S,
+                                    "out_bytes": S * hb * wb},
+            "cell_active_blocks": {"kernel_us": round(k_cell, 2), "api_us": round(a_cell, 1),
+                                   "cpu_us": round(c_cell, 1), "cell": cell, "radii": len(radii),
+                                   "in_bytes": int(cells.numel()), "out_bytes": int(cout.numel())},
+            "note": "outside the timed step; kernel_us = CUDA-event time per call over back-to-back "
+                    "ctypes launches (the box masks are bound by the host's call rate at this size); "
+                    "cpu_us is the numpy restatement of the reference's loops on one host thread"}
 
 
 def run_reference(args):
@@ -404,6 +481,11 @@ def run_b200(args):
                "steps": args.e2e_steps, "input": "pinned host uint8 BGR, normalisation fused into the gate",
                "modes_seen": sorted({int(m) for m in ring[:, 0].tolist()})}
 
+    # --- the mask utilities beside the step (rank 0; untimed by the step's clock)
+    masks = None
+    if rank == 0 and not args.no_masks:
+        masks = time_mask_kernels(dev, S, H, W, eng.block)
+
     # --- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -435,7 +517,7 @@ def run_b200(args):
             "conv_us_per_layer": {l.dst: round(1e3 * t / max(nprof, 1), 1) for l, t in zip(eng.layers, per_layer)},
             "conv_tflops_per_layer": {l.dst: round(f / (t * 1e-3) / 1e12, 1) if t > 0 else None
                                       for l, f, t in zip(eng.layers, flops_layer, per_layer)},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "mask_kernels": masks,
             "clocks": clock_info}
     print(json.dumps(line), flush=True)
 

@@ -150,12 +150,15 @@ def dilate(mask, d):
     if d == 0:
         return mask.copy()
     n, hb, wb = mask.shape
-    p = np.zeros((n, hb + 2 * d, wb + 2 * d), bool)
-    p[:, d:d + hb, d:d + wb] = mask
+    # a max over a (2d+1)^2 square is a max over rows of a max over columns (separable)
+    p = np.zeros((n, hb, wb + 2 * d), bool)
+    p[:, :, d:d + wb] = mask
+    rows = np.zeros((n, hb + 2 * d, wb), bool)
+    for dx in range(2 * d + 1):
+        rows[:, d:d + hb] |= p[:, :, dx:dx + wb]
     out = np.zeros_like(mask)
     for dy in range(2 * d + 1):
-        for dx in range(2 * d + 1):
-            out |= p[:, dy:dy + hb, dx:dx + wb]
+        out |= rows[:, dy:dy + hb]
     return out
 
 

@@ -9,8 +9,15 @@
 //
 // The two steps compose into one test per output block: it is active when any cell in the
 // block's own cell range, widened by the cell radius on every side (and clipped to the
-// image), changed.  One thread per (radius, camera, block) ORs that window; masks are
-// bytes, so the result is exact.
+// image), changed.
+//
+// cell_bits_kernel: one CTA per (camera, block row).  Its warps pack the cell rows that the
+// largest radius reaches into bit rows in shared memory (one __ballot_sync per 32 cells),
+// then each thread answers one (radius, block) by ORing, over the window's rows, the one or
+// two words that hold the window's columns, and masking the column range.  When the bit rows
+// do not fit in 48 KB (very wide images with very large radii), cell_active_kernel ORs each
+// window's bytes straight from global memory instead.  Both are exact.
+#include <algorithm>
 #include <cstdio>
 #include <string>
 
@@ -21,11 +28,14 @@ namespace {
 
 constexpr int kMaxRadii = 16;
 
+constexpr int kBitsSmemMax = 48 * 1024;
+
 struct CellArgs {
   const uint8_t* cells;  // [n][hc][wc], nonzero = changed
   uint8_t* out;          // [n_r][n][hc / k][wc / k]
   int n, hc, wc, k, hb, wb, n_r;
   int r[kMaxRadii];      // dilation in cells per output mask
+  int rmax, wpr;         // largest r; 32-bit words per bit row
 };
 
 __global__ void __launch_bounds__(256) cell_active_kernel(const CellArgs a) {
@@ -48,6 +58,50 @@ __global__ void __launch_bounds__(256) cell_active_kernel(const CellArgs a) {
     for (int x = x0; x <= x1; ++x) acc |= __ldg(row + x);
   }
   a.out[idx] = acc != 0 ? 1 : 0;
+}
+
+__global__ void __launch_bounds__(256) cell_bits_kernel(const CellArgs a) {
+  extern __shared__ uint32_t s_bits[];  // [rows][wpr], bit l of word w = cell column 32 w + l
+  const int by = blockIdx.x, cam = blockIdx.y;
+  const int ybase = max(0, by * a.k - a.rmax);
+  const int yend = min(a.hc - 1, by * a.k + a.k - 1 + a.rmax);
+  const int nwords = (yend - ybase + 1) * a.wpr;
+  const uint8_t* base = a.cells + (size_t)cam * a.hc * a.wc;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  // warp-uniform loop (every lane votes); eight words per warp and pass, their byte loads
+  // issued together
+  constexpr int U = 8;
+  for (int t0 = warp * U; t0 < nwords; t0 += nwarps * U) {
+    bool on[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const int t = t0 + j;
+      const int y = t / a.wpr, w = t - y * a.wpr;
+      const int x = w * 32 + lane;
+      on[j] = t < nwords && x < a.wc && __ldg(base + (size_t)(ybase + y) * a.wc + x) != 0;
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const uint32_t word = __ballot_sync(0xffffffffu, on[j]);
+      if (lane == 0 && t0 + j < nwords) s_bits[t0 + j] = word;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.n_r * a.wb; i += blockDim.x) {
+    const int ri = i / a.wb, bx = i - ri * a.wb;
+    const int r = a.r[ri];
+    const int y0 = max(0, by * a.k - r) - ybase, y1 = min(a.hc - 1, by * a.k + a.k - 1 + r) - ybase;
+    const int x0 = max(0, bx * a.k - r), x1 = min(a.wc - 1, bx * a.k + a.k - 1 + r);
+    uint32_t hit = 0;
+    for (int w = x0 >> 5; w <= (x1 >> 5); ++w) {
+      const int lo = max(x0 - 32 * w, 0), hi = min(x1 - 32 * w, 31);
+      const uint32_t m = (hi == 31 ? 0xffffffffu : (1u << (hi + 1)) - 1u) & (0xffffffffu << lo);
+      uint32_t acc = 0;
+      for (int y = y0; y <= y1; ++y) acc |= s_bits[y * a.wpr + w];
+      hit |= acc & m;
+    }
+    a.out[(((size_t)ri * a.n + cam) * a.hb + by) * a.wb + bx] = hit ? 1 : 0;
+  }
 }
 
 }  // namespace
@@ -77,15 +131,25 @@ extern "C" int sb_cell_active_blocks(const uint8_t* cells_dev, int n_cams, int h
   a.hb = hc / k;
   a.wb = wc / k;
   a.n_r = n_radii;
+  const int rcap = hc > wc ? hc : wc;  // a larger radius reaches no further cell
   for (int i = 0; i < n_radii; ++i) {
     if (radii[i] < 0) return record_error(SB_EINVAL, "sb_cell_active_blocks: negative radius");
-    a.r[i] = (radii[i] + cell - 1) / cell;  // ceil(R / cell) cells (gating.py:43)
+    const int rc = radii[i] / cell + (radii[i] % cell != 0);  // ceil(R / cell) cells (gating.py:43)
+    a.r[i] = rc < rcap ? rc : rcap;
+    a.rmax = a.r[i] > a.rmax ? a.r[i] : a.rmax;
   }
   const long long total = (long long)n_radii * n_cams * a.hb * a.wb;
   if (total > (1ll << 31) - 256) return record_error(SB_EINVAL, "sb_cell_active_blocks: output too large");
+  a.wpr = (wc + 31) / 32;
+  const long long rows = std::min<long long>(hc, (long long)k + 2ll * a.rmax);
+  const long long bits_smem = rows * a.wpr * 4;
   const int threads = 256;
-  const int grid = (int)((total + threads - 1) / threads);
-  cell_active_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  if (bits_smem <= kBitsSmemMax && n_cams <= 65535) {
+    cell_bits_kernel<<<dim3(a.hb, n_cams), threads, (size_t)bits_smem, static_cast<cudaStream_t>(stream)>>>(a);
+  } else {
+    const int grid = (int)((total + threads - 1) / threads);
+    cell_active_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  }
   cudaError_t rc = cudaGetLastError();
   if (rc != cudaSuccess)
     return record_error(SB_ECUDA, (std::string("sb_cell_active_blocks: launch: ") + cudaGetErrorString(rc)).c_str());

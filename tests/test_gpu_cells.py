@@ -74,3 +74,24 @@ def test_edges_and_errors():
         cell_active_blocks(one, list(range(17)), 16, 32)
     with pytest.raises(SarbonLibraryError, match="negative"):
         cell_active_blocks(one, [-1], 16, 32)
+
+
+@pytest.mark.parametrize("wc,radius", [(2048, 1040), (2048, 24), (100, 2 ** 31 - 1)])
+def test_wide_images_and_large_radii(wc, radius):
+    """Both kernels behind the entry point: the bit-row kernel (bit rows of the cells a
+    radius reaches fit in 48 KB of shared memory) and the byte-window kernel it falls back
+    to (256 rows x 64 words at 130 cells of radius do not); a radius far past the image
+    (capped to the image size inside) marks every block of a camera with any change."""
+    from sarbon_b200 import cell_active_blocks
+    cell, block, hc = 8, 32, 256
+    g = torch.Generator(device="cuda").manual_seed(wc + radius % 1000)
+    cells = torch.rand(2, hc, wc, device="cuda", generator=g) < 0.002
+    cells[1] = False
+    cells[1, 7, wc - 1] = True  # one change in the last column of camera 1
+    got = cell_active_blocks(cells, [radius, 0], cell, block).cpu().numpy()
+    c = cells.cpu().numpy()
+    r_eq = min(radius, cell * (max(hc, wc) + 1))  # the oracle's loops need a finite radius
+    np.testing.assert_array_equal(got[0], so.active_blocks_cell_level(c, r_eq, cell, block))
+    np.testing.assert_array_equal(got[1], so.active_blocks_cell_level(c, 0, cell, block))
+    if radius > cell * max(hc, wc):
+        assert got[0].all()
