@@ -209,22 +209,28 @@ def oracle_for(net, n, h, w, tau):
     return so.OracleEngine(so.fuse_program(nodes), n, h, w, dtype=np.float16, tau=tau)
 
 
-def cpu_run(net, frames_seq, tau, max_steps, seconds):
-    """Time the CPU oracle (the reference's algorithm) on 1 stream: reset, then one
-    stream-frame per step.  Returns (frames/s, steps, threads)."""
+def cpu_run(net, frames_seq, tau, max_steps, seconds, warmup=1, warmup_seconds=30.0):
+    """Time the CPU oracle (the reference's algorithm) on 1 stream: reset, ``warmup``
+    untimed steps (at least one, stopping early after ``warmup_seconds``), then one
+    stream-frame per timed step.  Returns (frames/s, timed steps, threads, warm-up steps)."""
     h, w = frames_seq[0].shape[1:3]
     ora = oracle_for(net, 1, h, w, tau)
     ora.reset(frames_seq[0])
-    ora.step(frames_seq[1 % len(frames_seq)])  # warm-up step (BLAS threads, page faults)
+    nw, t0 = 0, time.perf_counter()
+    while nw < max(1, warmup):  # BLAS threads, page faults
+        ora.step(frames_seq[(1 + nw) % len(frames_seq)])
+        nw += 1
+        if time.perf_counter() - t0 > warmup_seconds:
+            break
     t0 = time.perf_counter()
     n = 0
     while n < max_steps:
-        ora.step(frames_seq[(n + 2) % len(frames_seq)])
+        ora.step(frames_seq[(1 + nw + n) % len(frames_seq)])
         n += 1
         if time.perf_counter() - t0 > seconds:
             break
     dt = time.perf_counter() - t0
-    return n / dt, n, os.cpu_count()
+    return n / dt, n, os.cpu_count(), nw
 
 
 def time_mask_kernels(dev, S, H, W, block, seconds=2.0):
@@ -313,9 +319,9 @@ def run_reference(args):
     seq = [scenes.normalise(u8[i, :1]).numpy() for i in pingpong(min(args.frames, 8))]
     tau = 8 / float(scenes.STD.mean())
     budget = max(10.0, min(150.0, 0.5 * args.steps))
-    fps, n, cores = cpu_run(net, seq, tau, args.steps, budget)
+    fps, n, cores, nw = cpu_run(net, seq, tau, args.steps, budget, warmup=args.warmup)
     line = {"metric": METRIC, "value": fps, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": n,
-            "warmup": 1, "ms_per_step": 1e3 / fps, "higher_is_better": True, "scaling": "weak",
+            "warmup": nw, "ms_per_step": 1e3 / fps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 in / f32 accumulate (numpy fp32)", "data": "synthetic",
             "config": {"workload": f"1080p, {args.streams} streams/GPU, ~5% changed blocks",
                        "height": args.height, "width": args.width, "streams_per_gpu": args.streams,
@@ -490,7 +496,7 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cseq = [scenes.normalise(u8[i, :1]).cpu().numpy() for i in pingpong(min(args.frames, 8))]
-        fps, n, cores = cpu_run(net.cpu(), cseq, tau, 64, args.cpu_seconds)
+        fps, n, cores, _ = cpu_run(net.cpu(), cseq, tau, 64, args.cpu_seconds)
         cpu = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"{n} steps of 1 stream x {W}x{H} (numpy oracle restating sarbon/sparse; "
                          f"BLAS threads = host cores)"}
