@@ -65,6 +65,8 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-stats", action="store_true", help="skip the untimed statistics cycle")
     p.add_argument("--no-masks", action="store_true", help="skip timing the mask utility kernels")
+    p.add_argument("--cell", type=int, default=0,
+                   help="gate at cell level with this cell size (px; 0 = block level, the reference's rule)")
     p.add_argument("--cpu-seconds", type=float, default=20.0)
     return p.parse_args()
 
@@ -359,6 +361,9 @@ def run_b200(args):
     net = build_net(args.seed).to(dev)
     S, H, W = args.streams, args.height, args.width
     eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev)
+    if args.cell:
+        eng.set_cell_gating(args.cell)  # the u8 end-to-end step gates per block only
+        args.no_e2e = True
     u8, rects = make_frames(args, rank, dev, world)
     staged = torch.stack([scenes.normalise(u8[i]) for i in range(u8.shape[0])])  # [F,S,H,W,3] fp16
     order = pingpong(args.frames)
@@ -513,6 +518,7 @@ def run_b200(args):
             "data": "synthetic (seeded moving-rectangle camera streams, random-init Sarbon-S stem)",
             "config": {"workload": f"1080p x {S} streams/GPU, ~5% changed blocks",
                        "height": H, "width": W, "block": 32, "streams_per_gpu": S, "rects_per_stream": rects,
+                       "gating": f"cell level, {args.cell} px cells" if args.cell else "block level",
                        "tau_grey_levels": 8, "frames_staged": args.frames,
                        "changed_block_frac": changed_frac,
                        "active_block_frac": {f"d{d}": a for d, a in zip(eng.ds, act_frac)},

@@ -140,6 +140,18 @@ SB_API int sb_set_fallback(sb_engine* e, int64_t fallback, void* stream);
 SB_API int sb_set_tau(sb_engine* e, double tau);
 SB_API int sb_set_dense_check_every(sb_engine* e, int n, void* stream);
 
+/* Cell-level gating for the steps launched after this call (the tighter active-set
+ * estimate of the reference's gating.py:42-43, which the reference uses only in its
+ * gating analysis; its engine gates per block).  A cell of cell x cell pixels changed
+ * when its exact sum of |fp16 diff| exceeds float32(tau * cell^2 * 3), or its block is
+ * forced by `extra` / the refresh phase; a block changed (image cache update) when any
+ * of its cells did; the mask of dilation group i marks the blocks that the changed cells,
+ * dilated by cell_radii[i] cells, reach.  Lossless at tau = 0 when cell_radii[i] is at
+ * least ceil(R / cell) for every layer R of group i.  fp16 engines and sb_step only;
+ * cell a multiple of 8 dividing the block; n_radii = the number of dilation groups.
+ * cell = 0 returns to block-level gating.  Allocates the cell buffers on first use. */
+SB_API int sb_set_cell_gating(sb_engine* e, int cell, const int* cell_radii, int n_radii);
+
 /* Calibration support (fused_engine.py:261-264): run the conv sequence over
  * exactly `n_tiles` entries of the current block lists (entries past the active
  * count recompute block 0, like nonzero_static's fill_value=0), updating the

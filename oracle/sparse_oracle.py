@@ -180,6 +180,32 @@ def active_blocks_block_level(cells, radius, cell, block):
     return dilate(cells_to_blocks(cells, block // cell), -(-radius // block))
 
 
+
+def gate_cells(frames, img, cell, block, tau, extra=None, refresh=0, tick=0):
+    """Cell-level gate of the engine's optional cell mode: a cell changed when its exact
+    sum of |diff| exceeds float32(tau * cell^2 * 3) (the block gate, fused_engine.py:140-148,
+    applied per cell; gating.py:18-22 estimates cells the same way, as a mean) or when its
+    block is forced by ``extra`` or the refresh phase.  Returns (cells [N, H/c, W/c],
+    changed blocks [N, Hb, Wb]): a block changed when any of its cells did."""
+    k = block // cell
+    cells = block_change_sums(frames, img, cell) > np.float64(threshold(tau, cell))
+    n, h, w, _ = frames.shape
+    forced = np.zeros((n, h // block, w // block), bool)
+    if extra is not None:
+        forced |= extra.astype(bool)
+    if refresh:
+        lin = np.arange(forced.size, dtype=np.int64).reshape(forced.shape)
+        forced |= (lin % refresh) == (tick % refresh)
+    cells |= np.repeat(np.repeat(forced, k, axis=1), k, axis=2)
+    return cells, cells_to_blocks(cells, k)
+
+
+def cell_group_masks(cells, cell_radii, k):
+    """Block masks of the cell mode: the changed cells dilated by each group's radius (in
+    cells), any-pooled into blocks of k x k cells (gating.py:42-43)."""
+    return [cells_to_blocks(dilate(cells, r), k) for r in cell_radii]
+
+
 def boxes_to_block_mask(boxes, hb, wb, block, margin=0):
     """Track-steered mask of one camera (video.py:26-34): for each xyxy box in engine
     pixels, the block range from floor(lo / block) - margin to floor(hi / block) + margin,

@@ -105,6 +105,42 @@ __global__ void __launch_bounds__(256) cell_bits_kernel(const CellArgs a) {
 }
 
 }  // namespace
+
+// Shared by the entry point below and the engine's cell-level gating: radii rc[] in cells.
+cudaError_t launch_cell_masks(const uint8_t* cells, int n, int hc, int wc, int k, const int* rc, int n_r,
+                              uint8_t* out, cudaStream_t s) {
+  if (n_r < 1 || n_r > kMaxRadii || k <= 0 || hc % k || wc % k) return cudaErrorInvalidValue;
+  CellArgs a{};
+  a.cells = cells;
+  a.out = out;
+  a.n = n;
+  a.hc = hc;
+  a.wc = wc;
+  a.k = k;
+  a.hb = hc / k;
+  a.wb = wc / k;
+  a.n_r = n_r;
+  const int rcap = hc > wc ? hc : wc;  // a larger radius reaches no further cell
+  for (int i = 0; i < n_r; ++i) {
+    if (rc[i] < 0) return cudaErrorInvalidValue;
+    a.r[i] = rc[i] < rcap ? rc[i] : rcap;
+    a.rmax = a.r[i] > a.rmax ? a.r[i] : a.rmax;
+  }
+  const long long total = (long long)n_r * n * a.hb * a.wb;
+  if (total > (1ll << 31) - 256) return cudaErrorInvalidValue;
+  a.wpr = (wc + 31) / 32;
+  const long long rows = std::min<long long>(hc, (long long)k + 2ll * a.rmax);
+  const long long bits_smem = rows * a.wpr * 4;
+  const int threads = 256;
+  if (bits_smem <= kBitsSmemMax && n <= 65535) {
+    cell_bits_kernel<<<dim3(a.hb, n), threads, (size_t)bits_smem, s>>>(a);
+  } else {
+    const int grid = (int)((total + threads - 1) / threads);
+    cell_active_kernel<<<grid, threads, 0, s>>>(a);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace sb
 
 using namespace sb;
@@ -121,36 +157,15 @@ extern "C" int sb_cell_active_blocks(const uint8_t* cells_dev, int n_cams, int h
     return record_error(SB_EINVAL, "sb_cell_active_blocks: hc and wc must be multiples of block / cell");
   if (n_radii < 1 || n_radii > kMaxRadii)
     return record_error(SB_EINVAL, "sb_cell_active_blocks: n_radii must be in [1, 16]");
-  CellArgs a{};
-  a.cells = cells_dev;
-  a.out = out_dev;
-  a.n = n_cams;
-  a.hc = hc;
-  a.wc = wc;
-  a.k = k;
-  a.hb = hc / k;
-  a.wb = wc / k;
-  a.n_r = n_radii;
-  const int rcap = hc > wc ? hc : wc;  // a larger radius reaches no further cell
+  int rc_cells[kMaxRadii];
   for (int i = 0; i < n_radii; ++i) {
     if (radii[i] < 0) return record_error(SB_EINVAL, "sb_cell_active_blocks: negative radius");
-    const int rc = radii[i] / cell + (radii[i] % cell != 0);  // ceil(R / cell) cells (gating.py:43)
-    a.r[i] = rc < rcap ? rc : rcap;
-    a.rmax = a.r[i] > a.rmax ? a.r[i] : a.rmax;
+    rc_cells[i] = radii[i] / cell + (radii[i] % cell != 0);  // ceil(R / cell) cells (gating.py:43)
   }
-  const long long total = (long long)n_radii * n_cams * a.hb * a.wb;
-  if (total > (1ll << 31) - 256) return record_error(SB_EINVAL, "sb_cell_active_blocks: output too large");
-  a.wpr = (wc + 31) / 32;
-  const long long rows = std::min<long long>(hc, (long long)k + 2ll * a.rmax);
-  const long long bits_smem = rows * a.wpr * 4;
-  const int threads = 256;
-  if (bits_smem <= kBitsSmemMax && n_cams <= 65535) {
-    cell_bits_kernel<<<dim3(a.hb, n_cams), threads, (size_t)bits_smem, static_cast<cudaStream_t>(stream)>>>(a);
-  } else {
-    const int grid = (int)((total + threads - 1) / threads);
-    cell_active_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  }
-  cudaError_t rc = cudaGetLastError();
+  if ((long long)n_radii * n_cams * (hc / k) * (wc / k) > (1ll << 31) - 256)
+    return record_error(SB_EINVAL, "sb_cell_active_blocks: output too large");
+  cudaError_t rc = launch_cell_masks(cells_dev, n_cams, hc, wc, k, rc_cells, n_radii, out_dev,
+                                     static_cast<cudaStream_t>(stream));
   if (rc != cudaSuccess)
     return record_error(SB_ECUDA, (std::string("sb_cell_active_blocks: launch: ") + cudaGetErrorString(rc)).c_str());
   return SB_OK;

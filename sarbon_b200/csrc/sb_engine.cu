@@ -100,6 +100,13 @@ struct sb_engine {
   int32_t* host_out_dev = nullptr;
   int n_sms = 148;
   int last_launches = 0;
+  // cell-level gating (0: block level): cell size, cell radius per dilation group, buffers
+  int cell = 0;
+  int cell_r[SB_MAX_DILATIONS] = {};
+  int64_t cell_thr_fx = 0;
+  uint8_t* cells = nullptr;   // [N][H/cell][W/cell], allocated by the first sb_set_cell_gating
+  int cells_cell = 0;         // the cell size `cells` was allocated for
+  uint8_t* cmasks = nullptr;  // [nd][N][Hb][Wb] block masks from the cells
   std::vector<void*> allocs;
   // optional per-launch timing (sb_step_profiled)
   bool profiling = false;
@@ -128,16 +135,24 @@ int alloc_dev(sb_engine* e, void** p, size_t bytes) {
   return SB_OK;
 }
 
+// floor(float32(tau * side^2 * 3) * 2^24): the gate threshold of a side x side area as an
+// exact fixed-point value (-1: every area changes, INT64_MAX: none does)
+int64_t threshold_fx(double tau, int side) {
+  const float thr32 = (float)(tau * side * side * 3);
+  if (std::isnan(thr32)) return INT64_MAX;
+  if (thr32 < 0.f) return -1;
+  if (std::isinf(thr32) || (double)thr32 * 16777216.0 >= 9.0e18) return INT64_MAX;
+  return (int64_t)std::floor((double)thr32 * 16777216.0);
+}
+
 // Gate threshold from tau: float32(tau * block * block * 3), compared as torch does
 // (fused_engine.py:144), as an exact fixed-point value and as the fp32 rounding band.
 void set_threshold(sb_engine* e, double tau) {
   e->tau = tau;
   const float thr32 = (float)(tau * e->block * e->block * 3);
   e->thr = (double)thr32;
-  if (std::isnan(thr32)) e->thr_fx = INT64_MAX;
-  else if (thr32 < 0.f) e->thr_fx = -1;
-  else if (std::isinf(thr32) || (double)thr32 * 16777216.0 >= 9.0e18) e->thr_fx = INT64_MAX;
-  else e->thr_fx = (int64_t)std::floor((double)thr32 * 16777216.0);
+  e->thr_fx = threshold_fx(tau, e->block);
+  if (e->cell) e->cell_thr_fx = threshold_fx(tau, e->cell);
   if (std::isnan(thr32)) e->thr = INFINITY;  // sum > NaN is false for every block
   // A recursive fp32 sum of n non-negative fp16 terms is within (n-1)*2^-24 relative of the
   // exact sum (any order); twice that margin decides the comparison from the fp32 sum.
@@ -247,7 +262,34 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
     g.stdv[c] = stdv ? stdv[c] : 1.f;
   }
   mark(e, s);
-  SB_CUDA(launch_gate(g, kind, s));
+  if (e->cell) {
+    if (kind != 0) return fail(SB_EINVAL, "cell-level gating needs fp16 frames (sb_step on an fp16 engine)");
+    CellGateArgs cg{};
+    cg.frames = frames;
+    cg.img = e->cache[0];
+    cg.extra = e->extra;
+    cg.changed = e->changed;
+    cg.cells = e->cells;
+    cg.st = e->st;
+    cg.n = e->n;
+    cg.h = e->h;
+    cg.w = e->w;
+    cg.hb = e->hb;
+    cg.wb = e->wb;
+    cg.block = e->block;
+    cg.cell = e->cell;
+    cg.k = e->block / e->cell;
+    cg.hc = e->h / e->cell;
+    cg.wc = e->w / e->cell;
+    cg.thr_fx = e->cell_thr_fx;
+    cg.refresh = e->refresh;
+    SB_CUDA(launch_cell_gate(cg, s));
+    // the block masks of every dilation group from the cells; the lists kernel then takes
+    // them as they are (dilation 0).  Timed with the gate when profiling.
+    SB_CUDA(launch_cell_masks(e->cells, e->n, cg.hc, cg.wc, cg.k, e->cell_r, e->nd, e->cmasks, s));
+  } else {
+    SB_CUDA(launch_gate(g, kind, s));
+  }
   mark(e, s);
   ListArgs l{};
   l.changed = e->changed;
@@ -265,7 +307,10 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
   l.hb = e->hb;
   l.wb = e->wb;
   l.n_dil = e->nd;
-  for (int i = 0; i < e->nd; ++i) l.ds[i] = e->ds[i];
+  for (int i = 0; i < e->nd; ++i) {
+    l.ds[i] = e->cell ? 0 : e->ds[i];
+    l.src[i] = e->cell ? e->cmasks + (size_t)i * e->n_blocks : nullptr;
+  }
   SB_CUDA(launch_lists(l, e->n_chunks, s));
   mark(e, s);
   CopyArgs c{};
@@ -287,7 +332,7 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
   }
   SB_CUDA(launch_copy(c, s));
   mark(e, s);
-  e->last_launches = 3;
+  e->last_launches = e->cell ? 4 : 3;
   rc = launch_convs(e, s);
   if (rc) return rc;
   SB_CUDA(launch_finalize(e->st, e->refresh, e->host_out_dev, s));
@@ -583,6 +628,39 @@ int sb_set_fallback(sb_engine* e, int64_t fallback, void* stream) {
 int sb_set_tau(sb_engine* e, double tau) {
   if (!e) return fail(SB_EINVAL, "null engine");
   set_threshold(e, tau);
+  return SB_OK;
+}
+
+int sb_set_cell_gating(sb_engine* e, int cell, const int* cell_radii, int n_radii) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (cell == 0) {
+    e->cell = 0;
+    return SB_OK;
+  }
+  if (e->dtype != SB_F16) return fail(SB_EINVAL, "cell-level gating: fp16 engines only");
+  if (cell < 8 || cell % 8 || e->block % cell)
+    return fail(SB_EINVAL, "cell-level gating: the cell must be a multiple of 8 px dividing the block");
+  if (!cell_radii || n_radii != e->nd)
+    return fail(SB_EINVAL, "cell-level gating: one cell radius per dilation group (" + std::to_string(e->nd) + ")");
+  for (int i = 0; i < n_radii; ++i)
+    if (cell_radii[i] < 0) return fail(SB_EINVAL, "cell-level gating: negative cell radius");
+  SB_CUDA(cudaSetDevice(e->dev));
+  if (!e->cmasks) {
+    void* p = nullptr;
+    int rc = alloc_dev(e, &p, (size_t)e->nd * e->n_blocks);
+    if (rc) return rc;
+    e->cmasks = static_cast<uint8_t*>(p);
+  }
+  if (e->cells_cell != cell) {  // cells of another size: a new buffer (the old one stays owned)
+    void* p = nullptr;
+    int rc = alloc_dev(e, &p, (size_t)e->n * (e->h / cell) * (e->w / cell));
+    if (rc) return rc;
+    e->cells = static_cast<uint8_t*>(p);
+    e->cells_cell = cell;
+  }
+  for (int i = 0; i < n_radii; ++i) e->cell_r[i] = cell_radii[i];
+  e->cell = cell;
+  e->cell_thr_fx = threshold_fx(e->tau, cell);
   return SB_OK;
 }
 

@@ -359,6 +359,68 @@ SB_DEV uint32_t lookback(unsigned long long* stat, uint32_t chunk, uint32_t epoc
   return excl;
 }
 
+// Cell-level gate (fp16 frames).  A cell of c x c pixels changed when its exact
+// sum(|fp16(fp32(a) - fp32(b))|) exceeds float32(tau * c^2 * 3) -- the block rule of the
+// gate above, applied per cell (the reference's gating.py:18-22 estimates cells the same
+// way, as a mean) -- or when its block is forced by `extra` or the refresh phase.  A block
+// changed when any of its cells did; changed blocks are copied into the image cache as in
+// the block-level gate.  One CTA per (block row, camera); one thread per (cell row of the
+// block row, cell column), summing exactly in integer multiples of 2^-24.
+__global__ void __launch_bounds__(256) cell_gate_kernel(CellGateArgs a) {
+  grid_dep_wait();
+  if (in_hysteresis(a.st)) return;
+  extern __shared__ uint32_t s_blk[];  // [wb] changed flag per block of this block row
+  const int by = blockIdx.x, cam = blockIdx.y;
+  for (int i = threadIdx.x; i < a.wb; i += blockDim.x) s_blk[i] = 0u;
+  __syncthreads();
+  const int C = a.cell, k = a.k;
+  const int vpc = C * 3 / 8;                    // 16-byte vectors per cell row (C % 8 == 0)
+  const size_t row_v = (size_t)a.w * 3 / 8;     // 16-byte vectors per image row
+  const size_t base = ((size_t)cam * a.h + (size_t)by * a.block) * row_v;
+  const uint4* f = reinterpret_cast<const uint4*>(a.frames) + base;
+  const uint4* g = reinterpret_cast<const uint4*>(a.img) + base;
+  const int64_t tick = a.st->tick;
+  for (int it = threadIdx.x; it < k * a.wc; it += blockDim.x) {
+    const int j = it / a.wc, cx = it - j * a.wc, bx = cx / k;
+    uint64_t acc = 0;
+    uint32_t flags = 0;
+    for (int r = 0; r < C; ++r) {
+      const size_t off = (size_t)(j * C + r) * row_v + (size_t)cx * vpc;
+      for (int v = 0; v < vpc; ++v) {
+        const uint4 x = __ldg(f + off + v), y = __ldg(g + off + v);
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          accum_h(sub_h(xs[q] & 0xFFFF, ys[q] & 0xFFFF), acc, flags);
+          accum_h(sub_h(xs[q] >> 16, ys[q] >> 16), acc, flags);
+        }
+      }
+    }
+    bool ch;
+    if (flags & GATE_NAN) ch = false;
+    else if (flags & GATE_INF) ch = a.thr_fx < INT64_MAX;  // inf > finite thr; inf > inf is false
+    else ch = (int64_t)acc > a.thr_fx;
+    const int64_t lin = ((int64_t)cam * a.hb + by) * a.wb + bx;
+    ch = ch || a.extra[lin] != 0;
+    if (a.refresh) ch = ch || (lin % a.refresh) == (tick % a.refresh);
+    a.cells[((size_t)cam * a.hc + (size_t)by * k + j) * a.wc + cx] = ch ? 1 : 0;
+    if (ch) s_blk[bx] = 1u;  // every writer stores the same value
+  }
+  __syncthreads();
+  for (int bx = threadIdx.x; bx < a.wb; bx += blockDim.x)
+    a.changed[((size_t)cam * a.hb + by) * a.wb + bx] = s_blk[bx] ? 1 : 0;
+  // image-cache update for changed blocks (fused_engine.py:157-160); this CTA read its
+  // block row of the cache above, and no other CTA reads it
+  const int vpb = a.block * 3 / 8;
+  uint4* gw = reinterpret_cast<uint4*>(a.img) + base;
+  for (int v = threadIdx.x; v < vpb * a.wb; v += blockDim.x) {
+    if (!s_blk[v / vpb]) continue;
+#pragma unroll 4
+    for (int r = 0; r < a.block; ++r) gw[(size_t)r * row_v + v] = __ldg(f + (size_t)r * row_v + v);
+  }
+  grid_dep_launch();
+}
+
 __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
   grid_dep_wait();
   State* st = a.st;
@@ -406,8 +468,8 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
     coord[kind][0] = cam;
     coord[kind][1] = ry;
     coord[kind][2] = rx;
-    const uint8_t* cm = a.changed + (size_t)cam * per;
     for (int di = 0; di < a.n_dil; ++di) {
+      const uint8_t* cm = (a.src[di] ? a.src[di] : a.changed) + (size_t)cam * per;
       const int d = a.ds[di], L = kind * a.n_dil + di;
       bool on = false;
       if (valid) {
@@ -603,6 +665,10 @@ cudaError_t launch_gate(const GateArgs& a_in, int kind, cudaStream_t s) {
     case 1: return launch_pdl(gate_kernel<1>, grid, dim3(256), smem, s, a);
     default: return launch_pdl(gate_kernel<2>, grid, dim3(256), smem, s, a);
   }
+}
+
+cudaError_t launch_cell_gate(const CellGateArgs& a, cudaStream_t s) {
+  return launch_pdl(cell_gate_kernel, dim3(a.hb, a.n), dim3(256), (size_t)a.wb * 4, s, a);
 }
 
 cudaError_t launch_lists(const ListArgs& a, int n_chunks, cudaStream_t s) {

@@ -67,6 +67,21 @@ struct ListArgs {
   State* st;
   int n_blocks, hb, wb, n_dil;
   int ds[SB_MAX_DILATIONS];
+  // per-dilation source mask, dilated by ds[i] (nullptr: `changed`).  Cell-level gating
+  // passes the block masks it computed from cells, with ds[i] = 0.
+  const uint8_t* src[SB_MAX_DILATIONS];
+};
+
+struct CellGateArgs {      // cell-level gate (fp16 frames)
+  const void* frames;      // [N][H][W][3] fp16
+  void* img;               // image cache [N][H][W][3] fp16
+  const uint8_t* extra;    // [N][Hb][Wb]
+  uint8_t* changed;        // [N][Hb][Wb]: any cell of the block changed (or forced)
+  uint8_t* cells;          // [N][H/cell][W/cell]
+  State* st;
+  int n, h, w, hb, wb, block, cell, k, hc, wc;
+  int64_t thr_fx;          // floor(float32(tau * cell^2 * 3) * 2^24); -1: always; INT64_MAX: never
+  int refresh;
 };
 
 struct CopyArgs {          // dense img copy or masked update
@@ -110,6 +125,10 @@ cudaError_t launch_lists(const ListArgs& a, int n_chunks, cudaStream_t s);
 cudaError_t launch_copy(const CopyArgs& a, cudaStream_t s);
 cudaError_t launch_finalize(State* st, int refresh, int32_t* host_out, cudaStream_t s);
 cudaError_t launch_set_mode(State* st, int mode, int reset_hyst, int64_t force_tiles, cudaStream_t s);
+cudaError_t launch_cell_gate(const CellGateArgs& a, cudaStream_t s);
+// block masks [n_r][n][hc/k][wc/k] of cells [n][hc][wc] dilated by rc[i] cells (sb_cells.cu)
+cudaError_t launch_cell_masks(const uint8_t* cells, int n, int hc, int wc, int k, const int* rc, int n_r,
+                              uint8_t* out, cudaStream_t s);
 
 // fp16 tcgen05 path.  Returns cudaErrorInvalidValue for shapes without an instantiation.
 bool conv_tc_supported(int cin, int cout, int t, int s);  // some mode exists for the shape

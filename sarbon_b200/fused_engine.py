@@ -11,6 +11,8 @@ unchanged:
   ``set_extra(mask)``, ``outputs_nchw()``, ``dilation(radius)``  (:121-275)
 * added: ``steer(boxes_per_cam, margin=1)``, the caller's track steering
   (``sarbon/inference/video.py:139-147``) as one kernel writing ``extra``
+* added: ``set_cell_gating(cell)``, cell-level gating (``sarbon/sparse/gating.py:42-43``)
+  inside the step
 * attributes ``n, h, w, block, hb, wb, n_blocks, dtype, tau, refresh, layers, ds,
   outputs, cache, frames, changed, extra, masks, buckets, fallback,
   dense_check_every, dense_graph, stats``.
@@ -134,6 +136,7 @@ class FusedSparseEngine:
         if dtype not in (torch.float16, torch.float32):
             raise ValueError("dtype must be torch.float16 or torch.float32")
         self.n, self.h, self.w, self.block = n_cams, height, width, block
+        self.cell, self.cell_radii = 0, None  # block-level gating (set_cell_gating)
         self.hb, self.wb = height // block, width // block
         self.n_blocks = n_cams * self.hb * self.wb
         self.dtype, self.tau, self.refresh = dtype, tau, refresh
@@ -244,6 +247,28 @@ class FusedSparseEngine:
     def set_extra(self, mask):
         """Blocks [N, Hb, Wb] recomputed next step regardless of pixel change (:201-205)."""
         self.extra.copy_(mask)  # a view of the engine's mask: the next gate reads it
+
+    def set_cell_gating(self, cell):
+        """Gate at cell level from the next step on (``cell`` px, a multiple of 8 dividing
+        the block; 0 = block level, the reference's engine behaviour).
+
+        The tighter estimate of the reference's gating analysis (gating.py:42-43): cells
+        whose exact sum of |diff| exceeds float32(tau * cell^2 * 3) are dilated by
+        ceil(R / cell) cells, R the largest receptive radius of each dilation group, and
+        any-pooled into the group's block mask.  Lossless at tau = 0, like block level; a
+        change in the middle of a block no longer activates its whole ring of neighbours.
+        fp16 engines and ``step``/``step_async`` only (not ``step_u8``)."""
+        if cell == 0:
+            check(lib().sb_set_cell_gating(self._h.ptr, 0, None, 0), "sb_set_cell_gating")
+            self.cell, self.cell_radii = 0, None
+            return
+        rc = [0] * len(self.ds)
+        for l in self.layers:
+            di = self.ds.index(self.dilation(l.radius))
+            rc[di] = max(rc[di], -(-l.radius // cell))
+        arr = (C.c_int * len(rc))(*rc)
+        check(lib().sb_set_cell_gating(self._h.ptr, int(cell), arr, len(rc)), "sb_set_cell_gating")
+        self.cell, self.cell_radii = int(cell), rc
 
     def steer(self, boxes_per_cam, margin=1):
         """Track steering (video.py:139-147): the blocks each camera's predicted boxes
