@@ -16,11 +16,17 @@ Arms:
                          HBM; `e2e` runs the same steps through the public API from pinned
                          host uint8 BGR frames (H2D copy of every frame and a D2H read of
                          every step's {mode, count} inside the timed region).
-  --impl reference       the reference algorithm on the host CPU (the numpy oracle that
-                         restates sarbon/sparse's engine), one stream-frame per step.
+  --impl reference       the reference's own CPU path for the stem features on the host
+                         cores: with no CUDA device SarbonVideo runs the dense stem every
+                         frame (sarbon/inference/video.py:101-104), i.e. the reference's
+                         LocalBackbone forward in fp32 (installed under baseline/_ref); the
+                         numpy oracle that restates the sparse engine when it is absent.
 
-Multi-GPU (torchrun): streams are independent; each rank runs its own S streams (weak
-scaling) with no collective inside the timed region; the time is the max over ranks.
+Multi-GPU (torchrun): streams are independent; each rank runs its own shard of the
+streams with no collective inside the timed region; the time is the max over ranks.
+Weak scaling (default): S streams per GPU.  Strong scaling (--total-streams T, e.g.
+64 streams of 1280x720 padded to 736 over 1/2/4/8 GPUs): the job's T
+streams split contiguously over the ranks.
 """
 from __future__ import annotations
 
@@ -53,8 +59,12 @@ def parse():
     p.add_argument("--steps", type=int, default=1000)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    p.add_argument("--streams", type=int, default=16, help="camera streams per GPU")
+    p.add_argument("--streams", type=int, default=16, help="camera streams per GPU (weak scaling)")
+    p.add_argument("--total-streams", type=int, default=0,
+                   help="streams of the whole job split over the GPUs (strong scaling; 0 = weak)")
     p.add_argument("--height", type=int, default=1088)
+    p.add_argument("--camera-height", type=int, default=0,
+                   help="camera frame height, zero-padded at the bottom to --height (0 = --height)")
     p.add_argument("--width", type=int, default=1920)
     p.add_argument("--rects", type=int, default=0, help="moving rectangles per stream (0 = auto for ~5%%)")
     p.add_argument("--frames", type=int, default=16, help="distinct frames staged per stream")
@@ -68,6 +78,9 @@ def parse():
     p.add_argument("--cell", type=int, default=0,
                    help="gate at cell level with this cell size (px; 0 = block level, the reference's rule)")
     p.add_argument("--cpu-seconds", type=float, default=20.0)
+    p.add_argument("--no-reference-gpu", action="store_true",
+                   help="skip timing the reference's own Triton engine on the GPU (rank 0, N = 1)")
+    p.add_argument("--reference-gpu-steps", type=int, default=60)
     return p.parse_args()
 
 
@@ -86,20 +99,10 @@ def pingpong(n):
     return list(range(n)) + list(range(n - 2, 0, -1))
 
 
-def load_traffic(streams):
-    """DRAM bytes per launch measured by ncu (profiles/dram_traffic_8x1080p_5pct.md), scaled
-    from its 8-stream capture to `streams` (traffic grows with the active blocks); None
-    when the summary is absent."""
-    p = ROOT / "profiles" / "dram_traffic_8x1080p_5pct.md"
-    out = {}
-    if p.exists():
-        for line in p.read_text().splitlines():
-            line = line.strip()
-            for key in ("conv", "gate"):
-                tag = f"{key}_traffic_bytes_per_launch_8_streams:"
-                if line.startswith(tag):
-                    out[key] = float(line[len(tag):]) * streams / 8
-    return out
+# DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one capture of
+# the default workload (16 streams x 1920x1088, ~5 % changed blocks); they describe the
+# kernels as they were at that capture, named in "capture".  None: not captured.
+TRAFFIC = {"conv": None, "gate": None, "capture": None}
 
 
 def load_peaks():
@@ -170,11 +173,38 @@ def layer_flops(eng, counts, mode):
 
 
 def gate_bytes(eng, n_changed):
-    """Gate kernel bytes: read frames and image cache (fp16), copy the changed blocks'
-    frames into the cache (re-read + write), write the change mask."""
+    """Algorithmic bytes of the gate kernel: read the frames and the image cache (fp16),
+    write the changed blocks into the image cache (block^2 * 3 fp16 each), read the extra
+    mask and write the change mask (one byte per block each)."""
     px = eng.n * eng.h * eng.w * 3
-    blk = eng.block * eng.block * 3 * 2
-    return 2 * px * 2 + n_changed * 2 * blk + eng.n_blocks
+    return 2 * px * 2 + n_changed * eng.block * eng.block * 3 * 2 + 2 * eng.n_blocks
+
+
+def mma_flops(eng, mode):
+    """FLOPs the tile-conv kernels issue on the tensor cores in one step, per layer:
+    2 x 128-row M-tiles x 128 x C_out x issued K.  Above the algorithmic FLOPs because
+    window layers compute whole regions (inactive blocks inside an active region too),
+    the first layer pads its 27 taps to K = 32 and the 32-channel stride-2 layer issues
+    6 K-blocks of 64 for its 9 x 32 taps."""
+    import torch.nn.functional as F
+    out = []
+    for l, m in zip(eng.layers, eng.layer_variants()):
+        t = eng.block // l.out_stride
+        cin, cout = l.w_tile.shape[2], l.w_tile.shape[3]
+        win = m & 7
+        rw, rh = (8 // t, 16 // t if win == 3 else 1) if win else (1, 1)
+        mask = eng.masks[eng.dilation(l.radius)]
+        if mode == "dense":
+            mask = torch.ones_like(mask)
+        if rw * rh > 1:
+            units = int(F.max_pool2d(mask.float()[:, None], (rh, rw), (rh, rw), ceil_mode=True).sum())
+        else:
+            units = int(mask.sum())
+        upx = 8 * (16 if win == 3 else t) if win else t * t   # output pixels per unit
+        mtiles = -(-units * upx // 128) if upx < 128 else units * (upx // 128)
+        k = 32 if cin < 16 else (6 * 64 if (win == 2 and cin == 32) else 9 * cin)
+        out.append(2 * mtiles * 128 * cout * k)
+    return out
 
 
 def build_net(seed):
@@ -183,17 +213,34 @@ def build_net(seed):
     return LocalBackbone().eval()
 
 
+def job_streams(args, world):
+    """Streams of the whole job: --total-streams (strong scaling) or S per GPU (weak)."""
+    return args.total_streams if args.total_streams else world * args.streams
+
+
 def make_frames(args, rank, dev, world=1):
-    """This rank's shard of the job's world x S streams (contiguous global stream ids),
-    seeded by its first global stream id so that no two ranks share a camera."""
+    """This rank's shard of the job's streams (contiguous global stream ids), seeded by its
+    first global stream id so that no two ranks share a camera.  Frames are generated at
+    the camera height and zero-padded at the bottom to the engine height (720p -> 736)."""
     from sarbon_b200 import scenes
     from sarbon_b200.multi import shard_streams, stream_seed
-    rects = args.rects or auto_rects(args.height, args.width)
-    shard = shard_streams(world * args.streams, world, rank)
-    src = scenes.Streams(len(shard), args.height, args.width, seed=stream_seed(args.seed, shard.start),
+    cam_h = args.camera_height or args.height
+    rects = args.rects or auto_rects(cam_h, args.width)
+    shard = shard_streams(job_streams(args, world), world, rank)
+    src = scenes.Streams(len(shard), cam_h, args.width, seed=stream_seed(args.seed, shard.start),
                          n_rects=rects, device=dev)
-    u8 = torch.stack([src.next() for _ in range(args.frames)])  # [F, S, H, W, 3] RGB
+    u8 = torch.stack([src.next() for _ in range(args.frames)])  # [F, S, h, W, 3] RGB
+    if cam_h < args.height:
+        u8 = torch.nn.functional.pad(u8, (0, 0, 0, 0, 0, args.height - cam_h))
     return u8, rects
+
+
+def workload_name(args, world):
+    cam_h = args.camera_height or args.height
+    res = f"{args.width}x{cam_h}" + (f" padded to {args.width}x{args.height}" if cam_h < args.height else "")
+    if args.total_streams:
+        return f"{res} x {args.total_streams} streams over {world} GPU(s), ~5% changed blocks"
+    return f"{res} x {args.streams} streams/GPU, ~5% changed blocks"
 
 
 # ----------------------------------------------------------------------------- CPU (reference algorithm)
@@ -233,6 +280,82 @@ def cpu_run(net, frames_seq, tau, max_steps, seconds, warmup=1, warmup_seconds=3
             break
     dt = time.perf_counter() - t0
     return n / dt, n, os.cpu_count(), nw
+
+
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def import_reference():
+    """The reference package installed under baseline/_ref (its block_sparse and
+    fused_engine modules), or None when it is not installed."""
+    if not (REF_DIR / "sarbon").is_dir():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    try:
+        import sarbon.sparse.block_sparse as bs
+        import sarbon.sparse.fused_engine as fe
+        return bs, fe
+    except Exception:
+        return None
+
+
+def reference_net(ref, net):
+    """The reference's own LocalBackbone (sarbon/sparse/block_sparse.py:62-76) holding the
+    same weights as `net` (the module and parameter names are the same)."""
+    bs, _ = ref
+    rnet = bs.LocalBackbone().eval()
+    rnet.load_state_dict({k: v.detach().cpu() for k, v in net.state_dict().items()})
+    return rnet
+
+
+def cpu_reference_run(rnet, frames_nchw, max_steps, seconds, warmup=1, warmup_seconds=30.0):
+    """The reference's CPU path for the stem features: SarbonVideo without a CUDA device
+    runs the dense stem on every frame (video.py:101-104), fp32, all host threads.  One
+    stream-frame per step.  Returns (frames/s, timed steps, threads, warm-up steps)."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    nw, t0 = 0, time.perf_counter()
+    with torch.no_grad():
+        while nw < max(1, warmup):
+            rnet(frames_nchw[nw % len(frames_nchw)])
+            nw += 1
+            if time.perf_counter() - t0 > warmup_seconds:
+                break
+        n, t0 = 0, time.perf_counter()
+        while n < max_steps:
+            rnet(frames_nchw[(nw + n) % len(frames_nchw)])
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+    return n / (time.perf_counter() - t0), n, torch.get_num_threads(), nw
+
+
+def gpu_reference_run(ref, net, seq, tau, steps, dev):
+    """The reference's own FusedSparseEngine (Triton tile kernel JIT-compiled for this GPU,
+    CUDA graphs, one host sync per step; sarbon/sparse/fused_engine.py:54-240) on the same
+    staged frames and weights: frames/s over `steps` steps after one warm-up pass over the
+    sequence (which captures the budget buckets the sequence needs), CUDA events."""
+    _, fe = ref
+    rnet = reference_net(ref, net).to(dev)
+    S, H, W = seq[0].shape[:3]
+    eng = fe.FusedSparseEngine(rnet, S, H, W, dtype=torch.float16, tau=tau, device=str(dev))
+    eng.reset(seq[0])
+    modes = {}
+    for f in seq[1:] + seq[:1]:
+        m, _ = eng.step(f)
+        modes[m] = modes.get(m, 0) + 1
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        eng.step(seq[1 + i % (len(seq) - 1)])
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    del eng
+    return {"value": S * steps / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms / steps, "steps": steps,
+            "modes_warmup": modes, "what": "the reference FusedSparseEngine (its Triton tile kernel, "
+            "CUDA graphs and per-step host sync) on the same frames and weights, this GPU"}
 
 
 def time_mask_kernels(dev, S, H, W, block, seconds=2.0):
@@ -318,19 +441,34 @@ def run_reference(args):
     from sarbon_b200 import scenes
     net = build_net(args.seed)
     u8, rects = make_frames(args, 0, "cpu")
-    seq = [scenes.normalise(u8[i, :1]).numpy() for i in pingpong(min(args.frames, 8))]
+    order = pingpong(min(args.frames, 8))
     tau = 8 / float(scenes.STD.mean())
     budget = max(10.0, min(150.0, 0.5 * args.steps))
-    fps, n, cores, nw = cpu_run(net, seq, tau, args.steps, budget, warmup=args.warmup)
+    from sarbon_b200.multi import shard_streams
+    S = len(shard_streams(job_streams(args, world), world, 0))
+    ref = import_reference()
+    if ref is not None:
+        rnet = reference_net(ref, net)
+        frames = [scenes.normalise(u8[i, :1], torch.float32).permute(0, 3, 1, 2).contiguous() for i in order]
+        fps, n, cores, nw = cpu_reference_run(rnet, frames, args.steps, budget, warmup=args.warmup)
+        kind, dtype = "reference", "f32 (the reference's dense CPU path)"
+        sample = (f"{n} steps of 1 stream x {args.width}x{args.height}: the reference's own LocalBackbone "
+                  f"forward (sarbon/sparse/block_sparse.py:62-76, installed under baseline/_ref), the stem "
+                  f"SarbonVideo runs per frame without CUDA (video.py:101-104); torch threads = host cores")
+    else:
+        seq = [scenes.normalise(u8[i, :1]).numpy() for i in order]
+        fps, n, cores, nw = cpu_run(net, seq, tau, args.steps, budget, warmup=args.warmup)
+        kind, dtype = "port", "f16 in / f32 accumulate (numpy fp32)"
+        sample = (f"{n} steps of 1 stream x {args.width}x{args.height} after reset (numpy oracle restating "
+                  f"sarbon/sparse, BLAS threads = host cores; the reference is not installed under baseline/_ref)")
     line = {"metric": METRIC, "value": fps, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": n,
-            "warmup": nw, "ms_per_step": 1e3 / fps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16 in / f32 accumulate (numpy fp32)", "data": "synthetic",
-            "config": {"workload": f"1080p, {args.streams} streams/GPU, ~5% changed blocks",
-                       "height": args.height, "width": args.width, "streams_per_gpu": args.streams,
+            "warmup": nw, "ms_per_step": 1e3 / fps, "higher_is_better": True,
+            "scaling": "strong" if args.total_streams else "weak",
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+            "config": {"workload": workload_name(args, world),
+                       "height": args.height, "width": args.width, "streams_per_gpu": S,
                        "rects_per_stream": rects, "sample": "1 stream-frame per step"},
-            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"{n} steps of 1 stream x {args.width}x{args.height} after reset "
-                                       f"(numpy oracle restating sarbon/sparse, BLAS threads = host cores)"},
+            "cpu_baseline": {"value": fps, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": fps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -359,7 +497,11 @@ def run_b200(args):
     dev = torch.device("cuda", local)
     tau = 8 / float(scenes.STD.mean())
     net = build_net(args.seed).to(dev)
-    S, H, W = args.streams, args.height, args.width
+    from sarbon_b200.multi import shard_streams
+    if args.total_streams and args.total_streams % world:
+        raise SystemExit(f"--total-streams {args.total_streams} does not split evenly over {world} GPUs")
+    S = len(shard_streams(job_streams(args, world), world, rank))
+    H, W = args.height, args.width
     eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev)
     if args.cell:
         eng.set_cell_gating(args.cell)  # the u8 end-to-end step gates per block only
@@ -416,6 +558,7 @@ def run_b200(args):
     per_layer = [0.0] * len(eng.layers)
     conv_flops, gbytes, nprof = 0, 0, 0
     flops_layer = [0] * len(eng.layers)
+    mma_layer = [0] * len(eng.layers)
     eng.reset(seq[0])
     for i in range(args.profile_steps):
         f = seq[1 + i % (len(seq) - 1)]
@@ -432,23 +575,28 @@ def run_b200(args):
             fl = layer_flops(eng, counts, mode)
             conv_flops += sum(fl)
             flops_layer = [a + b for a, b in zip(flops_layer, fl)]
+            mma_layer = [a + b for a, b in zip(mma_layer, mma_flops(eng, mode))]
         gbytes += gate_bytes(eng, int(eng.changed.sum().item()))
         nprof += 1
     peaks, src = load_peaks()
-    traffic = load_traffic(S)
+    default_workload = (S, H, W) == (16, 1088, 1920) and not args.cell
+    traffic = TRAFFIC if default_workload else {"conv": None, "gate": None, "capture": None}
     n_conv = nprof * len(eng.layers)
     conv_tflops = conv_flops / (prof["conv"] * 1e-3) / 1e12
     gate_gbs = gbytes / (prof["gate"] * 1e-3) / 1e9
+    # the kernels are timed one launch at a time (CUDA events around each launch of a
+    # 24-step pass): the burst GEMM peak is the matching denominator
     roof = {"bound": "tensor", "kernel": "sb::conv_tc_kernel (tile conv, all 11 layers)",
-            "achieved": conv_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
-            "frac": conv_tflops / peaks["bf16_tflops_sustained"],
-            "traffic": traffic.get("conv"), "traffic_source": "ncu dram__bytes_read+write per conv launch, "
-            "8-stream capture scaled to this stream count (profiles/dram_traffic_8x1080p_5pct.md)",
-            "peak_source": f"{src} bf16_tflops_sustained (fp16 dense = bf16 rate)",
-            "flops_per_launch": conv_flops / n_conv, "ms_per_launch": prof["conv"] / n_conv}
+            "achieved": conv_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": conv_tflops / peaks["bf16_tflops"],
+            "traffic": traffic["conv"], "traffic_source": traffic["capture"],
+            "peak_source": f"{src} bf16_tflops (burst; fp16 dense runs at the bf16 rate; each launch "
+                           f"is timed alone by CUDA events)",
+            "flops_per_launch": conv_flops / n_conv, "mma_flops_per_launch": sum(mma_layer) / n_conv,
+            "ms_per_launch": prof["conv"] / n_conv}
     roof_gate = {"bound": "hbm", "kernel": "sb::gate_kernel<0>", "achieved": gate_gbs, "peak": peaks["hbm_gbs"],
                  "unit": "GB/s", "frac": gate_gbs / peaks["hbm_gbs"], "bytes_per_launch": gbytes / nprof,
-                 "traffic": traffic.get("gate"),
+                 "traffic": traffic["gate"], "traffic_source": traffic["capture"],
                  "ms_per_launch": prof["gate"] / nprof}
     share = {k: v / sum(prof.values()) for k, v in prof.items()}
 
@@ -499,12 +647,33 @@ def run_b200(args):
 
     # --- CPU baseline (rank 0, N = 1 only)
     cpu = None
+    ref = import_reference()
+    ref_gpu = None
+    if rank == 0 and world == 1 and not args.no_reference_gpu:
+        if ref is None:
+            ref_gpu = {"unavailable": "the reference is not installed under baseline/_ref"}
+        else:
+            try:
+                ref_gpu = gpu_reference_run(ref, net, seq[:len(seq)], tau, args.reference_gpu_steps, dev)
+            except Exception as ex:  # report, do not fail the bench
+                ref_gpu = {"unavailable": f"{type(ex).__name__}: {str(ex)[:200]}"}
+            torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu:
-        cseq = [scenes.normalise(u8[i, :1]).cpu().numpy() for i in pingpong(min(args.frames, 8))]
-        fps, n, cores, _ = cpu_run(net.cpu(), cseq, tau, 64, args.cpu_seconds)
-        cpu = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{n} steps of 1 stream x {W}x{H} (numpy oracle restating sarbon/sparse; "
-                         f"BLAS threads = host cores)"}
+        order = pingpong(min(args.frames, 8))
+        if ref is not None:
+            rnet = reference_net(ref, net)
+            frames = [scenes.normalise(u8[i, :1].cpu(), torch.float32).permute(0, 3, 1, 2).contiguous()
+                      for i in order]
+            fps, n, cores, _ = cpu_reference_run(rnet, frames, 64, args.cpu_seconds)
+            cpu = {"value": fps, "unit": UNIT, "cores": cores, "kind": "reference",
+                   "sample": f"{n} steps of 1 stream x {W}x{H}: the reference's dense CPU stem "
+                             f"(LocalBackbone forward, fp32; video.py:101-104); torch threads = host cores"}
+        else:
+            cseq = [scenes.normalise(u8[i, :1]).cpu().numpy() for i in order]
+            fps, n, cores, _ = cpu_run(net.cpu(), cseq, tau, 64, args.cpu_seconds)
+            cpu = {"value": fps, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"{n} steps of 1 stream x {W}x{H} (numpy oracle restating sarbon/sparse; "
+                             f"BLAS threads = host cores)"}
 
     if world > 1:
         dist.barrier()
@@ -514,9 +683,10 @@ def run_b200(args):
     value = job_rate(world, S, args.steps, ms_max)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16 (fp32 accumulate)",
+            "scaling": "strong" if args.total_streams else "weak", "vs_baseline": None,
+            "dtype": "f16 (fp32 accumulate)",
             "data": "synthetic (seeded moving-rectangle camera streams, random-init Sarbon-S stem)",
-            "config": {"workload": f"1080p x {S} streams/GPU, ~5% changed blocks",
+            "config": {"workload": workload_name(args, world), "job_streams": job_streams(args, world),
                        "height": H, "width": W, "block": 32, "streams_per_gpu": S, "rects_per_stream": rects,
                        "gating": f"cell level, {args.cell} px cells" if args.cell else "block level",
                        "tau_grey_levels": 8, "frames_staged": args.frames,
@@ -529,8 +699,11 @@ def run_b200(args):
             "conv_us_per_layer": {l.dst: round(1e3 * t / max(nprof, 1), 1) for l, t in zip(eng.layers, per_layer)},
             "conv_tflops_per_layer": {l.dst: round(f / (t * 1e-3) / 1e12, 1) if t > 0 else None
                                       for l, f, t in zip(eng.layers, flops_layer, per_layer)},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "mask_kernels": masks,
-            "clocks": clock_info}
+            # issued tensor-core work over algorithmic work per layer (window regions, K padding)
+            "conv_mma_over_alg_per_layer": {l.dst: round(m / f, 3) if f else None
+                                            for l, f, m in zip(eng.layers, flops_layer, mma_layer)},
+            "cpu_baseline": cpu, "reference_gpu": ref_gpu, "e2e": e2e, "gpu_launches": launches,
+            "mask_kernels": masks, "clocks": clock_info}
     print(json.dumps(line), flush=True)
 
 

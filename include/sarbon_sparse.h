@@ -158,6 +158,13 @@ SB_API int sb_set_cell_gating(sb_engine* e, int cell, const int* cell_radii, int
  * image cache from `frames_dev` where `changed` is set. */
 SB_API int sb_run_sparse_forced(sb_engine* e, const void* frames_dev, int64_t n_tiles, void* stream);
 
+/* Dense recompute of layers first..last only (the per-layer loop of the reference's
+ * dense pass, fused_engine.py:176-185), every block, from the caches as they are: the
+ * image cache is not touched and the gate is not run.  With caches loaded from another
+ * implementation (sb_cache_ptr), one layer's output from that implementation's own inputs
+ * can be compared layer by layer. */
+SB_API int sb_dense_layers(sb_engine* e, int first, int last, void* stream);
+
 /* Cache views (fused_engine.py:67-71,124-125): device pointer and NHWC shape of
  * cache id (0 = image, i+1 = layer i output). */
 SB_API int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]);

@@ -167,8 +167,9 @@ void set_threshold(sb_engine* e, double tau) {
   }
 }
 
-int launch_convs(sb_engine* e, cudaStream_t s) {
-  for (int i = 0; i < e->n_layers; ++i) {
+int launch_convs(sb_engine* e, cudaStream_t s, int first = 0, int last = -1) {
+  if (last < 0) last = e->n_layers - 1;
+  for (int i = first; i <= last; ++i) {
     const sb_layer_desc& L = e->layers[i];
     if (!e->wok[i]) return fail(SB_EINVAL, "weights of layer " + std::to_string(i) + " not uploaded");
     ConvArgs a{};
@@ -695,6 +696,16 @@ int sb_run_sparse_forced(sb_engine* e, const void* frames_dev, int64_t n_tiles, 
   if (rc) return rc;
   SB_CUDA(launch_set_mode(e->st, SB_MODE_SPARSE, 0, 0, s));
   return SB_OK;
+}
+
+int sb_dense_layers(sb_engine* e, int first, int last, void* stream) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (first < 0 || last < first || last >= e->n_layers) return fail(SB_EINVAL, "layer range out of range");
+  SB_CUDA(cudaSetDevice(e->dev));
+  cudaStream_t s = (cudaStream_t)stream;
+  SB_CUDA(launch_set_mode(e->st, SB_MODE_DENSE, 0, 0, s));
+  e->last_launches = 1;
+  return launch_convs(e, s, first, last);
 }
 
 int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]) {

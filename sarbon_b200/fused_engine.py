@@ -340,6 +340,14 @@ class FusedSparseEngine:
         mode, k = self.query()
         return mode, k, [ms[i] for i in range(n.value)]
 
+    @torch.no_grad()
+    def dense_layers(self, first, last=None):
+        """Recompute layers ``first..last`` densely from the caches as they are (the image
+        cache and the gate untouched): one layer of this engine on inputs loaded from
+        elsewhere, e.g. the reference's own caches."""
+        last = first if last is None else last
+        check(lib().sb_dense_layers(self._h.ptr, int(first), int(last), self._stream()), "sb_dense_layers")
+
     def result_view(self):
         """int64 [2] device tensor {mode, count} written by every step's last kernel."""
         p = C.c_void_p()

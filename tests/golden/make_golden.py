@@ -1,8 +1,8 @@
 """Generate golden vectors by running the reference engine itself on CPU.
 
-Run once in a container that has the reference checkout (its path is the first
-argument, default ``/root/reference``); the GPU tests only read the ``.npz`` files
-written next to this script and never need the reference.
+Run once in a container that has the reference checkout (its path is the first,
+required argument); the GPU tests only read the ``.npz`` files written next to this
+script and never need the reference.
 
 The reference ``FusedSparseEngine`` (sarbon/sparse/fused_engine.py) normally runs
 on CUDA with CUDA graphs; here it runs on CPU with Triton's interpreter
@@ -12,7 +12,7 @@ replays the body eagerly. Every number in the fixtures comes from the
 reference's own code: its gate, its ``nonzero_static`` lists, its Triton tile
 kernel (interpreted) and its dense ``F.conv2d`` path.
 
-Usage: python tests/golden/make_golden.py [/path/to/reference]
+Usage: python tests/golden/make_golden.py /path/to/reference [case ...]
 """
 import os
 import sys
@@ -25,9 +25,12 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 OUT = Path(__file__).resolve().parent
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) < 2:
+    sys.exit("usage: make_golden.py /path/to/reference [case ...]")
+REF = Path(sys.argv[1])
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(OUT.parent))
+sys.path.insert(0, str(OUT.parent.parent))
 from golden_io import conv_specs, golden_weights, weights_digest  # noqa: E402
 
 from sarbon.sparse import LocalBackbone  # noqa: E402
@@ -77,8 +80,14 @@ def _rect(frames, cam, y, x, h, w, value):
     frames[cam, y:y + h, x:x + w] = value
 
 
-def run_case(name, dtype, n_cams, h, w, block, tau, refresh, domain, seed, steps):
-    """Drive the reference engine through `steps` and record everything it produced."""
+def _all_caches(eng):
+    return {k: v.float().numpy().copy() for k, v in eng.cache.items()}
+
+
+def run_case(name, dtype, n_cams, h, w, block, tau, refresh, domain, seed, steps, all_caches=False):
+    """Drive the reference engine through `steps` and record everything it produced.
+    With ``all_caches`` every cache (image and all layers) is also kept after the reset
+    and after the last step, for layer-by-layer checks from the reference's own inputs."""
     torch.manual_seed(seed)
     net = LocalBackbone().eval()
     # replace the random init by the seeded, fp16-representable weights of golden_io
@@ -94,8 +103,13 @@ def run_case(name, dtype, n_cams, h, w, block, tau, refresh, domain, seed, steps
     eng = fe.FusedSparseEngine(net, n_cams, h, w, block=block, dtype=dtype, tau=tau,
                                refresh=refresh, device="cpu")
     g = torch.Generator().manual_seed(seed + 1)
+    scene = None
     if domain == "unit":
         frames = torch.rand(n_cams, h, w, 3, generator=g).to(dtype)
+    elif domain == "norm":  # the bench's camera streams, normalised as SarbonVideo._prep does
+        from sarbon_b200 import scenes
+        scene = scenes.Streams(n_cams, h, w, seed=seed, n_rects=1)
+        frames = scenes.normalise(scene.next(), dtype)
     else:  # integer-valued raw 0..255 frames
         frames = torch.randint(0, 256, (n_cams, h, w, 3), generator=g).to(dtype)
     rec = {"frames0": frames.float().numpy().astype(np.float16 if dtype == torch.float16 else np.float32, copy=True)}
@@ -103,6 +117,8 @@ def run_case(name, dtype, n_cams, h, w, block, tau, refresh, domain, seed, steps
     eng.reset(frames)
     rec["reset_t7"] = eng.cache["t7"].float().numpy().copy()
     rec["reset_t14"] = eng.cache["t14"].float().numpy().copy()
+    if all_caches:
+        rec["reset_caches"] = _all_caches(eng)
     log = []
     for i, ev in enumerate(steps):
         frames = frames.clone()
@@ -123,6 +139,9 @@ def run_case(name, dtype, n_cams, h, w, block, tau, refresh, domain, seed, steps
             eng.set_extra(m)
         elif kind == "clear_extra":
             eng.set_extra(torch.zeros_like(eng.extra))
+        elif kind == "scene":  # next frame of the camera streams
+            from sarbon_b200 import scenes
+            frames = scenes.normalise(scene.next(), dtype)
         elif kind == "same":
             pass
         mode, k = eng.step(frames)
@@ -148,6 +167,8 @@ def run_case(name, dtype, n_cams, h, w, block, tau, refresh, domain, seed, steps
         log.append(step)
         print(f"  {name} step {i}: {mode} k={k}", flush=True)
     rec["steps"] = log
+    if all_caches:
+        rec["final_caches"] = _all_caches(eng)
     print(f"{name}: {time.time() - t0:.1f}s", flush=True)
     nodes, outs = _net_arrays(net)
     rec["weight_seed"], rec["weights_sha256"] = seed, digest
@@ -182,15 +203,25 @@ def save(name, meta, rec, nodes, outs, eng):
         if "lists" in s:
             for d, l in s["lists"].items():
                 arrays[p + f"list{d}"] = l
+    for when in ("reset", "final"):
+        if when + "_caches" in rec:
+            for key, v in rec[when + "_caches"].items():
+                arrays[f"{when}_cache_{key}"] = v.astype(fdt)
     steps = [{"mode": s["mode"], "k": int(s["k"]), "cap": int(s.get("cap", 0))} for s in rec["steps"]]
     topo = nodes
     import json
     arrays["meta_json"] = np.frombuffer(json.dumps({
-        **meta, "weight_seed": rec["weight_seed"], "weights_sha256": rec["weights_sha256"], "steps": steps, "nodes": topo, "outputs": list(outs), "ds": list(eng.ds),
+        **{k: v for k, v in meta.items() if k != "all_caches"}, "all_caches": bool(meta.get("all_caches")),
+        "weight_seed": rec["weight_seed"], "weights_sha256": rec["weights_sha256"], "steps": steps, "nodes": topo, "outputs": list(outs), "ds": list(eng.ds),
         "buckets": list(eng.buckets), "hb": eng.hb, "wb": eng.wb}).encode(), np.uint8)
     np.savez_compressed(OUT / f"{name}.npz", **arrays)
     print(f"wrote {name}.npz ({(OUT / f'{name}.npz').stat().st_size / 1e6:.2f} MB)", flush=True)
 
+
+# SarbonVideo's engine threshold for its default-style tau of 8 grey levels, computed as
+# video.py:63-64 computes it: tau * 255 / float(STD.mean()) with STD the float32 array
+_STD = np.array([0.229, 0.224, 0.225], np.float32) * 255
+TAU_8_GREY = (8 / 255) * 255 / float(_STD.mean())
 
 CASES = {
     # the reference test's own scenario (tests/test_fused_engine.py:24-45), smaller frames
@@ -210,6 +241,14 @@ CASES = {
                          domain="raw", seed=7,
                          steps=[("noise",), ("rect", 0, 30, 40, 20, 50), ("extra", 1, 2, 3),
                                 ("clear_extra",), ("noise",)]),
+    # the production gate setting: normalised fp16 camera frames (SarbonVideo._prep) with
+    # tau = 8 grey levels (SarbonVideo(tau=8/255), video.py:63-64), refresh and an extra
+    # mask; every cache kept after the reset and after the last step
+    "norm_tau_fp16": dict(dtype=torch.float16, n_cams=2, h=96, w=192, block=32,
+                          tau=TAU_8_GREY, refresh=5,
+                          domain="norm", seed=11, all_caches=True,
+                          steps=[("scene",), ("scene",), ("extra", 1, 1, 4), ("scene",), ("clear_extra",),
+                                 ("scene",)]),
 }
 
 

@@ -46,6 +46,11 @@ def load(name):
         if p + f"list{meta['ds'][0]}" in z:
             st["lists"] = {d: z[p + f"list{d}"] for d in meta["ds"]}
         case["steps"].append(st)
+    for when in ("reset", "final"):
+        pre = f"{when}_cache_"
+        caches = {k[len(pre):]: z[k].astype(fdt) for k in z.files if k.startswith(pre)}
+        if caches:
+            case[when + "_caches"] = caches
     return case
 
 
@@ -55,21 +60,44 @@ def feature_tol(dtype):
     return (1e-2, 1e-3) if dtype == np.float16 else (1e-5, 1e-6)
 
 
-def assert_close(a, b, dtype, what=""):
-    """fp16: every element within 1e-3 + 1e-2 * max|b| (relative to the feature map's
-    scale, the reference test's max-abs / max-ref metric, plus an absolute floor); errors
-    of deep layers scale with the map, not with each element.  fp32: max-abs / max-ref
-    below 1e-5, exactly the reference test's check."""
+def fp16_ulp(x):
+    """Spacing of fp16 numbers at |x| (one unit in the last place)."""
+    return np.spacing(np.abs(np.asarray(x, np.float16))).astype(np.float64)
+
+
+def assert_close(a, b, dtype, what="", extra_ulps=0):
+    """fp16: every element within 1e-3 + 1e-2 * |b| (elementwise), widened by
+    ``extra_ulps`` fp16 units of the map's largest value for outputs that went through
+    several layers of independently rounded fp16 caches (each layer rounds its fp32
+    accumulation once; two implementations that sum in different orders differ by an
+    ulp here and there, and those differences travel through the later layers).
+    fp32: max-abs / max-ref below 1e-5, exactly the reference test's check.
+    Returns the largest error as a multiple of the bound."""
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     rtol, atol = feature_tol(dtype)
     if dtype == np.float16:
-        bound = atol + rtol * np.abs(b).max()
+        bound = atol + rtol * np.abs(b) + extra_ulps * fp16_ulp(np.abs(b).max())
         err = np.abs(a - b)
-        assert (err <= bound).all(), f"{what}: {(err > bound).sum()} elements above {bound:.3g}; max abs err {err.max():.3g}"
+        worst = float((err / bound).max()) if err.size else 0.0
+        assert (err <= bound).all(), (f"{what}: {(err > bound).sum()} of {err.size} elements above "
+                                      f"1e-3 + 1e-2|b| + {extra_ulps} ulp(max|b|); max abs err {err.max():.3g}, "
+                                      f"worst err/bound {worst:.3g}")
+        return worst
     else:
         err = np.abs(a - b).max() / max(np.abs(b).max(), 1e-30)
         assert err < rtol, f"{what}: max rel err {err:.3g} >= {rtol}"
+        return float(err / rtol)
+
+
+# fp16 allowance of the end-to-end outputs checked against the reference's own caches:
+# p4 (t7, 8 conv layers deep) and p8 (t14, 11 layers) are held to the elementwise
+# 1e-2 / 1e-3 bar plus 2 and 4 fp16 ulps of the map's largest value.  Measured for the
+# oracle against the reference over every fp16 fixture: at most 0.11 ulp (t7) and 0.78 ulp
+# (t14) beyond the plain bar.  Every single layer, computed from the reference's own input
+# caches, meets the plain elementwise bar with no allowance
+# (tests/test_gpu_golden_layers.py, test_oracle_every_layer_from_reference_inputs).
+OUTPUT_ULPS = {"t7": 2, "t14": 4}
 
 
 def golden_weights(convs, seed):
