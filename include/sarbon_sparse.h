@@ -224,16 +224,31 @@ SB_API int sb_debug_lists(sb_engine* e, int d_index, int32_t** cam, int32_t** by
  *              ascending flat order (nonzero_static, fused_engine.py:161-165); entries
  *              past the count are left as they were
  *   counts_dev int32 [n_dil] (may be NULL): active blocks per dilation, or -1 in every
- *              slot if a bounded device wait gave up (the lists are then invalid).
+ *              slot if a bounded device wait gave up (the lists are then invalid).  It
+ *              is the only failure signal of the device side: a caller that needs to know
+ *              that its lists are valid must pass it.
+ * Dilations larger than max(hb, wb) give the same masks as max(hb, wb) and are clamped.
  * Its scratch is one static device array sized for n_cams*hb*wb <= SB_STATIC_LISTS_MAX_BLOCKS;
  * larger masks are rejected with SB_EINVAL.  Every call on a device shares that array:
  * calls must be ordered (one stream, or events between streams); overlapping calls race.
  * The first call on each device looks the array up (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture on the device. */
+ * device current and keeps the address for the life of the process; make that first
+ * call before any stream capture on the device, and do not use the entry point across a
+ * cudaDeviceReset (the kept address would be stale).  The array is 33,024 bytes. */
 #define SB_STATIC_LISTS_MAX_BLOCKS (1 << 20)
 SB_API int sb_block_lists_static(const uint8_t* changed_dev, int n_cams, int hb, int wb, const int* dilations,
                                  int n_dil, uint8_t* masks_dev, int32_t* lists_dev, int32_t* counts_dev,
                                  void* stream);
+
+/* Test hook with no counterpart in the reference: in the steps of engine `e` (or, with
+ * e == NULL, the sb_block_lists_static calls) launched after this call, list-kernel chunk
+ * `withhold_chunk` (blocks withhold_chunk*1024 .. +1023; -1 = none) publishes no look-back
+ * words, and every look-back wait gives up after `spin_limit` polls (0 = the default limit,
+ * 2^24 polls).  The next chunk's bounded wait then runs out: the list kernel sets its
+ * timeout flag and finishes, the step completes without a fault, and the host sees
+ * SB_ETIMEOUT from sb_step (and the flag in sb_stats().error) or -1 counts from
+ * sb_block_lists_static.  The lists and features of such a step are invalid.  Synchronous. */
+SB_API int sb_debug_withhold_lookback(sb_engine* e, int withhold_chunk, int spin_limit);
 
 /* Counters (fused_engine.py:92,239) and sticky device errors (synchronises). */
 SB_API int sb_stats(sb_engine* e, void* stream, sb_stats_t* out);

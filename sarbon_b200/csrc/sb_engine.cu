@@ -9,6 +9,7 @@
 // Every conv kernel reads the mode and its list length from device memory and runs a
 // persistent grid, so there is no host sync inside a step.
 #include <algorithm>
+#include <cstddef>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -652,7 +653,15 @@ int sb_set_cell_gating(sb_engine* e, int cell, const int* cell_radii, int n_radi
     if (rc) return rc;
     e->cmasks = static_cast<uint8_t*>(p);
   }
-  if (e->cells_cell != cell) {  // cells of another size: a new buffer (the old one stays owned)
+  if (e->cells_cell != cell) {  // cells of another size: the old buffer is freed, a new one made
+    if (e->cells) {
+      SB_CUDA(cudaDeviceSynchronize());  // no launched step may still write the old buffer
+      e->allocs.erase(std::remove(e->allocs.begin(), e->allocs.end(), static_cast<void*>(e->cells)),
+                      e->allocs.end());
+      SB_CUDA(cudaFree(e->cells));
+      e->cells = nullptr;
+      e->cells_cell = 0;
+    }
     void* p = nullptr;
     int rc = alloc_dev(e, &p, (size_t)e->n * (e->h / cell) * (e->w / cell));
     if (rc) return rc;
@@ -706,6 +715,23 @@ int sb_dense_layers(sb_engine* e, int first, int last, void* stream) {
   SB_CUDA(launch_set_mode(e->st, SB_MODE_DENSE, 0, 0, s));
   e->last_launches = 1;
   return launch_convs(e, s, first, last);
+}
+
+int sb_debug_withhold_lookback(sb_engine* e, int withhold_chunk, int spin_limit) {
+  if (withhold_chunk < -1 || spin_limit < 0) return fail(SB_EINVAL, "withhold_chunk >= -1 and spin_limit >= 0");
+  if (!e) {
+    static_lists_debug(withhold_chunk, (unsigned)spin_limit);
+    return SB_OK;
+  }
+  SB_CUDA(cudaSetDevice(e->dev));
+  const int32_t w = withhold_chunk >= 0 ? withhold_chunk + 1 : 0;
+  const uint32_t lim = (uint32_t)spin_limit;
+  // synchronous copies: ordered after every step launched so far on any stream
+  SB_CUDA(cudaMemcpy(reinterpret_cast<uint8_t*>(e->st) + offsetof(State, lb_withhold), &w, 4,
+                     cudaMemcpyHostToDevice));
+  SB_CUDA(cudaMemcpy(reinterpret_cast<uint8_t*>(e->st) + offsetof(State, lb_spin_limit), &lim, 4,
+                     cudaMemcpyHostToDevice));
+  return SB_OK;
 }
 
 int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]) {

@@ -330,7 +330,7 @@ SB_DEV uint32_t warp_sum(uint32_t v) {
 // Exclusive prefix of chunk `chunk` in the look-back array `stat` (executed by a full warp;
 // the result is returned on every lane).  Lane i reads predecessor p - i; a window is
 // usable once every lane up to the nearest inclusive prefix has published.
-SB_DEV uint32_t lookback(unsigned long long* stat, uint32_t chunk, uint32_t epoch, State* st) {
+SB_DEV uint32_t lookback(unsigned long long* stat, uint32_t chunk, uint32_t epoch, State* st, uint32_t limit) {
   const uint32_t lane = threadIdx.x & 31;
   uint32_t excl = 0;
   int p = (int)chunk - 1;
@@ -344,7 +344,7 @@ SB_DEV uint32_t lookback(unsigned long long* stat, uint32_t chunk, uint32_t epoc
     const uint32_t incm = __ballot_sync(0xFFFFFFFFu, inc);
     const uint32_t upto = incm ? (2u << (__ffs(incm) - 1)) - 1u : 0xFFFFFFFFu;  // lanes 0..first inclusive
     if (notready & upto) {
-      if (++spins > SB_SPIN_LIMIT) {
+      if (++spins > limit) {
         if (lane == 0) atomicOr(&st->error, SB_ERR_TIMEOUT_LOOKBK);
         break;
       }
@@ -439,9 +439,13 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
   __shared__ uint32_t s_warp[ML][LIST_WARPS];
   __shared__ uint32_t s_excl[ML];
   const uint32_t epoch = st->epoch;
+  const uint32_t spin_limit = st->lb_spin_limit ? st->lb_spin_limit : SB_SPIN_LIMIT;
   if (threadIdx.x == 0) s_chunk = atomicAdd(&st->ticket, 1u);
   __syncthreads();
   const uint32_t chunk = s_chunk;
+  // test hook: this chunk keeps its look-back words unpublished, so its successor's bounded
+  // wait runs out (sb_debug_withhold_lookback)
+  const bool publish = st->lb_withhold != (int32_t)chunk + 1;
   const int nchunks = gridDim.x;
   const int f = (int)chunk * LIST_THREADS + threadIdx.x;
   const int per = a.hb * a.wb, ncam = a.n_blocks / per;
@@ -507,11 +511,11 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
     unsigned long long* stat = a.status + (size_t)L * nchunks;
     uint32_t excl = 0;
     if (chunk == 0) {
-      if (lane == 0) lb_store(stat, lb_pack(epoch, LB_FLAG_INC, agg));
+      if (lane == 0 && publish) lb_store(stat, lb_pack(epoch, LB_FLAG_INC, agg));
     } else {
-      if (lane == 0) lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_AGG, agg));
-      excl = lookback(stat, chunk, epoch, st);
-      if (lane == 0) lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_INC, excl + agg));
+      if (lane == 0 && publish) lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_AGG, agg));
+      excl = lookback(stat, chunk, epoch, st, spin_limit);
+      if (lane == 0 && publish) lb_store(stat + chunk, lb_pack(epoch, LB_FLAG_INC, excl + agg));
     }
     if (lane == 0) {
       s_excl[L] = excl;

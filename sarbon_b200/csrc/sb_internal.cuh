@@ -39,6 +39,10 @@ struct State {
   int32_t pad_;
   int64_t result[2];    // {mode, count} of the last finished step
   int32_t rcounts[SB_MAX_RKINDS][SB_MAX_DILATIONS];  // active regions per region kind and dilation
+  // test hook (sb_debug_withhold_lookback): list chunk lb_withhold - 1 publishes no look-back
+  // words (0 = none); look-back waits give up after lb_spin_limit polls (0 = SB_SPIN_LIMIT)
+  int32_t lb_withhold;
+  uint32_t lb_spin_limit;
 };
 
 struct GateArgs {
@@ -149,6 +153,10 @@ cudaError_t conv_tc_make_tmap_out(CUtensorMap* map, void* dst, int n, int ho, in
 cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, const CUtensorMap* map_y, int grid_x,
                            cudaStream_t s);
 int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s, int mode);
+
+// Look-back test hook of sb_block_lists_static's calls launched after this one
+// (sb_debug_withhold_lookback with a NULL engine; sb_noalloc.cu).
+void static_lists_debug(int withhold_chunk, unsigned spin_limit);
 
 // Sets the message sb_last_error() returns on this thread; returns `code`.
 int record_error(int code, const char* msg);

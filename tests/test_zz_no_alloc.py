@@ -141,3 +141,21 @@ def test_static_lists_reject_oversize_and_bad_args():
     assert rc == 1 and b"n_dil" in lib().sb_last_error()
     rc = lib().sb_block_lists_static(None, 1, 4, 4, dil, 1, one, one, None, None)
     assert rc == 1 and b"null pointer" in lib().sb_last_error()
+
+
+def test_static_lists_huge_dilation_is_clamped():
+    """A dilation far beyond the grid (up to INT_MAX) marks every block of a camera that has
+    a change, exactly as a dilation of max(hb, wb) does."""
+    changed = torch.zeros((3, 9, 13), dtype=torch.uint8, device="cuda")
+    changed[0, 4, 6] = 1
+    changed[2, 0, 12] = 1
+    ds = [2 ** 31 - 1, 13, 1]
+    ch = changed.cpu().numpy()
+    for _ in range(2):
+        m, l, c = static_lists(changed, ds)
+        for i, d in enumerate(ds):
+            em, el = np_lists(ch, min(d, 13))
+            assert int(c[i]) == el.shape[1], d
+            assert np.array_equal(m[i].cpu().numpy(), em), d
+            assert np.array_equal(l[i, :, :el.shape[1]].cpu().numpy(), el), d
+    assert int(c[0]) == 2 * 9 * 13  # cameras 0 and 2 entirely, camera 1 nothing
