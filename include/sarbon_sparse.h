@@ -112,6 +112,15 @@ SB_API int sb_step(sb_engine* e, const void* frames_dev, void* stream, int* mode
 SB_API int sb_step_u8(sb_engine* e, const uint8_t* frames_dev, const float mean[3], const float std_[3],
                void* stream, int* mode_out, int64_t* count_out);
 
+/* The same step on uint8 BGR frames [N][cam_h][cam_w][3] of any camera size: the whole
+ * `_prep` of the caller (video.py:95-99: BGR->RGB, the bilinear resize to the engine size
+ * with align_corners=False when the sizes differ, (x - mean[c]) / std[c] in fp32) runs
+ * as one kernel of this library writing fp16 frames into an engine-owned buffer (allocated
+ * by the first call that resizes), which the step then gates.  Equal sizes take
+ * sb_step_u8's path (no extra pass).  fp16 engines only. */
+SB_API int sb_step_u8_resized(sb_engine* e, const uint8_t* frames_dev, int cam_h, int cam_w, const float mean[3],
+                              const float std_[3], void* stream, int* mode_out, int64_t* count_out);
+
 /* sb_step with a CUDA event before and after every kernel it launches (gate, lists,
  * dense copy, one conv per layer, finalize); synchronises `stream` and writes the
  * duration of each launch in ms to kernel_ms[0..*n_kernels).  Measurement aid with

@@ -54,6 +54,8 @@ PROTOTYPES = {
     "sb_step": (_I, [_P, _P, _P, C.POINTER(_I), C.POINTER(_I64)]),
     "sb_step_u8": (_I, [_P, _P, C.POINTER(C.c_float), C.POINTER(C.c_float), _P, C.POINTER(_I),
                         C.POINTER(_I64)]),
+    "sb_step_u8_resized": (_I, [_P, _P, _I, _I, C.POINTER(C.c_float), C.POINTER(C.c_float), _P,
+                                C.POINTER(_I), C.POINTER(_I64)]),
     "sb_query": (_I, [_P, _P, C.POINTER(_I), C.POINTER(_I64)]),
     "sb_step_profiled": (_I, [_P, _P, _P, C.POINTER(C.c_float), _I, C.POINTER(_I)]),
     "sb_result_ptr": (_I, [_P, C.POINTER(_P)]),

@@ -108,6 +108,7 @@ struct sb_engine {
   uint8_t* cells = nullptr;   // [N][H/cell][W/cell], allocated by the first sb_set_cell_gating
   int cells_cell = 0;         // the cell size `cells` was allocated for
   uint8_t* cmasks = nullptr;  // [nd][N][Hb][Wb] block masks from the cells
+  void* prep = nullptr;       // [N][H][W][3] fp16 frames resized from the camera size (first use)
   std::vector<void*> allocs;
   // optional per-launch timing (sb_step_profiled)
   bool profiling = false;
@@ -575,6 +576,29 @@ int sb_step_u8(sb_engine* e, const uint8_t* frames_dev, const float mean[3], con
   if (!e || !mean || !std_) return fail(SB_EINVAL, "null argument");
   if (e->dtype != SB_F16) return fail(SB_EINVAL, "uint8 frames need an fp16 engine");
   return step_impl(e, frames_dev, 2, mean, std_, (cudaStream_t)stream, mode_out, count_out);
+}
+
+int sb_step_u8_resized(sb_engine* e, const uint8_t* frames_dev, int cam_h, int cam_w, const float mean[3],
+                       const float std_[3], void* stream, int* mode_out, int64_t* count_out) {
+  if (!e || !mean || !std_ || !frames_dev) return fail(SB_EINVAL, "null argument");
+  if (e->dtype != SB_F16) return fail(SB_EINVAL, "uint8 frames need an fp16 engine");
+  if (cam_h < 1 || cam_w < 1) return fail(SB_EINVAL, "camera size must be positive");
+  if (cam_h == e->h && cam_w == e->w)  // no resize: the uint8 path fused into the gate
+    return step_impl(e, frames_dev, 2, mean, std_, (cudaStream_t)stream, mode_out, count_out);
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, frames_dev) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
+    return fail(SB_EINVAL, "frames must be device memory");
+  SB_CUDA(cudaSetDevice(e->dev));
+  if (!e->prep) {
+    int rc = alloc_dev(e, &e->prep, (size_t)e->n * e->h * e->w * 3 * 2);
+    if (rc) return rc;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  SB_CUDA(launch_prep_resize(frames_dev, e->n, cam_h, cam_w, static_cast<__half*>(e->prep), e->h, e->w, mean, std_,
+                             e->n_sms, s));
+  const int rc = step_impl(e, e->prep, 0, nullptr, nullptr, s, mode_out, count_out);
+  e->last_launches += 1;
+  return rc;
 }
 
 int sb_step_profiled(sb_engine* e, const void* frames_dev, void* stream, float* kernel_ms, int capacity,

@@ -154,6 +154,11 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
                            cudaStream_t s);
 int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s, int mode);
 
+// uint8 BGR frames at camera size -> bilinear resize (align_corners=False) -> RGB,
+// (x - mean) / std, fp16 NHWC at engine size (sb_prep.cu)
+cudaError_t launch_prep_resize(const uint8_t* src, int n, int hin, int win, __half* dst, int hout, int wout,
+                               const float mean[3], const float stdv[3], int n_sms, cudaStream_t s);
+
 // Look-back test hook of sb_block_lists_static's calls launched after this one
 // (sb_debug_withhold_lookback with a NULL engine; sb_noalloc.cu).
 void static_lists_debug(int withhold_chunk, unsigned spin_limit);

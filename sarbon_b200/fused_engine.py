@@ -317,13 +317,24 @@ class FusedSparseEngine:
 
     @torch.no_grad()
     def step_u8(self, frames_u8, mean, std, sync=True):
-        """One step on uint8 BGR frames [N, H, W, 3] with normalisation fused into the gate
-        (the caller's ``_prep``: BGR->RGB, (x - mean) / std in fp32, fp16)."""
+        """One step on uint8 BGR frames [N, h, w, 3] (device memory) with the caller's
+        ``_prep`` (video.py:95-99) done by this library: BGR->RGB, (x - mean) / std in fp32,
+        fp16 -- fused into the gate at engine size, or, for cameras of another size, one
+        prep kernel that also resizes bilinearly (align_corners=False) to the engine size."""
+        if frames_u8.dtype != torch.uint8 or frames_u8.dim() != 4 or frames_u8.shape[0] != self.n \
+                or frames_u8.shape[3] != 3 or not frames_u8.is_contiguous():
+            raise ValueError(f"need contiguous uint8 frames [{self.n}, h, w, 3]")
         mean = (C.c_float * 3)(*[float(np.float32(v)) for v in mean])
         std = (C.c_float * 3)(*[float(np.float32(v)) for v in std])
         mode, k = C.c_int(), C.c_int64()
-        check(lib().sb_step_u8(self._h.ptr, C.c_void_p(frames_u8.data_ptr()), mean, std, self._stream(),
-                               C.byref(mode) if sync else None, C.byref(k) if sync else None), "sb_step_u8")
+        cam_h, cam_w = int(frames_u8.shape[1]), int(frames_u8.shape[2])
+        if (cam_h, cam_w) == (self.h, self.w):
+            check(lib().sb_step_u8(self._h.ptr, C.c_void_p(frames_u8.data_ptr()), mean, std, self._stream(),
+                                   C.byref(mode) if sync else None, C.byref(k) if sync else None), "sb_step_u8")
+        else:
+            check(lib().sb_step_u8_resized(self._h.ptr, C.c_void_p(frames_u8.data_ptr()), cam_h, cam_w, mean, std,
+                                           self._stream(), C.byref(mode) if sync else None,
+                                           C.byref(k) if sync else None), "sb_step_u8_resized")
         if sync:
             return self.MODES[mode.value], int(k.value)
         return None
