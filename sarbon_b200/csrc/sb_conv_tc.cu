@@ -59,6 +59,12 @@ template <int CIN, int NCTA, int T, int S, int WIN, int PAIR = 0>
 struct TcCfg {
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
+  // first layer: K slots per ky (its 3*CIN (kx, c) elements rounded up to even, so that each
+  // ky run starts on a 32-bit word of the A row); when two slots remain after the three runs
+  // they hold the bias: A = 1.0 there and B = the bias split into fp16 high and low parts,
+  // so the MMA adds it and the epilogue does not
+  static constexpr int KRUN = MANUAL ? ((3 * CIN + 1) / 2) * 2 : 0;
+  static constexpr bool BIAS_IN_K = MANUAL && 3 * KRUN + 2 <= KPAD;
   // K elements per K-block (WIN = 2: a pair of input pixels x channels)
   static constexpr int CH = MANUAL ? KPAD : WIN == 2 ? 64 : (CIN % 64 == 0 ? 64 : 32);
   static constexpr int NCH = (MANUAL || WIN == 2) ? 1 : CIN / CH;
@@ -534,39 +540,39 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           const int lr = r / T, lc = r % T;
           // element (ky, kx, c) of output (lr, lc): window row S*lr+ky, column
           // lead + (S*lc + kx)*CIN + c  (the window starts one input pixel left of the tile)
-          // The 3*CIN elements (kx, c) of one ky are contiguous in the window row and in the
-          // A row; they are read as 32-bit words (S = 2 puts every pixel's run at the same
-          // parity: it starts at an odd element when WIN_LEAD is odd) and shifted into place.
-          constexpr int RUN = 3 * CIN;
+          // The 3*CIN elements (kx, c) of one ky are contiguous in the window row; in the A
+          // row they fill K slots ky*KRUN .. (a run padded to even length), so each ky is
+          // read as 32-bit words (S = 2 puts every pixel's run at the same parity: it starts
+          // at an odd element when WIN_LEAD is odd) and realigned by funnel shifts.
+          constexpr int RUN = 3 * CIN, KRUN = C::KRUN, NW = KRUN / 2;
           constexpr int ODD = C::WIN_LEAD & 1;
           constexpr int NWD = (RUN + ODD + 1) / 2;
           const uint32_t* wrow32 =
               reinterpret_cast<const uint32_t*>(wbase + (S * lr) * C::WIN_COLS + (S * lc) * CIN - ODD);
-          uint16_t v[C::KPAD > 0 ? C::KPAD : 16];
+          uint32_t o[C::KPAD > 0 ? C::KPAD / 2 : 8];
 #pragma unroll
-          for (int k = 0; k < C::KPAD; ++k) v[k] = 0;
+          for (int k = 0; k < C::KPAD / 2; ++k) o[k] = 0u;
 #pragma unroll
           for (int ky = 0; ky < 3; ++ky) {
-            uint32_t w[NWD];
+            uint32_t w[NWD + 1];
 #pragma unroll
             for (int i = 0; i < NWD; ++i) w[i] = wrow32[ky * (C::WIN_COLS / 2) + i];
+            w[NWD] = 0u;
 #pragma unroll
-            for (int t = 0; t < RUN; ++t) {
-              const int h = t + ODD;
-              v[ky * RUN + t] = (uint16_t)(w[h >> 1] >> ((h & 1) * 16));
+            for (int j = 0; j < NW; ++j) {
+              uint32_t v = ODD ? __funnelshift_r(w[j], w[j + 1], 16) : w[j];
+              if (2 * j + 1 >= RUN) v &= 0xFFFFu;  // the run's padding slot
+              if (2 * j >= RUN) v = 0u;
+              o[ky * NW + j] = v;
             }
           }
+          if (C::BIAS_IN_K) o[3 * NW] = 0x3C003C00u;  // 1.0, 1.0: the bias's high and low parts
           uint8_t* row = sA + s * C::A_STAGE + r * C::ROWB;
           constexpr int NQ = C::ROWB / 16;
 #pragma unroll
           for (int q = 0; q < NQ; ++q) {
             const int pq = C::SWZ == 2 ? (q ^ (r & 7)) : (q ^ ((r >> 1) & 3));
-            uint4 w4;
-            w4.x = v[q * 8 + 0] | ((uint32_t)v[q * 8 + 1] << 16);
-            w4.y = v[q * 8 + 2] | ((uint32_t)v[q * 8 + 3] << 16);
-            w4.z = v[q * 8 + 4] | ((uint32_t)v[q * 8 + 5] << 16);
-            w4.w = v[q * 8 + 6] | ((uint32_t)v[q * 8 + 7] << 16);
-            *reinterpret_cast<uint4*>(row + pq * 16) = w4;
+            *reinterpret_cast<uint4*>(row + pq * 16) = make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
           }
         }
         fence_proxy_async_smem();  // these generic-proxy writes feed the MMA (async proxy)
@@ -987,12 +993,17 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
 #pragma unroll
           for (int j = 0; j < C::NCOL / 8; ++j) {
             float f[8];
-            const float* bsrc = C::BIAS_SMEM ? sBias : a.bias_v;  // warp-uniform index either way
-            const float4 b0 = *reinterpret_cast<const float4*>(bsrc + cu.n0 + j * 8);
-            const float4 b1 = *reinterpret_cast<const float4*>(bsrc + cu.n0 + j * 8 + 4);
-            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+            if constexpr (C::BIAS_IN_K) {  // the MMA added the bias (its K slots)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + bb[e];
+              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]);
+            } else {
+              const float* bsrc = C::BIAS_SMEM ? sBias : a.bias_v;  // warp-uniform index either way
+              const float4 b0 = *reinterpret_cast<const float4*>(bsrc + cu.n0 + j * 8);
+              const float4 b1 = *reinterpret_cast<const float4*>(bsrc + cu.n0 + j * 8 + 4);
+              const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(v[j * 8 + e]) + bb[e];
+            }
             if (res != nullptr) {
               const __half2* h = reinterpret_cast<const __half2*>(&cu.rr[j]);
 #pragma unroll
@@ -1092,6 +1103,7 @@ const std::vector<Variant>& variants() {
   static const std::vector<Variant> v = {
       // block 32
       make_variant<3, 32, 16, 2>(32),
+      make_variant<32, 32, 8, 2, 2, 1>(64),    // CTA pairs (M=256, N=64), pair windows over blocks
       make_variant<32, 64, 8, 2, 2>(64),       // pair windows over blocks
       make_variant<32, 64, 8, 2>(64),
       make_variant<64, 32, 8, 1, 1, 1>(64),    // CTA pairs (M=256, N=64), row windows over blocks
@@ -1191,7 +1203,8 @@ int out_channel_of_column(int n, int g) {
 // Weight image for the tcgen05 B operand: per C_out slice, per K-block (tap-major,
 // then channel chunk), NCTA rows of ROWB bytes, K-major, with the 128B/64B swizzle
 // applied exactly as the MMA reads it from a 1024-byte-aligned shared buffer.
-void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w, uint16_t* out) {
+void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w, const float* bias,
+                        uint16_t* out) {
   const Variant* v = picked(cin, cout, t, s, mode);
   if (!v) return;
   if (v->win == 2 && cin == 32) {
@@ -1234,9 +1247,15 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* 
         for (int k = 0; k < ch; ++k) {
           float val = 0.f;
           if (manual) {
-            if (k < 9 * cin) {
-              const int tap = k / cin, ci = k % cin;
-              val = w[((size_t)tap * cin + ci) * cout + co];
+            // K slot k: ky = k / krun, element t = k % krun = kx * cin + c of that ky's run;
+            // slots 3*krun and 3*krun + 1 carry the bias as fp16 high and low parts
+            const int krun = ((3 * cin + 1) / 2) * 2;
+            if (k < 3 * krun) {
+              const int ky = k / krun, tt = k % krun;
+              if (tt < 3 * cin) val = w[((size_t)(ky * 3 + tt / cin) * cin + tt % cin) * cout + co];
+            } else if (3 * krun + 2 <= ch && k < 3 * krun + 2) {
+              const float hi = __half2float(__float2half_rn(bias[co]));
+              val = k == 3 * krun ? hi : bias[co] - hi;
             }
           } else {
             const int tap = kb / nch, ci = (kb % nch) * ch + k;

@@ -546,7 +546,7 @@ int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias
   if (e->dtype == SB_F16) {
     const size_t bytes = conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer]);
     std::vector<uint16_t> img(bytes / 2);
-    conv_tc_build_wimg(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer], w, img.data());
+    conv_tc_build_wimg(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer], w, bias, img.data());
     SB_CUDA(cudaMemcpy(e->wdev[layer], img.data(), bytes, cudaMemcpyHostToDevice));
   } else {
     SB_CUDA(cudaMemcpy(e->wdev[layer], w, (size_t)9 * L.cin * L.cout * 4, cudaMemcpyHostToDevice));

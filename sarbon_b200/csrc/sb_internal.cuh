@@ -143,7 +143,7 @@ int conv_tc_pick_mode(int cin, int cout, int t, int s);
 int conv_tc_nsplit(int cin, int cout, int t, int s, int mode);   // CTA splits of cout
 size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode);  // all splits
 void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w /*[3][3][cin][cout]*/,
-                        uint16_t* out /* fp16 bits */);
+                        const float* bias /*[cout]*/, uint16_t* out /* fp16 bits */);
 cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s,
                               int mode);
 // the destination cache's map for the variants whose epilogue stages its output in shared
