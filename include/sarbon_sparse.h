@@ -128,6 +128,13 @@ SB_API int sb_step_u8_resized(sb_engine* e, const uint8_t* frames_dev, int cam_h
 SB_API int sb_step_profiled(sb_engine* e, const void* frames_dev, void* stream, float* kernel_ms, int capacity,
                             int* n_kernels);
 
+/* sb_step with CUDA events only at its phase boundaries: phase_ms[0] gate, [1] list
+ * kernel, [2] dense image copy, [3] the whole conv sequence (all layers, launched back to
+ * back with programmatic dependent launch as in sb_step, so each layer's start-up overlaps
+ * the previous layer's tail), [4] finalize.  Synchronises `stream`.  Measurement aid with
+ * no counterpart in the reference. */
+SB_API int sb_step_phases(sb_engine* e, const void* frames_dev, void* stream, float phase_ms[5]);
+
 /* Device address of two int64 {mode, count} the last step's finalize kernel wrote;
  * lets a caller copy each step's result to the host asynchronously.  No counterpart
  * in the reference (its step returns them after a host sync, fused_engine.py:228-240). */

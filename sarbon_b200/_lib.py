@@ -58,6 +58,7 @@ PROTOTYPES = {
                                 C.POINTER(_I), C.POINTER(_I64)]),
     "sb_query": (_I, [_P, _P, C.POINTER(_I), C.POINTER(_I64)]),
     "sb_step_profiled": (_I, [_P, _P, _P, C.POINTER(C.c_float), _I, C.POINTER(_I)]),
+    "sb_step_phases": (_I, [_P, _P, _P, C.POINTER(C.c_float)]),
     "sb_result_ptr": (_I, [_P, C.POINTER(_P)]),
     "sb_set_extra": (_I, [_P, _P, _P]),
     "sb_set_fallback": (_I, [_P, _I64, _P]),

@@ -110,8 +110,10 @@ struct sb_engine {
   uint8_t* cmasks = nullptr;  // [nd][N][Hb][Wb] block masks from the cells
   void* prep = nullptr;       // [N][H][W][3] fp16 frames resized from the camera size (first use)
   std::vector<void*> allocs;
-  // optional per-launch timing (sb_step_profiled)
+  // optional timing: an event after every launch (sb_step_profiled) or only at the phase
+  // boundaries gate | lists | copy | conv sequence | finalize (sb_step_phases)
   bool profiling = false;
+  bool phases = false;
   std::vector<cudaEvent_t> events;
   int n_events = 0;
 };
@@ -223,8 +225,9 @@ int launch_convs(sb_engine* e, cudaStream_t s, int first = 0, int last = -1) {
     if (err != cudaSuccess)
       return fail(SB_ECUDA, "conv launch (layer " + std::to_string(i) + "): " + cudaGetErrorString(err));
     e->last_launches += 1;
-    mark(e, s);
+    if (!e->phases) mark(e, s);
   }
+  if (e->phases) mark(e, s);  // the conv sequence as one interval: PDL stays on between layers
   return SB_OK;
 }
 
@@ -619,6 +622,23 @@ int sb_step_profiled(sb_engine* e, const void* frames_dev, void* stream, float* 
     SB_CUDA(cudaEventElapsedTime(&ms, e->events[i], e->events[i + 1]));
     kernel_ms[i] = ms;
   }
+  return SB_OK;
+}
+
+int sb_step_phases(sb_engine* e, const void* frames_dev, void* stream, float phase_ms[5]) {
+  if (!e || !phase_ms) return fail(SB_EINVAL, "null argument");
+  e->profiling = true;
+  e->phases = true;
+  e->n_events = 0;
+  int mode;
+  int64_t count;
+  const int rc = step_impl(e, frames_dev, e->dtype == SB_F16 ? 0 : 1, nullptr, nullptr, (cudaStream_t)stream,
+                           &mode, &count);
+  e->profiling = false;
+  e->phases = false;
+  if (rc) return rc;
+  if (e->n_events != 6) return fail(SB_ECUDA, "phase timing: unexpected event count");
+  for (int i = 0; i < 5; ++i) SB_CUDA(cudaEventElapsedTime(&phase_ms[i], e->events[i], e->events[i + 1]));
   return SB_OK;
 }
 

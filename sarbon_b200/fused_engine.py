@@ -359,6 +359,18 @@ class FusedSparseEngine:
         last = first if last is None else last
         check(lib().sb_dense_layers(self._h.ptr, int(first), int(last), self._stream()), "sb_dense_layers")
 
+    @torch.no_grad()
+    def step_phases(self, frames):
+        """One step on ``frames`` (used in place) with CUDA events only between its phases;
+        returns (mode, k, {"gate", "lists", "copy", "conv", "finalize": ms}).  The conv
+        phase is the whole layer sequence launched as in ``step`` (layers overlap their
+        start-up with the previous layer's tail)."""
+        ms = (C.c_float * 5)()
+        check(lib().sb_step_phases(self._h.ptr, C.c_void_p(frames.data_ptr()), self._stream(), ms),
+              "sb_step_phases")
+        mode, k = self.query()
+        return mode, k, dict(zip(("gate", "lists", "copy", "conv", "finalize"), list(ms)))
+
     def result_view(self):
         """int64 [2] device tensor {mode, count} written by every step's last kernel."""
         p = C.c_void_p()

@@ -276,3 +276,27 @@ def test_calibrate_restores_caches_and_sets_crossover():
     # the engine still steps normally with the calibrated crossover
     mode, k = eng.step(scenes.normalise(src.next()))
     assert mode in ("skip", "sparse", "dense")
+
+
+def test_step_phases_times_the_same_step():
+    """step_phases (events only between the step's phases) computes exactly what step does and
+    returns a positive time for every phase."""
+    from sarbon_b200 import FusedSparseEngine, LocalBackbone, scenes
+    n, h, w = 2, 256, 384
+    torch.manual_seed(12)
+    net = LocalBackbone().cuda().eval()
+    tau = 8 / float(scenes.STD.mean())
+    a = FusedSparseEngine(net, n, h, w, dtype=torch.float16, tau=tau)
+    b = FusedSparseEngine(net, n, h, w, dtype=torch.float16, tau=tau)
+    src = scenes.Streams(n, h, w, seed=13, n_rects=2, device="cuda")
+    f = scenes.normalise(src.next())
+    a.reset(f)
+    b.reset(f)
+    for _ in range(3):
+        f = scenes.normalise(src.next())
+        ma = a.step(f.clone())
+        mode, k, ph = b.step_phases(f.clone())
+        assert ma == (mode, k)
+        assert set(ph) == {"gate", "lists", "copy", "conv", "finalize"} and all(v > 0 for v in ph.values())
+        for name in a.cache:
+            assert torch.equal(a.cache[name], b.cache[name]), name
