@@ -106,6 +106,15 @@ SB_API int sb_dense(sb_engine* e, const void* frames_dev, void* stream);
  * hysteresis dense step). */
 SB_API int sb_step(sb_engine* e, const void* frames_dev, void* stream, int* mode_out, int64_t* count_out);
 
+/* Step graphs (on by default): sb_step, sb_step_u8 and sb_step_u8_resized capture their
+ * launch sequence into a CUDA graph the first time they see an input (frames pointer,
+ * input kind, camera size, normalisation) and replay it afterwards, so a step costs the
+ * host one graph launch instead of ~15 kernel launches (the reference replays CUDA graphs
+ * too, fused_engine.py:85-88,196-199).  Up to 64 inputs are kept (least recently used
+ * dropped); sb_set_tau, sb_set_cell_gating and sb_upload_weights drop them all, since they
+ * change kernel arguments.  on = 0 launches every kernel directly. */
+SB_API int sb_set_step_graphs(sb_engine* e, int on);
+
 /* The same step on uint8 BGR frames [N][H][W][3] with the caller's normalisation
  * fused into the gate (sarbon/inference/video.py:74-99, `_prep`: BGR->RGB,
  * (x - mean[c]) / std[c] in fp32, rounded to fp16).  fp16 engines only. */

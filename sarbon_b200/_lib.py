@@ -67,6 +67,7 @@ PROTOTYPES = {
     "sb_set_cell_gating": (_I, [_P, _I, C.POINTER(_I), _I]),
     "sb_run_sparse_forced": (_I, [_P, _P, _I64, _P]),
     "sb_dense_layers": (_I, [_P, _I, _I, _P]),
+    "sb_set_step_graphs": (_I, [_P, _I]),
     "sb_debug_withhold_lookback": (_I, [_P, _I, _I]),
     "sb_cache_ptr": (_I, [_P, _I, C.POINTER(_P), C.POINTER(_I64)]),
     "sb_layer_variant": (_I, [_P, _I, C.POINTER(_I)]),

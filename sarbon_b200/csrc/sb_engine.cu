@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -110,6 +111,22 @@ struct sb_engine {
   uint8_t* cmasks = nullptr;  // [nd][N][Hb][Wb] block masks from the cells
   void* prep = nullptr;       // [N][H][W][3] fp16 frames resized from the camera size (first use)
   std::vector<void*> allocs;
+  // CUDA graphs of the step's launch sequence, one per input (frames pointer, input kind,
+  // camera size, normalisation): a step is then one graph launch instead of ~15 kernel
+  // launches from the host.  Dropped when a host-side value baked into kernel arguments
+  // changes (threshold, gating mode, weights).
+  struct StepGraph {
+    const void* frames;
+    int kind, cam_h, cam_w;
+    float mean[3], stdv[3];
+    cudaGraphExec_t exec;
+    int launches;
+    uint64_t used;
+  };
+  bool graphs_on = true;
+  std::vector<StepGraph> graphs;
+  cudaStream_t cap_stream = nullptr;
+  uint64_t graph_clock = 0;
   // optional timing: an event after every launch (sb_step_profiled) or only at the phase
   // boundaries gate | lists | copy | conv sequence | finalize (sb_step_phases)
   bool profiling = false;
@@ -130,6 +147,70 @@ void mark(sb_engine* e, cudaStream_t s) {
     e->events.push_back(ev);
   }
   cudaEventRecord(e->events[e->n_events++], s);
+}
+
+void drop_graphs(sb_engine* e) {
+  for (auto& g : e->graphs) cudaGraphExecDestroy(g.exec);
+  e->graphs.clear();
+}
+
+constexpr size_t kMaxStepGraphs = 64;
+
+// Runs a step's launch sequence `launch` on `s`: through the step graph of this input
+// (captured on first use on the engine's capture stream and instantiated), or directly when
+// graphs are off or a step is being timed launch by launch.
+int run_step(sb_engine* e, const void* frames, int kind, int cam_h, int cam_w, const float* mean, const float* stdv,
+             const std::function<int(cudaStream_t)>& launch, cudaStream_t s) {
+  if (!e->graphs_on || e->profiling) return launch(s);
+  float mv[3], sv[3];
+  for (int c = 0; c < 3; ++c) {
+    mv[c] = mean ? mean[c] : 0.f;
+    sv[c] = stdv ? stdv[c] : 1.f;
+  }
+  sb_engine::StepGraph* hit = nullptr;
+  for (auto& g : e->graphs)
+    if (g.frames == frames && g.kind == kind && g.cam_h == cam_h && g.cam_w == cam_w &&
+        std::memcmp(g.mean, mv, sizeof mv) == 0 && std::memcmp(g.stdv, sv, sizeof sv) == 0)
+      hit = &g;
+  if (!hit) {
+    if (!e->cap_stream) SB_CUDA(cudaStreamCreateWithFlags(&e->cap_stream, cudaStreamNonBlocking));
+    SB_CUDA(cudaStreamBeginCapture(e->cap_stream, cudaStreamCaptureModeRelaxed));
+    const int rc = launch(e->cap_stream);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(e->cap_stream, &graph);
+    if (rc) {
+      if (graph) cudaGraphDestroy(graph);
+      return rc;
+    }
+    if (ce != cudaSuccess || !graph)
+      return fail(SB_ECUDA, std::string("step graph capture: ") + cudaGetErrorString(ce));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return fail(SB_ECUDA, std::string("step graph instantiate: ") + cudaGetErrorString(ie));
+    if (e->graphs.size() >= kMaxStepGraphs) {  // the least recently used input goes
+      size_t lru = 0;
+      for (size_t i = 1; i < e->graphs.size(); ++i)
+        if (e->graphs[i].used < e->graphs[lru].used) lru = i;
+      cudaGraphExecDestroy(e->graphs[lru].exec);
+      e->graphs.erase(e->graphs.begin() + (long)lru);
+    }
+    sb_engine::StepGraph g{};
+    g.frames = frames;
+    g.kind = kind;
+    g.cam_h = cam_h;
+    g.cam_w = cam_w;
+    std::memcpy(g.mean, mv, sizeof mv);
+    std::memcpy(g.stdv, sv, sizeof sv);
+    g.exec = exec;
+    g.launches = e->last_launches;
+    e->graphs.push_back(g);
+    hit = &e->graphs.back();
+  }
+  hit->used = ++e->graph_clock;
+  SB_CUDA(cudaGraphLaunch(hit->exec, s));
+  e->last_launches = hit->launches;
+  return SB_OK;
 }
 
 int alloc_dev(sb_engine* e, void** p, size_t bytes) {
@@ -240,11 +321,9 @@ int check_frames(sb_engine* e, const void* p) {
   return SB_OK;
 }
 
-int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, const float* stdv,
-              cudaStream_t s, int* mode_out, int64_t* count_out) {
-  int rc = check_frames(e, frames);
-  if (rc) return rc;
-  SB_CUDA(cudaSetDevice(e->dev));
+// Every launch of one step on `s` (no host sync).
+int launch_step(sb_engine* e, const void* frames, int kind, const float* mean, const float* stdv, cudaStream_t s) {
+  int rc;
   e->last_launches = 0;
   GateArgs g{};
   g.frames = frames;
@@ -344,6 +423,11 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
   SB_CUDA(launch_finalize(e->st, e->refresh, e->host_out_dev, s));
   mark(e, s);
   e->last_launches += 1;
+  return SB_OK;
+}
+
+// Reads the step's {mode, count} after a stream sync when the caller asked for them.
+int finish_step(sb_engine* e, cudaStream_t s, int* mode_out, int64_t* count_out) {
   if (mode_out || count_out) {
     SB_CUDA(cudaStreamSynchronize(s));
     volatile int32_t* ho = e->host_out;
@@ -355,6 +439,17 @@ int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, con
     if (ho[2]) return fail(SB_ECUDA, "device error flags " + std::to_string(ho[2]));
   }
   return SB_OK;
+}
+
+int step_impl(sb_engine* e, const void* frames, int kind, const float* mean, const float* stdv,
+              cudaStream_t s, int* mode_out, int64_t* count_out) {
+  int rc = check_frames(e, frames);
+  if (rc) return rc;
+  SB_CUDA(cudaSetDevice(e->dev));
+  rc = run_step(e, frames, kind, e->h, e->w, mean, stdv,
+                [&](cudaStream_t st) { return launch_step(e, frames, kind, mean, stdv, st); }, s);
+  if (rc) return rc;
+  return finish_step(e, s, mode_out, count_out);
 }
 
 int dense_impl(sb_engine* e, const void* frames, int reset, cudaStream_t s) {
@@ -544,6 +639,7 @@ int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias
   if (layer < 0 || layer >= e->n_layers) return fail(SB_EINVAL, "layer out of range");
   const sb_layer_desc& L = e->layers[layer];
   SB_CUDA(cudaSetDevice(e->dev));
+  drop_graphs(e);  // the conv kernels take the bias by value
   SB_CUDA(cudaMemcpy(e->bias[layer], bias, (size_t)L.cout * 4, cudaMemcpyHostToDevice));
   for (int c = 0; c < L.cout && c < 128; ++c) e->bias_h[layer][c] = bias[c];
   if (e->dtype == SB_F16) {
@@ -597,11 +693,15 @@ int sb_step_u8_resized(sb_engine* e, const uint8_t* frames_dev, int cam_h, int c
     if (rc) return rc;
   }
   cudaStream_t s = (cudaStream_t)stream;
-  SB_CUDA(launch_prep_resize(frames_dev, e->n, cam_h, cam_w, static_cast<__half*>(e->prep), e->h, e->w, mean, std_,
-                             e->n_sms, s));
-  const int rc = step_impl(e, e->prep, 0, nullptr, nullptr, s, mode_out, count_out);
-  e->last_launches += 1;
-  return rc;
+  int rc = run_step(e, frames_dev, 3, cam_h, cam_w, mean, std_, [&](cudaStream_t st) {
+    SB_CUDA(launch_prep_resize(frames_dev, e->n, cam_h, cam_w, static_cast<__half*>(e->prep), e->h, e->w, mean,
+                               std_, e->n_sms, st));
+    const int r = launch_step(e, e->prep, 0, nullptr, nullptr, st);
+    e->last_launches += 1;
+    return r;
+  }, s);
+  if (rc) return rc;
+  return finish_step(e, s, mode_out, count_out);
 }
 
 int sb_step_profiled(sb_engine* e, const void* frames_dev, void* stream, float* kernel_ms, int capacity,
@@ -673,12 +773,14 @@ int sb_set_fallback(sb_engine* e, int64_t fallback, void* stream) {
 
 int sb_set_tau(sb_engine* e, double tau) {
   if (!e) return fail(SB_EINVAL, "null engine");
+  drop_graphs(e);  // the threshold is a kernel argument of the captured steps
   set_threshold(e, tau);
   return SB_OK;
 }
 
 int sb_set_cell_gating(sb_engine* e, int cell, const int* cell_radii, int n_radii) {
   if (!e) return fail(SB_EINVAL, "null engine");
+  drop_graphs(e);  // the gating mode decides which kernels a step launches
   if (cell == 0) {
     e->cell = 0;
     return SB_OK;
@@ -759,6 +861,13 @@ int sb_dense_layers(sb_engine* e, int first, int last, void* stream) {
   SB_CUDA(launch_set_mode(e->st, SB_MODE_DENSE, 0, 0, s));
   e->last_launches = 1;
   return launch_convs(e, s, first, last);
+}
+
+int sb_set_step_graphs(sb_engine* e, int on) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (!on) drop_graphs(e);
+  e->graphs_on = on != 0;
+  return SB_OK;
 }
 
 int sb_debug_withhold_lookback(sb_engine* e, int withhold_chunk, int spin_limit) {
@@ -849,6 +958,8 @@ int sb_destroy(sb_engine* e) {
   if (!e) return SB_OK;
   cudaSetDevice(e->dev);
   cudaDeviceSynchronize();
+  drop_graphs(e);
+  if (e->cap_stream) cudaStreamDestroy(e->cap_stream);
   for (void* p : e->allocs) cudaFree(p);
   for (cudaEvent_t ev : e->events) cudaEventDestroy(ev);
   if (e->host_out) cudaFreeHost(e->host_out);

@@ -200,6 +200,11 @@ class FusedSparseEngine:
         self._fallback = int(v)
         check(lib().sb_set_fallback(self._h.ptr, int(v), self._stream()), "sb_set_fallback")
 
+    def set_step_graphs(self, on):
+        """Replay each step's launch sequence as a captured CUDA graph (default) or launch
+        every kernel from the host (``on=False``)."""
+        check(lib().sb_set_step_graphs(self._h.ptr, int(bool(on))), "sb_set_step_graphs")
+
     def set_tau(self, tau):
         """Change threshold for the steps launched after this call (mean |diff| per block;
         an extension: the reference fixes `tau` at construction)."""
