@@ -304,23 +304,13 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
 
   // Programmatic dependent launch: this kernel may start while the previous kernel of the
-  // stream (the previous layer, or the frame copy) still runs.  That kernel began its item
-  // loop only after the kernel before it had completed, and it writes nothing but its
-  // output cache and error flags; so the step's device state and unit lists (written by
-  // the gate / list / mode kernels, two or more launches back) and this CTA's weight slice
-  // are read before griddepcontrol.wait.  Only the threads that read caches written by
+  // stream (the previous layer, or the frame copy) still runs.  That kernel triggered this
+  // launch only after its own griddepcontrol.wait had returned (the kernel before it had
+  // completed), and it writes nothing but its output cache and error flags; so the step's
+  // device state and unit lists (written by the gate / list / mode kernels, two or more
+  // launches back) and this CTA's weight slice are read before griddepcontrol.wait.  Only the threads that read caches written by
   // earlier layers wait: the producer before its first input copy, the epilogue before its
   // first residual read.
-  if (warp == C::PROD_WARP && lane == 0) {
-    const int wsplit = PAIR ? (int)rank : (int)blockIdx.x % (a.cout / NCTA);
-    const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)wsplit * C::W_BYTES;
-    mbar_arrive_expect_tx(wfull, C::W_BYTES);
-    for (int off = 0; off < C::W_BYTES; off += 32768) {
-      const int len = C::W_BYTES - off < 32768 ? C::W_BYTES - off : 32768;
-      bulk_load(sW + off, wsrc + off, len, wfull);
-    }
-  }
-
   // work of this launch, decided on the device (no host sync)
   const int mode = a.st->mode_cur;
   const int listed = (WIN && a.rkind >= 0) ? a.st->rcounts[a.rkind][a.d_idx] : a.st->counts[a.d_idx];
@@ -346,6 +336,17 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
     if (PAIR) return Item{(int)rank, 2 * (pair + it * npairs) + (int)rank};
     return item_at(it, nsplit);
   };
+  // the CTA's weight slice, copied only when it has items this launch (both CTAs of a pair
+  // have the same item count)
+  if (my_items > 0 && warp == C::PROD_WARP && lane == 0) {
+    const int wsplit = PAIR ? (int)rank : (int)blockIdx.x % (a.cout / NCTA);
+    const uint8_t* wsrc = static_cast<const uint8_t*>(a.wimg) + (size_t)wsplit * C::W_BYTES;
+    mbar_arrive_expect_tx(wfull, C::W_BYTES);
+    for (int off = 0; off < C::W_BYTES; off += 32768) {
+      const int len = C::W_BYTES - off < 32768 ? C::W_BYTES - off : 32768;
+      bulk_load(sW + off, wsrc + off, len, wfull);
+    }
+  }
 
   if (my_items > 0) {
     if (warp == C::PROD_WARP || (C::NPROD == 2 && warp == C::PROD_WARP2)) {
@@ -485,6 +486,10 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       Coords ca, cb;
       fetch_lane(0, ca);
       grid_dep_wait();  // the input cache (previous layer / frame copy) is complete
+      // The previous kernel has completed, so the next layer may start its prologue (barriers,
+      // TMEM, weight copy) on SMs as they free up; it waits for this kernel before touching
+      // any cache, and reads only state written two or more launches back before that.
+      grid_dep_launch();
       for (int base = 0; base < n_loc; base += 64) {
         if (base + 32 < n_loc) fetch_lane(base + 32, cb);
         if (!run_batch(base, ca) || base + 32 >= n_loc) break;
@@ -1060,8 +1065,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       __syncwarp();
     }
   }
-  // the weight copy has landed before the CTA may exit (also when it had no items)
-  if (warp == C::PROD_WARP) {
+  // the weight copy (issued when the CTA had items) has landed before the CTA may exit
+  if (warp == C::PROD_WARP && my_items > 0) {
     volatile int never = 0;
     warp_wait(wfull, 0, &never);
   }
