@@ -87,6 +87,25 @@ SB_API int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, i
               int block, int dtype, double tau, int refresh, int dense_check_every,
               sb_engine** out);
 
+/* sb_create with creation flags.  SB_CREATE_BLOCK_UNITS: every layer runs over single
+ * blocks (no multi-block window regions), which M0 mode needs; slower for the 4x4-pixel
+ * layers.  sb_create(...) is sb_create_ex(..., 0, out). */
+#define SB_CREATE_BLOCK_UNITS 1
+SB_API int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width,
+                        int block, int dtype, double tau, int refresh, int dense_check_every, int flags,
+                        sb_engine** out);
+
+/* M0 semantics for the steps launched after this call (the reference's first engine,
+ * BlockSparseEngine.step / update, block_sparse.py:196-295): every step copies the whole
+ * frame into the image cache (so the gate compares a frame with the previous one), there is
+ * no dense fallback, and with capacity > 0 every layer recomputes exactly `capacity` entries
+ * of its dilation's block list: the first `capacity` active blocks, padded with block 0
+ * (nonzero_static(size=capacity, fill_value=0), :268-271); more active blocks than that are
+ * left as they were (the caller sees count > capacity, the reference's overflow flag).
+ * capacity = 0 recomputes the active blocks (update, :211-218).  on = 0 returns to the fused
+ * engine's behaviour.  Needs an engine created with SB_CREATE_BLOCK_UNITS (or fp32). */
+SB_API int sb_set_m0(sb_engine* e, int on, int64_t capacity);
+
 /* Layer weights from host memory: w float32 [3][3][cin][cout] (the Triton kernel's
  * w_tile layout, fused_engine.py:114) and bias float32 [cout] (:116). */
 SB_API int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias);

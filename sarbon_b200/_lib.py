@@ -14,6 +14,7 @@ SB_OK, SB_EINVAL, SB_EOVERFLOW, SB_ETIMEOUT, SB_ECUDA, SB_ENOMEM = range(6)
 SB_F16, SB_F32 = 0, 1
 SB_MODE_SKIP, SB_MODE_SPARSE, SB_MODE_DENSE = 0, 1, 2
 MODE_NAMES = ("skip", "sparse", "dense")
+SB_CREATE_BLOCK_UNITS = 1
 SB_MAX_LAYERS = 32
 SB_MAX_DILATIONS = 4
 
@@ -48,6 +49,8 @@ _I64 = C.c_int64
 # name -> (restype, argtypes); every symbol declared in include/sarbon_sparse.h
 PROTOTYPES = {
     "sb_create": (_I, [C.POINTER(LayerDesc), _I, _I, _I, _I, _I, _I, C.c_double, _I, _I, C.POINTER(_P)]),
+    "sb_create_ex": (_I, [C.POINTER(LayerDesc), _I, _I, _I, _I, _I, _I, C.c_double, _I, _I, _I, C.POINTER(_P)]),
+    "sb_set_m0": (_I, [_P, _I, _I64]),
     "sb_upload_weights": (_I, [_P, _I, C.POINTER(C.c_float), C.POINTER(C.c_float)]),
     "sb_reset": (_I, [_P, _P, _P]),
     "sb_dense": (_I, [_P, _P, _P]),

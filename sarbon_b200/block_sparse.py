@@ -4,17 +4,25 @@ sarbon/sparse/block_sparse.py:122-326) on the B200 engine.
 M0 runs one camera: CHW frames, `full()` for the dense initialisation, `update()` with a
 caller-given change mask, the sync-free `step(frame, capacity, tau)` returning an overflow
 flag, and the helpers `changed_blocks` / `active_blocks` / `dilation`.  Here every one of
-those calls runs the B200 engine (`FusedSparseEngine`, one stream): the halo gather is the
-conv kernels' TMA window reads, the scatter their epilogue stores into the caches, and the
-bounded-capacity contract the engine's device-side dispatch.
+those calls runs the B200 engine (`FusedSparseEngine`, one stream) in its M0 mode
+(`set_m0`): the whole frame enters the image cache every step, so the gate compares a
+frame with the previous one (block_sparse.py:265,272-274); `step` recomputes exactly the
+first `capacity` active blocks of every dilation, padded with block 0 like
+`nonzero_static(size=capacity, fill_value=0)` (:268-271), leaves any further active block
+as it was and raises the overflow flag (:271, count > capacity); `update` recomputes the
+given blocks, dilated (:206-218).  The engine is created with single-block units so that
+"the first `capacity` blocks" is exact for every layer.  The halo gather is the conv
+kernels' TMA reads, the scatter their epilogue stores into the caches.
 
 Differences from the reference, on purpose:
   * caches are the engine's NHWC caches without a border; `cache[name]` and the returned
     outputs are CHW *views* of them (M0 keeps CHW caches with a one-pixel zero border,
-    block_sparse.py:22,135-140);
-  * when more blocks are active than `capacity`, M0 recomputes only the first `capacity`
-    of them and flags the overflow so that the caller refreshes; here the step turns dense
-    (the engine's fallback) and the outputs stay exact -- the flag is raised all the same.
+    block_sparse.py:22,135-140), and a conv + residual add is one fused layer (M0 also
+    caches the conv output before the add);
+  * the change test is the engine's: the exact per-block sum of |diff| against
+    float32(tau * block^2 * 3), where M0 compares the fp32 mean (avg_pool of the channel
+    mean, :323-326) with tau -- the same rule, which can differ only for a block whose sum
+    lies within fp32 rounding of the threshold.
 """
 from __future__ import annotations
 
@@ -57,11 +65,23 @@ class BlockSparseEngine:
         key = (h, w, frame.dtype, frame.device)
         if self._eng is None or self._key != key:
             self._eng = FusedSparseEngine(self.net, 1, h, w, block=self.block, dtype=frame.dtype, tau=0.0,
-                                          refresh=0, dense_check_every=1, device=frame.device)
+                                          refresh=0, dense_check_every=1, device=frame.device, block_units=True)
             self._key = key
+            self._tau, self._m0 = 0.0, None
             self._buf = torch.empty(1, h, w, 3, dtype=frame.dtype, device=frame.device)
             self.cache = {name: v[0].permute(2, 0, 1) for name, v in self._eng.cache.items()}
         return self._eng
+
+    def _configure(self, tau, capacity):
+        """Threshold and M0 capacity of the next step (set only when they change: a new
+        threshold drops the engine's captured step graphs)."""
+        eng = self._eng
+        if tau != self._tau:
+            eng.set_tau(tau)
+            self._tau = tau
+        if self._m0 != capacity:
+            eng.set_m0(True, capacity)
+            self._m0 = capacity
 
     def _interior(self, name):
         return self.cache[name]
@@ -103,23 +123,24 @@ class BlockSparseEngine:
         if self._eng is None:
             raise RuntimeError("call full() first")
         eng = self._engine(frame)
-        eng.set_tau(math.inf)                  # no block changes by its pixels ...
+        self._configure(math.inf, 0)           # no block changes by its pixels ...
         eng.set_extra(changed.reshape(1, eng.hb, eng.wb).bool())  # ... only the given ones
-        eng.fallback = eng.n_blocks            # always sparse
         eng.step_async(self._stage(frame))
         return self._outputs()
 
     @torch.no_grad()
     def step(self, frame, capacity, tau=0.0):
-        """Gate + sparse update for the next frame with no host sync.  Returns (outputs,
-        overflow): overflow is a 0-dim bool device tensor, True when more blocks were active
-        than `capacity` (the step then ran dense, so the outputs are exact)."""
+        """Gate + sparse update for the next frame with no host sync (block_sparse.py:253-295).
+        Returns (outputs, overflow): overflow is a 0-dim bool device tensor, True when more
+        blocks were active than `capacity`; only the first `capacity` of them were
+        recomputed, so the caller should schedule a dense refresh (`full`)."""
         if self._eng is None:
             raise RuntimeError("call full() first")
+        if not 1 <= int(capacity) <= self._eng.n_blocks:
+            raise ValueError(f"capacity must be in [1, {self._eng.n_blocks}]")
         eng = self._engine(frame)
-        eng.set_tau(tau)
+        self._configure(float(tau), int(capacity))
         eng.extra.zero_()
-        eng.fallback = int(capacity)
         eng.step_async(self._stage(frame))
         over = eng.result_view()[1] > int(capacity)
         return self._outputs(), over

@@ -1121,6 +1121,7 @@ const std::vector<Variant>& variants() {
       make_variant<128, 64, 4, 1, 1>(128),     // row windows, two C_out slices
       make_variant<128, 64, 4, 1, 3, 1>(128),  // CTA pairs, full windows over 2x4-block regions
       make_variant<128, 64, 4, 1, 3>(128),     // full windows, two C_out slices
+      make_variant<128, 64, 4, 1, 0, 1>(128),  // CTA pairs, per-tap boxes over blocks (block units)
       // block 64
       make_variant<3, 32, 32, 2>(32),
       make_variant<32, 64, 16, 2>(64),
@@ -1168,6 +1169,19 @@ int conv_tc_pick_mode(int cin, int cout, int t, int s) {
     if (find_variant(cin, cout, t, s, want)) return want;
   }
   return v->mode();
+}
+
+int conv_tc_block_mode(int cin, int cout, int t, int s) {
+  const bool no_pair = pairs_disabled();
+  const Variant* best = nullptr;
+  for (const auto& v : variants()) {
+    if (v.cin != cin || v.cout != cout || v.t != t || v.s != s) continue;
+    if (no_pair && v.pair) continue;
+    const bool one_block = v.win == 0 || (8 / t == 1 && (v.win != 3 || 16 / t == 1));
+    if (!one_block) continue;
+    if (!best || (v.pair && !best->pair)) best = &v;
+  }
+  return best ? best->mode() : -1;
 }
 
 namespace {

@@ -483,7 +483,14 @@ const char* sb_version(void) { return "sarbon_b200 0.1 sm_100a (tcgen05 fp16 til
 
 int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width, int block,
               int dtype, double tau, int refresh, int dense_check_every, sb_engine** out) {
+  return sb_create_ex(layers, n_layers, n_streams, height, width, block, dtype, tau, refresh, dense_check_every, 0,
+                      out);
+}
+
+int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width, int block,
+                 int dtype, double tau, int refresh, int dense_check_every, int flags, sb_engine** out) {
   if (!out || !layers) return fail(SB_EINVAL, "null argument");
+  if (flags & ~SB_CREATE_BLOCK_UNITS) return fail(SB_EINVAL, "unknown creation flags");
   *out = nullptr;
   if (n_layers < 1 || n_layers > SB_MAX_LAYERS) return fail(SB_EINVAL, "n_layers out of range");
   if (n_streams < 1 || height < 1 || width < 1) return fail(SB_EINVAL, "bad frame geometry");
@@ -577,6 +584,15 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
     e->layer_mode[i] = dtype == SB_F16 ? conv_tc_pick_mode(layers[i].cin, layers[i].cout, e->layer_t[i],
                                                            layers[i].stride)
                                        : 0;
+    if (dtype == SB_F16 && (flags & SB_CREATE_BLOCK_UNITS)) {
+      const int t = e->layer_t[i], win = e->layer_mode[i] & 7;
+      const bool one_block = win == 0 || (8 / t == 1 && (win != 3 || 16 / t == 1));
+      if (!one_block) {
+        const int m = conv_tc_block_mode(layers[i].cin, layers[i].cout, t, layers[i].stride);
+        if (m < 0) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": no block-unit tile conv"));
+        e->layer_mode[i] = m;
+      }
+    }
     const int win = e->layer_mode[i] & 7;  // bit 3: CTA pairs
     if (win == 0) continue;
     const int t = e->layer_t[i];
@@ -861,6 +877,19 @@ int sb_dense_layers(sb_engine* e, int first, int last, void* stream) {
   SB_CUDA(launch_set_mode(e->st, SB_MODE_DENSE, 0, 0, s));
   e->last_launches = 1;
   return launch_convs(e, s, first, last);
+}
+
+int sb_set_m0(sb_engine* e, int on, int64_t capacity) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (capacity < 0 || capacity > e->n_blocks) return fail(SB_EINVAL, "capacity must be in [0, n_blocks]");
+  if (on)
+    for (int i = 0; i < e->n_layers; ++i)
+      if (e->layer_rk[i] >= 0)
+        return fail(SB_EINVAL, "M0 mode needs an engine whose layers run over single blocks (SB_CREATE_BLOCK_UNITS)");
+  SB_CUDA(cudaSetDevice(e->dev));
+  const int32_t v[2] = {on ? 1 : 0, on ? (int32_t)capacity : 0};
+  SB_CUDA(cudaMemcpy(reinterpret_cast<uint8_t*>(e->st) + offsetof(State, m0_mode), v, 8, cudaMemcpyHostToDevice));
+  return SB_OK;
 }
 
 int sb_set_step_graphs(sb_engine* e, int on) {

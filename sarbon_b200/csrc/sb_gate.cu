@@ -544,7 +544,15 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
     __threadfence();
     const int64_t k = st->counts[a.n_dil - 1];
     st->count_cur = k;
-    st->mode_cur = k == 0 ? SB_MODE_SKIP : (k <= st->fallback ? SB_MODE_SPARSE : SB_MODE_DENSE);
+    if (st->m0_mode) {
+      // M0 (block_sparse.py:264-275): no dense fallback; with a capacity every layer runs
+      // exactly that many list entries (nonzero_static, size=capacity, fill_value=0)
+      st->mode_cur = st->m0_cap > 0 ? SB_MODE_SPARSE : (k == 0 ? SB_MODE_SKIP : SB_MODE_SPARSE);
+      st->force_tiles = st->m0_cap > 0 ? st->m0_cap : 0;
+    } else {
+      st->mode_cur = k == 0 ? SB_MODE_SKIP : (k <= st->fallback ? SB_MODE_SPARSE : SB_MODE_DENSE);
+      st->force_tiles = 0;
+    }
   }
 }
 
@@ -555,7 +563,9 @@ __global__ void __launch_bounds__(256) copy_kernel(CopyArgs a) {
   grid_dep_wait();
   grid_dep_launch();  // after the wait: the next kernel may start its prologue now
   const int mode = a.st->mode_cur;
-  if (a.changed == nullptr && mode != SB_MODE_DENSE) return;
+  // dense steps and M0-mode steps (the whole frame enters the image cache,
+  // block_sparse.py:272) copy every block
+  if (a.changed == nullptr && mode != SB_MODE_DENSE && !a.st->m0_mode) return;
   const int by = blockIdx.x, cam = blockIdx.y, B = a.block;
   __shared__ __half s_lut[768];
   if (a.u8) {

@@ -43,6 +43,11 @@ struct State {
   // words (0 = none); look-back waits give up after lb_spin_limit polls (0 = SB_SPIN_LIMIT)
   int32_t lb_withhold;
   uint32_t lb_spin_limit;
+  // M0 mode (sb_set_m0, block_sparse.py:253-295): every step copies the whole frame into the
+  // image cache; m0_cap > 0 runs every layer over exactly m0_cap list entries (padding
+  // entries recompute block 0); m0_cap = 0 runs the listed blocks (and skips when none)
+  int32_t m0_mode;
+  int32_t m0_cap;
 };
 
 struct GateArgs {
@@ -140,6 +145,9 @@ bool conv_tc_supported(int cin, int cout, int t, int s);  // some mode exists fo
 // 1 per-ky row windows over (8/t)x1-block regions, 3 full windows over (8/t)x(16/t)
 // regions; plus 8 when 2-CTA clusters run M=256 cta_group::2 MMAs
 int conv_tc_pick_mode(int cin, int cout, int t, int s);
+// a mode whose units are single blocks (window mode 0, or a window mode whose region is one
+// block), CTA pairs preferred; -1 when the shape has none
+int conv_tc_block_mode(int cin, int cout, int t, int s);
 int conv_tc_nsplit(int cin, int cout, int t, int s, int mode);   // CTA splits of cout
 size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode);  // all splits
 void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w /*[3][3][cin][cout]*/,

@@ -13,6 +13,8 @@ unchanged:
   (``sarbon/inference/video.py:139-147``) as one kernel writing ``extra``
 * added: ``set_cell_gating(cell)``, cell-level gating (``sarbon/sparse/gating.py:42-43``)
   inside the step
+* added: ``block_units=True`` and ``set_m0(on, capacity)``, the M0 engine's semantics
+  (``sarbon/sparse/block_sparse.py:196-295``) on this engine
 * attributes ``n, h, w, block, hb, wb, n_blocks, dtype, tau, refresh, layers, ds,
   outputs, cache, frames, changed, extra, masks, buckets, fallback,
   dense_check_every, dense_graph, stats``.
@@ -131,7 +133,7 @@ class FusedSparseEngine:
     MODES = _lib.MODE_NAMES
 
     def __init__(self, net, n_cams, height, width, block=32, dtype=torch.float16, tau=0.0, refresh=0,
-                 dense_check_every=4, device="cuda"):
+                 dense_check_every=4, device="cuda", block_units=False):
         assert height % block == 0 and width % block == 0
         if dtype not in (torch.float16, torch.float32):
             raise ValueError("dtype must be torch.float16 or torch.float32")
@@ -159,9 +161,10 @@ class FusedSparseEngine:
                                       l.w_tile.shape[3], l.stride, l.out_stride, l.radius, int(l.act))
         handle = C.c_void_p()
         with torch.cuda.device(self.dev):
-            check(L.sb_create(descs, len(self.layers), n_cams, height, width, block,
-                              _lib.SB_F16 if dtype == torch.float16 else _lib.SB_F32, float(tau),
-                              int(refresh), int(dense_check_every), C.byref(handle)), "sb_create")
+            check(L.sb_create_ex(descs, len(self.layers), n_cams, height, width, block,
+                                 _lib.SB_F16 if dtype == torch.float16 else _lib.SB_F32, float(tau),
+                                 int(refresh), int(dense_check_every),
+                                 _lib.SB_CREATE_BLOCK_UNITS if block_units else 0, C.byref(handle)), "sb_create_ex")
         self._h = _Handle(handle.value)
         for i, l in enumerate(self.layers):
             w = np.ascontiguousarray(l.w_tile.numpy(), np.float32)
@@ -199,6 +202,13 @@ class FusedSparseEngine:
     def fallback(self, v):
         self._fallback = int(v)
         check(lib().sb_set_fallback(self._h.ptr, int(v), self._stream()), "sb_set_fallback")
+
+    def set_m0(self, on, capacity=0):
+        """M0 semantics for the next steps (block_sparse.py:196-295): the whole frame enters
+        the image cache every step, no dense fallback, and with ``capacity`` > 0 every layer
+        recomputes exactly the first ``capacity`` entries of its block list (padded with
+        block 0).  Needs ``block_units=True`` (or an fp32 engine)."""
+        check(lib().sb_set_m0(self._h.ptr, int(bool(on)), int(capacity)), "sb_set_m0")
 
     def set_step_graphs(self, on):
         """Replay each step's launch sequence as a captured CUDA graph (default) or launch

@@ -55,7 +55,11 @@ def test_chained_steps_are_lossless_fp32(block):
     assert worst < 1e-5, worst
 
 
-def test_overflow_flag_and_exact_outputs_fp16():
+def test_overflow_flag_and_capacity_fp16():
+    """More active blocks than the capacity: the flag is raised and, as in M0
+    (block_sparse.py:268-271), only the first `capacity` blocks of each dilation are
+    recomputed -- the rest keep their old values until the caller's dense refresh; within
+    the capacity a step is exact (sparse == dense bit for bit at tau = 0)."""
     from sarbon_b200 import LocalBackbone
     from sarbon_b200.block_sparse import BlockSparseEngine
     torch.manual_seed(2)
@@ -69,9 +73,11 @@ def test_overflow_flag_and_exact_outputs_fp16():
     assert over.dim() == 0 and bool(over)
     ref = BlockSparseEngine(net, 32)
     ref_outs = ref.full(f1)
+    assert any(not torch.equal(o, r) for o, r in zip(outs, ref_outs)), "blocks past the capacity were recomputed"
+    # the dense refresh the flag asks for, then a small change within the budget: exact
+    outs = eng.full(f1)
     for o, r in zip(outs, ref_outs):
         assert torch.equal(o, r)
-    # a small change fits the budget: no overflow, still exact
     f2 = f1.clone()
     f2[:, 100:110, 200:210] += 0.5
     outs, over = eng.step(f2, (H // 32) * (W // 32))
