@@ -73,7 +73,6 @@ SB_DEV float absdiff2(uint32_t x, uint32_t y) {
 template <int KIND>  // 0: fp16 frames, 1: fp32 frames, 2: uint8 BGR frames (fused prep)
 __global__ void __launch_bounds__(256, 4) gate_kernel(GateArgs a) {
   grid_dep_wait();  // programmatic dependent launch: the previous kernel's writes are visible
-  grid_dep_launch();  // after the wait: the next kernel may start its prologue now
   if (in_hysteresis(a.st)) return;  // hysteresis dense step: the gate is not looked at (:222-226)
   // CTA = blocks [bx0, bx0 + nblk) of block row `by` of camera `cam` (a segment of the row)
   const int by = blockIdx.x, cam = blockIdx.y, bx0 = blockIdx.z * a.seg;
@@ -296,6 +295,7 @@ __global__ void __launch_bounds__(256, 4) gate_kernel(GateArgs a) {
       for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
     }
   }
+  grid_dep_launch();
 }
 
 // ---------------------------------------------------------------- dilation + ordered lists
@@ -368,7 +368,6 @@ SB_DEV uint32_t lookback(unsigned long long* stat, uint32_t chunk, uint32_t epoc
 // block row, cell column), summing exactly in integer multiples of 2^-24.
 __global__ void __launch_bounds__(256) cell_gate_kernel(CellGateArgs a) {
   grid_dep_wait();
-  grid_dep_launch();  // after the wait: the next kernel may start its prologue now
   if (in_hysteresis(a.st)) return;
   extern __shared__ uint32_t s_blk[];  // [wb] changed flag per block of this block row
   const int by = blockIdx.x, cam = blockIdx.y;
@@ -419,11 +418,11 @@ __global__ void __launch_bounds__(256) cell_gate_kernel(CellGateArgs a) {
 #pragma unroll 4
     for (int r = 0; r < a.block; ++r) gw[(size_t)r * row_v + v] = __ldg(f + (size_t)r * row_v + v);
   }
+  grid_dep_launch();
 }
 
 __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
   grid_dep_wait();
-  grid_dep_launch();  // after the wait: the next kernel may start its prologue now
   State* st = a.st;
   if (in_hysteresis(st)) {  // hysteresis dense step: no gate, count -1 (fused_engine.py:222-226)
     if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -554,6 +553,7 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
       st->force_tiles = 0;
     }
   }
+  grid_dep_launch();
 }
 
 // ---------------------------------------------------------------- img copies
@@ -561,7 +561,6 @@ __global__ void __launch_bounds__(LIST_THREADS) lists_kernel(ListArgs a) {
 // Masked (calibration replays): img <- frames where `changed` (:157-160).
 __global__ void __launch_bounds__(256) copy_kernel(CopyArgs a) {
   grid_dep_wait();
-  grid_dep_launch();  // after the wait: the next kernel may start its prologue now
   const int mode = a.st->mode_cur;
   // dense steps and M0-mode steps (the whole frame enters the image cache,
   // block_sparse.py:272) copy every block
@@ -608,13 +607,13 @@ __global__ void __launch_bounds__(256) copy_kernel(CopyArgs a) {
       for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
     }
   }
+  grid_dep_launch();
 }
 
 // ---------------------------------------------------------------- state machine
 // End of a step (fused_engine.py:222-240): tick, hysteresis, stats, result slot.
 __global__ void finalize_kernel(State* st, int refresh, int32_t* host_out) {
   grid_dep_wait();
-  grid_dep_launch();  // after the wait: the next kernel may start its prologue now
   if (threadIdx.x != 0) return;
   const int mode = st->mode_cur;
   if (in_hysteresis(st)) {
@@ -636,6 +635,7 @@ __global__ void finalize_kernel(State* st, int refresh, int32_t* host_out) {
     host_out[2] = st->error;
     host_out[3] = 1;  // written
   }
+  grid_dep_launch();
 }
 
 // Reset / dense replay / calibration: force the mode of the conv sequence.
