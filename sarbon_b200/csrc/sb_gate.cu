@@ -74,6 +74,9 @@ template <int KIND>  // 0: fp16 frames, 1: fp32 frames, 2: uint8 BGR frames (fus
 __global__ void __launch_bounds__(256, 4) gate_kernel(GateArgs a) {
   grid_dep_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   if (in_hysteresis(a.st)) return;  // hysteresis dense step: the gate is not looked at (:222-226)
+  // CTA = blocks [bx0, bx0 + nblk) of block row `by` of camera `cam` (a segment of the row)
+  const int by = blockIdx.x, cam = blockIdx.y, bx0 = blockIdx.z * a.seg;
+  const int nblk = min(a.seg, a.wb - bx0);
   const int B = a.block;
   extern __shared__ __align__(16) uint8_t gsm[];
   unsigned long long* s_sx = reinterpret_cast<unsigned long long*>(gsm);  // [wb] exact sums (or double)
@@ -82,6 +85,12 @@ __global__ void __launch_bounds__(256, 4) gate_kernel(GateArgs a) {
   int* s_amb = reinterpret_cast<int*>(s_flag + a.seg);                   // [seg] ambiguous blocks
   __half* s_lut = reinterpret_cast<__half*>(s_amb + a.seg);              // [3][256] (u8 path)
   __shared__ int s_namb;
+  for (int i = threadIdx.x; i < nblk; i += blockDim.x) {
+    s_sx[i] = 0ull;
+    s_sf[i] = 0.f;
+    s_flag[i] = 0u;
+  }
+  if (threadIdx.x == 0) s_namb = 0;
   if (KIND == 2) {
     // normalised value of every uint8 level per RGB channel, with the reference's ops:
     // (x - mean[c]) / std[c] in fp32, then rounded to fp16 (video.py:99, :108)
@@ -90,20 +99,6 @@ __global__ void __launch_bounds__(256, 4) gate_kernel(GateArgs a) {
       s_lut[i] = __float2half_rn(__fdiv_rn(__fsub_rn((float)u, a.mean[c]), a.stdv[c]));
     }
   }
-  // Persistent grid (sized to the CTAs that fit at once): each CTA loops over work items =
-  // blocks [bx0, bx0 + nblk) of block row `by` of camera `cam` (a segment of the row), so the
-  // launch has no partial last wave.
-  const int nseg = (a.wb + a.seg - 1) / a.seg;
-  const int n_items = a.hb * a.n * nseg;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-  const int by = (item / nseg) % a.hb, cam = item / (nseg * a.hb), bx0 = (item % nseg) * a.seg;
-  const int nblk = min(a.seg, a.wb - bx0);
-  for (int i = threadIdx.x; i < nblk; i += blockDim.x) {
-    s_sx[i] = 0ull;
-    s_sf[i] = 0.f;
-    s_flag[i] = 0u;
-  }
-  if (threadIdx.x == 0) s_namb = 0;
   __syncthreads();
 
   const size_t row_px = (size_t)a.w;
@@ -300,8 +295,6 @@ __global__ void __launch_bounds__(256, 4) gate_kernel(GateArgs a) {
       for (int r = 0; r < B; ++r) g[(size_t)r * vpr + v] = __ldg(f + (size_t)r * vpr + v);
     }
   }
-  __syncthreads();  // the next item reuses the shared arrays
-  }  // work items
   grid_dep_launch();
 }
 
@@ -679,27 +672,13 @@ cudaError_t launch_gate(const GateArgs& a_in, int kind, cudaStream_t s) {
   GateArgs a = a_in;
   const int per_block = kind == 0 ? a.block * 3 / 8 : kind == 1 ? a.block * 3 / 4 : a.wb * a.block;
   a.seg = kind == 2 ? a.wb : std::max(1, std::min(a.wb, 256 / std::max(1, per_block)));
+  dim3 grid(a.hb, a.n, (a.wb + a.seg - 1) / a.seg);
   const size_t smem = (size_t)a.seg * (8 + 4 + 4 + 4) + 768 * 2 + 16;
-  void (*fn)(GateArgs) = kind == 0 ? gate_kernel<0> : kind == 1 ? gate_kernel<1> : gate_kernel<2>;
-  // as many CTAs as fit on the GPU at once (cached per kernel and shared-memory size)
-  static int n_sms = 0;
-  if (n_sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev) !=
-                                                  cudaSuccess || n_sms < 1)
-      n_sms = 148;
+  switch (kind) {
+    case 0: return launch_pdl(gate_kernel<0>, grid, dim3(256), smem, s, a);
+    case 1: return launch_pdl(gate_kernel<1>, grid, dim3(256), smem, s, a);
+    default: return launch_pdl(gate_kernel<2>, grid, dim3(256), smem, s, a);
   }
-  static int occ[3] = {}, occ_smem[3] = {};
-  if (occ[kind] == 0 || occ_smem[kind] != (int)smem) {
-    int o = 1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, fn, 256, smem) != cudaSuccess || o < 1) o = 1;
-    occ[kind] = o;
-    occ_smem[kind] = (int)smem;
-  }
-  const long long items = (long long)a.hb * a.n * ((a.wb + a.seg - 1) / a.seg);
-  const long long cap = (long long)n_sms * occ[kind];
-  dim3 grid((unsigned)(items < cap ? items : cap));
-  return launch_pdl(fn, grid, dim3(256), smem, s, a);
 }
 
 cudaError_t launch_cell_gate(const CellGateArgs& a, cudaStream_t s) {
