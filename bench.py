@@ -77,6 +77,9 @@ def parse():
     p.add_argument("--no-masks", action="store_true", help="skip timing the mask utility kernels")
     p.add_argument("--cell", type=int, default=0,
                    help="gate at cell level with this cell size (px; 0 = block level, the reference's rule)")
+    p.add_argument("--fp8", action="store_true",
+                   help="e4m3 caches and weights in the stride-8 stage (SB_CREATE_FP8_S8; BASELINE config 5's "
+                        "weight format)")
     p.add_argument("--cpu-seconds", type=float, default=20.0)
     p.add_argument("--no-reference-gpu", action="store_true",
                    help="skip timing the reference's own Triton engine on the GPU (rank 0, N = 1)")
@@ -502,12 +505,13 @@ def run_b200(args):
         raise SystemExit(f"--total-streams {args.total_streams} does not split evenly over {world} GPUs")
     S = len(shard_streams(job_streams(args, world), world, rank))
     H, W = args.height, args.width
-    eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev)
+    eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev, fp8=args.fp8)
     if args.cell:
         eng.set_cell_gating(args.cell)  # the u8 end-to-end step gates per block only
         args.no_e2e = True
     u8, rects = make_frames(args, rank, dev, world)
     staged = torch.stack([scenes.normalise(u8[i]) for i in range(u8.shape[0])])  # [F,S,H,W,3] fp16
+    fp8_scales = eng.calibrate_fp8(staged[0], net=net) if args.fp8 else None
     order = pingpong(args.frames)
     seq = [staged[i] for i in order]
 
@@ -582,6 +586,9 @@ def run_b200(args):
     # with programmatic dependent launch exactly as in the timed region
     ph = {"gate": 0.0, "lists": 0.0, "copy": 0.0, "conv": 0.0, "finalize": 0.0}
     ph_flops, nph = 0, 0
+    ph_ideal_s = 0.0  # the conv FLOPs at each layer's tensor peak (e4m3 layers: twice fp16)
+    peaks0, _ = load_peaks()
+    layer_peak = [peaks0["bf16_tflops"] * (2.0 if (m >> 4) == 2 else 1.0) for m in eng.layer_variants()]
     eng.reset(seq[0])
     for i in range(args.profile_steps):
         f = seq[1 + i % (len(seq) - 1)]
@@ -590,7 +597,9 @@ def run_b200(args):
         for key in ph:
             ph[key] += pm[key]
         if mode != "skip":
-            ph_flops += sum(layer_flops(eng, counts, mode))
+            fl = layer_flops(eng, counts, mode)
+            ph_flops += sum(fl)
+            ph_ideal_s += sum(f / (p * 1e12) for f, p in zip(fl, layer_peak))
         nph += 1
     peaks, src = load_peaks()
     default_workload = (S, H, W) == (16, 1088, 1920) and not args.cell
@@ -605,12 +614,17 @@ def run_b200(args):
     # launch's average duration is the sequence time / 11.  `isolated`: an event around every
     # launch, which serialises each layer's start-up (launch, barriers, weight copy, first
     # loads) with the previous layer's end; the step itself overlaps them.
+    # e4m3 layers run at twice the fp16 tensor rate: the peak is then the FLOP-weighted one
+    # of the sequence (FLOPs / the time they take at each layer's peak)
+    peak_eff = ph_flops / ph_ideal_s / 1e12 if ph_ideal_s > 0 else peaks["bf16_tflops"]
     roof = {"bound": "tensor", "kernel": "sb::conv_tc_kernel (tile conv, all 11 layers)",
-            "achieved": pipe_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": pipe_tflops / peaks["bf16_tflops"],
+            "achieved": pipe_tflops, "peak": peak_eff, "unit": "TFLOP/s",
+            "frac": pipe_tflops / peak_eff,
             "timing": "conv sequence of the pipelined step (events at the phase boundaries only)",
             "traffic": traffic["conv"], "traffic_source": traffic["capture"],
-            "peak_source": f"{src} bf16_tflops (burst; fp16 dense runs at the bf16 rate)",
+            "peak_source": f"{src} bf16_tflops (burst; fp16 dense runs at the bf16 rate)" + (
+                "; e4m3 layers (kind::f8f6f4) at 2x that, the dense fp8:fp16 ratio of the tensor cores, "
+                "FLOP-weighted over the sequence" if args.fp8 else ""),
             "flops_per_launch": ph_flops / (nph * len(eng.layers)),
             "mma_flops_per_launch": sum(mma_layer) / n_conv,
             "ms_per_launch": ph["conv"] / (nph * len(eng.layers)),
@@ -708,11 +722,12 @@ def run_b200(args):
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong" if args.total_streams else "weak", "vs_baseline": None,
-            "dtype": "f16 (fp32 accumulate)",
+            "dtype": "f16 + e4m3 stride-8 stage (fp32 accumulate)" if args.fp8 else "f16 (fp32 accumulate)",
             "data": "synthetic (seeded moving-rectangle camera streams, random-init Sarbon-S stem)",
             "config": {"workload": workload_name(args, world), "job_streams": job_streams(args, world),
                        "height": H, "width": W, "block": 32, "streams_per_gpu": S, "rects_per_stream": rects,
                        "gating": f"cell level, {args.cell} px cells" if args.cell else "block level",
+                       "fp8_act_scales": fp8_scales,
                        "tau_grey_levels": 8, "frames_staged": args.frames,
                        "changed_block_frac": changed_frac,
                        "active_block_frac": {f"d{d}": a for d, a in zip(eng.ds, act_frac)},

@@ -43,9 +43,11 @@ extern "C" {
 #define SB_ECUDA      4   /* a CUDA runtime/driver call failed */
 #define SB_ENOMEM     5   /* device or pinned allocation failed */
 
-/* cache element types (fused_engine.py:55-56 `dtype`) */
+/* cache element types (fused_engine.py:55-56 `dtype`); SB_F8: e4m3 codes with an
+ * activation scale per cache (value = code * scale), see SB_CREATE_FP8_S8 */
 #define SB_F16 0
 #define SB_F32 1
+#define SB_F8  2
 
 /* step modes (fused_engine.py:230-237) */
 #define SB_MODE_SKIP   0
@@ -91,6 +93,16 @@ SB_API int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, i
  * blocks (no multi-block window regions), which M0 mode needs; slower for the 4x4-pixel
  * layers.  sb_create(...) is sb_create_ex(..., 0, out). */
 #define SB_CREATE_BLOCK_UNITS 1
+/* SB_CREATE_FP8_S8 (fp16 engines): the caches of the stride-8 stage (every layer with
+ * out_stride >= 8) hold e4m3 codes with one activation scale per cache (sb_set_act_scale,
+ * default 1); the layer that enters the stage runs fp16 MMAs and writes e4m3, the layers
+ * inside it run tcgen05 kind::f8f6f4 MMAs on e4m3 activations and e4m3 weights quantised
+ * per output channel (scale = max |w| / 448 of the channel, sb_layer_wscale), dequantised
+ * in the fp32 epilogue (bias, residual, ReLU), then quantised to e4m3 again.  No reference
+ * counterpart (the reference casts its tile weights to the engine dtype,
+ * fused_engine.py:114): this is BASELINE config 5's weight format, applied to the stage where
+ * it halves the tensor-core work and the weights. */
+#define SB_CREATE_FP8_S8 2
 SB_API int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width,
                         int block, int dtype, double tau, int refresh, int dense_check_every, int flags,
                         sb_engine** out);
@@ -208,6 +220,20 @@ SB_API int sb_run_sparse_forced(sb_engine* e, const void* frames_dev, int64_t n_
  * implementation (sb_cache_ptr), one layer's output from that implementation's own inputs
  * can be compared layer by layer. */
 SB_API int sb_dense_layers(sb_engine* e, int first, int last, void* stream);
+
+/* Element type of cache `cache_id` (SB_F16, SB_F32 or SB_F8) and, for SB_F8, its activation
+ * scale (value = code * scale; scale may be NULL).  No reference counterpart. */
+SB_API int sb_cache_dtype(sb_engine* e, int cache_id, int* dtype, float* scale);
+
+/* Activation scale of an e4m3 cache (SB_CREATE_FP8_S8) for the steps launched after this
+ * call: the layer writing it stores e4m3(y / scale), the layers reading it multiply by it.
+ * Drops the captured step graphs.  No reference counterpart. */
+SB_API int sb_set_act_scale(sb_engine* e, int cache_id, float scale);
+
+/* Per-output-channel scales of layer `layer`'s e4m3 weights (n >= cout floats): weight =
+ * e4m3 code * scale[c], code = e4m3(w / scale[c]) rounded to nearest even.  No reference
+ * counterpart. */
+SB_API int sb_layer_wscale(sb_engine* e, int layer, float* out, int n);
 
 /* Cache views (fused_engine.py:67-71,124-125): device pointer and NHWC shape of
  * cache id (0 = image, i+1 = layer i output). */

@@ -408,3 +408,34 @@ class OracleEngine:
 
     def outputs_nchw(self):
         return [self.cache[o].transpose(0, 3, 1, 2) for o in self.outputs]
+
+
+# ----------------------------------------------------------------------------- e4m3 stage
+# The engine's optional e4m3 stride-8 stage has no reference counterpart (the reference
+# keeps its tile weights in the engine dtype, fused_engine.py:114); these restate its
+# arithmetic so that each e4m3 layer can be checked against its own inputs.
+def e4m3(x):
+    """Nearest e4m3 (E4M3FN) values of float array `x`, ties to even, saturated to +-448,
+    as float32 (torch's float8_e4m3fn type does the rounding)."""
+    import torch
+    t = torch.from_numpy(np.clip(np.asarray(x, np.float32), -448.0, 448.0))
+    return t.to(torch.float8_e4m3fn).to(torch.float32).numpy()
+
+
+def e4m3_codes(x):
+    """e4m3 bit patterns (uint8) of the values nearest to `x` (as `e4m3`)."""
+    import torch
+    t = torch.from_numpy(np.clip(np.asarray(x, np.float32), -448.0, 448.0))
+    return t.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+
+def conv_dense_e4m3(x, w, bias, stride, act, res, s_out, w_scale=None):
+    """One layer of the e4m3 stage, densely: x and res are dequantised float inputs; with
+    `w_scale` (per output channel) the weights are first quantised as the engine quantises
+    them, code = e4m3(w / s), value = code * s.  Returns the e4m3 codes of y / s_out."""
+    w = np.asarray(w, np.float32)
+    if w_scale is not None:
+        w = e4m3(w / w_scale[None, None, None, :]) * w_scale[None, None, None, :]
+    y = conv_dense(np.asarray(x, np.float32), w, bias, stride, act, None if res is None else np.asarray(res, np.float32),
+                   np.float32)
+    return e4m3_codes(y / np.float32(s_out))

@@ -11,10 +11,11 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libsarbon_sparse.so"
 
 SB_OK, SB_EINVAL, SB_EOVERFLOW, SB_ETIMEOUT, SB_ECUDA, SB_ENOMEM = range(6)
-SB_F16, SB_F32 = 0, 1
+SB_F16, SB_F32, SB_F8 = 0, 1, 2
 SB_MODE_SKIP, SB_MODE_SPARSE, SB_MODE_DENSE = 0, 1, 2
 MODE_NAMES = ("skip", "sparse", "dense")
 SB_CREATE_BLOCK_UNITS = 1
+SB_CREATE_FP8_S8 = 2
 SB_MAX_LAYERS = 32
 SB_MAX_DILATIONS = 4
 
@@ -73,6 +74,9 @@ PROTOTYPES = {
     "sb_set_step_graphs": (_I, [_P, _I]),
     "sb_debug_withhold_lookback": (_I, [_P, _I, _I]),
     "sb_cache_ptr": (_I, [_P, _I, C.POINTER(_P), C.POINTER(_I64)]),
+    "sb_cache_dtype": (_I, [_P, _I, C.POINTER(_I), C.POINTER(C.c_float)]),
+    "sb_set_act_scale": (_I, [_P, _I, C.c_float]),
+    "sb_layer_wscale": (_I, [_P, _I, C.POINTER(C.c_float), _I]),
     "sb_layer_variant": (_I, [_P, _I, C.POINTER(_I)]),
     "sb_cell_active_blocks": (_I, [_P, _I, _I, _I, _I, _I, C.POINTER(_I), _I, _P, _P]),
     "sb_boxes_to_block_mask": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),

@@ -25,6 +25,8 @@
 //   * the 3-channel first layer cannot be fetched by TMA (6-byte pixels); its A rows
 //     (27 taps x channels, zero-padded to K=32) are gathered by producer warps from a
 //     TMA-loaded input window.
+#include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -55,8 +57,15 @@ constexpr int kMaxCout = 128;     // widest layer of the stem (ConvArgs::bias_v 
 // PAIR = 1: a 2-CTA cluster runs M=256 cta_group::2 MMAs; each CTA holds NCTA of the
 //           2*NCTA output channels as its half of B and all 2*NCTA accumulator columns of
 //           its own 128 pixels.
-template <int CIN, int NCTA, int T, int S, int WIN, int PAIR = 0>
+// Q = 0: fp16 input, weights and output caches (kind::f16 MMAs).
+// Q = 1: fp16 input and weights, the output cache in e4m3 (scaled by 1 / its activation scale).
+// Q = 2: e4m3 input cache, weights (per output channel scale), residual and output caches;
+//        kind::f8f6f4 MMAs (K = 32 per instruction) and the dequantisation in the fp32 epilogue:
+//        y = acc * (s_in * s_w[c]) + bias[c] + s_res * res, ReLU, e4m3(y / s_out).
+template <int CIN, int NCTA, int T, int S, int WIN, int PAIR = 0, int Q = 0>
 struct TcCfg {
+  static constexpr int AE = Q == 2 ? 1 : 2;            // bytes per A / B element
+  static constexpr int OE = Q >= 1 ? 1 : 2;            // bytes per output (and residual) element
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
   // first layer: K slots per ky (its 3*CIN (kx, c) elements rounded up to even, so that each
@@ -66,13 +75,17 @@ struct TcCfg {
   static constexpr int KRUN = MANUAL ? ((3 * CIN + 1) / 2) * 2 : 0;
   static constexpr bool BIAS_IN_K = MANUAL && 3 * KRUN + 2 <= KPAD;
   // K elements per K-block (WIN = 2: a pair of input pixels x channels)
-  static constexpr int CH = MANUAL ? KPAD : WIN == 2 ? 64 : (CIN % 64 == 0 ? 64 : 32);
+  static constexpr int CH = MANUAL ? KPAD
+                           : WIN == 2 ? 64
+                           : AE == 1 ? (CIN % 128 == 0 ? 128 : 64)
+                                     : (CIN % 64 == 0 ? 64 : 32);
   static constexpr int NCH = (MANUAL || WIN == 2) ? 1 : CIN / CH;
   // WIN = 2 with 64 channels: two boxes per K-block (odd and even input columns)
   static constexpr int NBOX = (WIN == 2 && CIN == 64) ? 2 : 1;
   static constexpr int NKB = MANUAL ? 1 : (WIN == 3 ? 1 : (WIN == 1 || WIN == 2) ? 3 : 9) * NCH;  // per M-tile
   static constexpr int NWKB = MANUAL ? 1 : WIN == 2 ? (CIN == 32 ? 6 : 9) : 9 * NCH;  // weight K-blocks
-  static constexpr int ROWB = CH * 2;                 // bytes per operand row
+  static constexpr int ROWB = CH * AE;                // bytes per operand row
+  static constexpr int KSTEPS = ROWB / 32;            // MMAs per row: 32 bytes of K each
   static constexpr int SWZ = ROWB == 128 ? 2 : 4;     // 128B / 64B swizzle
   static constexpr int SBO = 8 * ROWB;
   static constexpr int TT = T * T;
@@ -104,7 +117,8 @@ struct TcCfg {
   // bias: CTA pairs stage it in shared memory; the other layers read it from the kernel
   // parameters (ConvArgs::bias_v, warp-uniform constant-cache reads) -- measured faster there
   static constexpr bool BIAS_SMEM = PAIR != 0;
-  static constexpr int BIAS_BYTES = BIAS_SMEM ? kMaxCout * 4 : 0;
+  // pairs: the bias, and for Q = 2 the per-channel dequantisation scales after it
+  static constexpr int BIAS_BYTES = BIAS_SMEM ? kMaxCout * 4 * (Q == 2 ? 2 : 1) : 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
   // Epilogue output through shared memory: each epilogue warp writes its 32 output pixels
   // (NCOL channels each) into its own staging buffer and stores them with one TMA tile
@@ -167,6 +181,8 @@ struct TcCfg {
   static_assert(NCTA % 32 == 0 && NCTA >= 32 && NMMA <= 256, "UMMA N / epilogue split");
   static_assert(!PAIR || !MANUAL, "CTA pairs need TMA-loaded A stages");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
+  static_assert(Q == 0 || (PAIR && !MANUAL), "e4m3 caches: CTA-pair layers only");
+  static_assert(Q != 2 || (WIN == 1 && ROWB == 128), "e4m3 inputs: row windows over 128-byte pixel rows");
   static_assert(!MANUAL || ((NISS * SUB) % NGW == 0 && NWB % NGW == 0), "gather warp per stage / window slot");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
   static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256 && WIN_COLS % 2 == 0), "first-layer window box");
@@ -226,11 +242,11 @@ SB_DEV void stage_of(int it, int kb, uint32_t& s, uint32_t& ph) {
   ph = (gu / C::SUB) & 1u;
 }
 
-template <int CIN, int NCTA, int T, int S, int WIN, int PAIR>
-__global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
+template <int CIN, int NCTA, int T, int S, int WIN, int PAIR, int Q>
+__global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS, 1)
     conv_tc_kernel(const __grid_constant__ ConvArgs a, const __grid_constant__ CUtensorMap tmap,
                    const __grid_constant__ CUtensorMap tmap_y) {
-  using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
+  using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sW = smem + C::W_OFF;
@@ -293,7 +309,10 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
     }
   }
   if (C::BIAS_SMEM)
-    for (int i = threadIdx.x; i < a.cout; i += blockDim.x) sBias[i] = a.bias_v[i];
+    for (int i = threadIdx.x; i < a.cout; i += blockDim.x) {
+      sBias[i] = a.bias_v[i];
+      if (Q == 2) sBias[kMaxCout + i] = a.dq_v[i];
+    }
   if (!C::MANUAL && warp == C::PROD_WARP && lane == 0) prefetch_tmap(&tmap);
   if (C::TSTORE && warp == 0 && lane == 0) prefetch_tmap(&tmap_y);
   tc_fence_before();
@@ -643,7 +662,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
 #pragma unroll
                 for (int kx = 0; kx < NTX; ++kx)
 #pragma unroll
-                  for (int kk = 0; kk < C::CH / 16; ++kk) {
+                  for (int kk = 0; kk < C::KSTEPS; ++kk) {
                     constexpr int SLOT = C::TPM * C::BOX_BYTES;
                     const uint32_t a_off = C::NBOX == 2
                                                ? (kx == 2 ? SLOT : 0) + (kx == 0 ? 0 : 1) * C::ROWB + kk * 32
@@ -651,7 +670,10 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
                     const int wk = C::NBOX == 2 ? kb * 3 + (kx == 0 ? 0 : kx == 1 ? 2 : 1)
                                    : WIN == 2 ? kb * 2 + kx : ((ky0 + dy) * 3 + kx) * C::NCH + ch;
                     const uint32_t b_off = wk * C::B_KB + kk * 32;
-                    if (PAIR)
+                    if (PAIR && Q == 2)
+                      mma_f8_ss2(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
+                                 (kb | dy | kx | kk) != 0 ? 1u : 0u);
+                    else if (PAIR)
                       mma_f16_ss2(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
                                   (kb | dy | kx | kk) != 0 ? 1u : 0u);
                     else
@@ -660,7 +682,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
                   }
             } else {
 #pragma unroll
-              for (int kk = 0; kk < C::CH / 16; ++kk) {
+              for (int kk = 0; kk < C::KSTEPS; ++kk) {
                 if (PAIR)
                   mma_f16_ss2(d_tmem, a_desc + ((kk * 32) >> 4), b_desc0 + ((kb * C::B_KB + kk * 32) >> 4),
                               C::IDESC, (kb | kk) != 0 ? 1u : 0u);
@@ -711,13 +733,19 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       const int q = warp & 3, eg = C::EPG == 2 ? (warp >> 2) : 0;  // lane quadrant, group
       const int col0 = C::EPG == 2 ? 0 : (warp >> 2) * C::NCOL;
       const int k = lane >> 2, m = lane & 3;
-      __half* y = static_cast<__half*>(a.y);
-      const __half* res = static_cast<const __half*>(a.res);
+      // output and residual caches: fp16, or e4m3 codes (C::OE bytes per element)
+      uint8_t* y = static_cast<uint8_t*>(a.y);
+      const uint8_t* res = static_cast<const uint8_t*>(a.res);
       // this thread's output channels are the same for every item of the launch
       const int n0 = (PAIR ? 0 : ((int)blockIdx.x % (a.cout / NCTA)) * NCTA) + col0 + CPT * m;
       float bias[CPT];
+      float dq[Q == 2 ? CPT : 1];  // e4m3 inputs: s_in * s_w[c] of each channel
 #pragma unroll
-      for (int t = 0; t < CPT; ++t) bias[t] = C::BIAS_SMEM ? sBias[n0 + t] : a.bias_v[n0 + t];
+      for (int t = 0; t < CPT; ++t) {
+        bias[t] = C::BIAS_SMEM ? sBias[n0 + t] : a.bias_v[n0 + t];
+        if constexpr (Q == 2) dq[t] = sBias[kMaxCout + n0 + t];
+      }
+      const float res_scale = a.res_scale, out_inv = a.out_inv_scale;
       // Pixel sr (0..3) of this thread is accumulator row q*32 + k + 8*sr.  When a warp's 32
       // rows lie in one unit (ONEUNIT) its pixels sit at fixed offsets from the first one.
       constexpr int UPX = WIN ? C::RPX : (C::TT >= 128 ? 128 : C::TT);  // rows of one unit in an M-tile
@@ -728,7 +756,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
         size_t pix[ONEUNIT ? 1 : 4];  // element of channel n0: pixel 0 (ONEUNIT) or each pixel
         int p;                        // pixel 0's index within its unit (ONEUNIT)
         unsigned okm;                 // bit sr: pixel sr is stored
-        uint4 rr[4][CPT / 8];         // residual: CPT channels of each pixel
+        uint4 rr[4][CPT * C::OE / 16];  // residual: CPT channels of each pixel
       };
       const size_t rowstride = (size_t)a.wo * a.cout;
       // offset of pixel sr from pixel 0 (ONEUNIT): unit pixel p + 8 sr, UW pixels per row
@@ -781,12 +809,12 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
           const bool st = valid && inb;
           if (st) o.okm |= 1u << sr;
           if (res != nullptr) {
-            const size_t px = pix_of(o, sr);
-            if constexpr (CPT == 16) {
-              if (st) ld_global_nc_v8(res + px, o.rr[sr][0], o.rr[sr][1]);
+            const uint8_t* rp = res + pix_of(o, sr) * C::OE;
+            if constexpr (CPT * C::OE == 32) {
+              if (st) ld_global_nc_v8(rp, o.rr[sr][0], o.rr[sr][1]);
               else o.rr[sr][0] = o.rr[sr][1] = make_uint4(0, 0, 0, 0);
             } else {
-              o.rr[sr][0] = st ? __ldg(reinterpret_cast<const uint4*>(res + px)) : make_uint4(0, 0, 0, 0);
+              o.rr[sr][0] = st ? __ldg(reinterpret_cast<const uint4*>(rp)) : make_uint4(0, 0, 0, 0);
             }
           }
         }
@@ -797,25 +825,46 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
       auto out_pixel = [&](const Row& cu, int sr, const uint32_t* f) {
         if (!((cu.okm >> sr) & 1u)) return;
         const uint32_t* rw = reinterpret_cast<const uint32_t*>(&cu.rr[sr][0]);
+        const uint16_t* rw8 = reinterpret_cast<const uint16_t*>(&cu.rr[sr][0]);
         uint32_t o[CPT / 2];
 #pragma unroll
         for (int jj = 0; jj < REP; ++jj) {
-          float f0 = __uint_as_float(f[4 * jj]) + bias[2 * jj];
-          float f1 = __uint_as_float(f[4 * jj + 1]) + bias[2 * jj + 1];
+          float f0, f1;
+          if constexpr (Q == 2) {  // dequantise the e4m3 x e4m3 accumulation per channel
+            f0 = fmaf(__uint_as_float(f[4 * jj]), dq[2 * jj], bias[2 * jj]);
+            f1 = fmaf(__uint_as_float(f[4 * jj + 1]), dq[2 * jj + 1], bias[2 * jj + 1]);
+          } else {
+            f0 = __uint_as_float(f[4 * jj]) + bias[2 * jj];
+            f1 = __uint_as_float(f[4 * jj + 1]) + bias[2 * jj + 1];
+          }
           if (res != nullptr) {
-            const float2 t2 = __half22float2(*reinterpret_cast<const __half2*>(&rw[jj]));
-            f0 += t2.x;
-            f1 += t2.y;
+            if constexpr (C::OE == 1) {
+              const float2 t2 = float2_of_e4m3x2(rw8[jj]);
+              f0 = fmaf(t2.x, res_scale, f0);
+              f1 = fmaf(t2.y, res_scale, f1);
+            } else {
+              const float2 t2 = __half22float2(*reinterpret_cast<const __half2*>(&rw[jj]));
+              f0 += t2.x;
+              f1 += t2.y;
+            }
           }
           if (a.act) {
             f0 = fmaxf(f0, 0.0f);
             f1 = fmaxf(f1, 0.0f);
           }
-          __half2 h2 = __floats2half2_rn(f0, f1);
-          o[jj] = *reinterpret_cast<uint32_t*>(&h2);
+          if constexpr (C::OE == 1) {  // two e4m3 codes per jj: 16 channels = 16 bytes
+            const uint32_t q = e4m3x2_of(f0 * out_inv, f1 * out_inv);
+            if (jj & 1) o[jj >> 1] |= q << 16;
+            else o[jj >> 1] = q;
+          } else {
+            __half2 h2 = __floats2half2_rn(f0, f1);
+            o[jj] = *reinterpret_cast<uint32_t*>(&h2);
+          }
         }
-        __half* dst = y + pix_of(cu, sr);
-        if constexpr (CPT == 16)
+        uint8_t* dst = y + pix_of(cu, sr) * C::OE;
+        if constexpr (C::OE == 1)
+          *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+        else if constexpr (CPT == 16)
           st_global_v8(dst, make_uint4(o[0], o[1], o[2], o[3]), make_uint4(o[4], o[5], o[6], o[7]));
         else
           *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -1085,18 +1134,18 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR>::THREADS, 1)
 namespace {
 
 struct Variant {
-  int cin, cout, t, s, win, ncta, pair;
+  int cin, cout, t, s, win, ncta, pair, q;
   void (*fn)(const ConvArgs, const CUtensorMap, const CUtensorMap);
   int smem, threads, w_bytes, ch, box_rows, win_cols, win_rows;
   int tstore, ncol, obw;  // staged output stores: flag, channels and width of a warp's box
   int mode() const { return win | (pair << 3); }
 };
 
-template <int CIN, int NCTA, int T, int S, int WIN = 0, int PAIR = 0>
+template <int CIN, int NCTA, int T, int S, int WIN = 0, int PAIR = 0, int Q = 0>
 Variant make_variant(int cout) {
-  using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR>;
-  Variant v{CIN,       cout,       T,         S,         WIN,       NCTA,      PAIR,
-                 conv_tc_kernel<CIN, NCTA, T, S, WIN, PAIR>,  C::SMEM,   C::THREADS, C::W_BYTES,
+  using C = TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>;
+  Variant v{CIN,       cout,       T,         S,         WIN,       NCTA,      PAIR,      Q,
+                 conv_tc_kernel<CIN, NCTA, T, S, WIN, PAIR, Q>,  C::SMEM,   C::THREADS, C::W_BYTES,
                  C::CH,     C::BOX_ROWS, C::WIN_COLS, C::WIN_ROWS, C::TSTORE ? 1 : 0, C::NCOL, C::OBW};
   return v;
 }
@@ -1121,6 +1170,9 @@ const std::vector<Variant>& variants() {
       make_variant<128, 64, 4, 1, 3, 1>(128),  // CTA pairs, full windows over 2x4-block regions
       make_variant<128, 64, 4, 1, 3>(128),     // full windows, two C_out slices
       make_variant<128, 64, 4, 1, 0, 1>(128),  // CTA pairs, per-tap boxes over blocks (block units)
+      // e4m3 caches of the stride-8 stage: fp16 in / e4m3 out, then e4m3 in and out
+      make_variant<64, 64, 4, 2, 2, 1, 1>(128),
+      make_variant<128, 64, 4, 1, 1, 1, 2>(128),
       // block 64
       make_variant<3, 32, 32, 2>(32),
       make_variant<32, 64, 16, 2>(64),
@@ -1143,11 +1195,15 @@ bool pairs_disabled() {
 }
 
 // mode < 0: the default variant of the shape; else the variant with that mode
-// (window mode | pair << 3).
-const Variant* find_variant(int cin, int cout, int t, int s, int mode = -1) {
+// (window mode | pair << 3).  q selects the e4m3 variants (0: fp16 caches).
+const Variant* find_variant(int cin, int cout, int t, int s, int mode = -1, int q = 0) {
   const bool no_pair = pairs_disabled();
   for (const auto& v : variants()) {
-    if (v.cin != cin || v.cout != cout || v.t != t || v.s != s) continue;
+    if (v.cin != cin || v.cout != cout || v.t != t || v.s != s || v.q != q) continue;
+    if (q) {
+      if (mode < 0 || v.mode() == mode) return &v;
+      continue;
+    }
     if (mode < 0 ? (no_pair && v.pair) : v.mode() != mode) continue;
     return &v;
   }
@@ -1183,22 +1239,27 @@ int conv_tc_block_mode(int cin, int cout, int t, int s) {
   return best ? best->mode() : -1;
 }
 
+int conv_tc_q_mode(int cin, int cout, int t, int s, int q) {
+  const Variant* v = find_variant(cin, cout, t, s, -1, q);
+  return v ? v->mode() : -1;
+}
+
 namespace {
 // The variant the engine runs (and whose weight image it builds) for a layer of mode `mode`.
-const Variant* picked(int cin, int cout, int t, int s, int mode) {
-  return mode < 0 ? nullptr : find_variant(cin, cout, t, s, mode);
+const Variant* picked(int cin, int cout, int t, int s, int mode, int q = 0) {
+  return mode < 0 ? nullptr : find_variant(cin, cout, t, s, mode, q);
 }
 }  // namespace
 
 bool conv_tc_supported(int cin, int cout, int t, int s) { return find_variant(cin, cout, t, s) != nullptr; }
 
-int conv_tc_nsplit(int cin, int cout, int t, int s, int mode) {
-  const Variant* v = picked(cin, cout, t, s, mode);
+int conv_tc_nsplit(int cin, int cout, int t, int s, int mode, int q) {
+  const Variant* v = picked(cin, cout, t, s, mode, q);
   return v ? v->cout / v->ncta : 0;
 }
 
-size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode) {
-  const Variant* v = picked(cin, cout, t, s, mode);
+size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode, int q) {
+  const Variant* v = picked(cin, cout, t, s, mode, q);
   return v ? (size_t)v->w_bytes * (v->cout / v->ncta) : 0;
 }
 
@@ -1222,9 +1283,42 @@ int out_channel_of_column(int n, int g) {
 // then channel chunk), NCTA rows of ROWB bytes, K-major, with the 128B/64B swizzle
 // applied exactly as the MMA reads it from a 1024-byte-aligned shared buffer.
 void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w, const float* bias,
-                        uint16_t* out) {
-  const Variant* v = picked(cin, cout, t, s, mode);
+                        uint16_t* out, int q, float* wscale) {
+  const Variant* v = picked(cin, cout, t, s, mode, q);
   if (!v) return;
+  if (q == 2) {
+    // e4m3 codes, one scale per output channel: wscale[c] = max |w[., ., ., c]| / 448 (the
+    // largest e4m3 magnitude), code = e4m3(w / wscale[c]) rounded to nearest even.  Layout
+    // as the fp16 image (tap-major K-blocks of ch input channels, one 128-byte row per
+    // output channel, 16-byte chunks swizzled), one byte per element.
+    const int ch = v->ch, rowb = ch, ncta = v->ncta, nsplit = cout / ncta, nch = cin / ch, nkb = 9 * nch;
+    std::vector<float> sc(cout);
+    for (int c = 0; c < cout; ++c) {
+      float amax = 0.f;
+      for (int k = 0; k < 9 * cin; ++k) amax = std::max(amax, std::fabs(w[(size_t)k * cout + c]));
+      sc[c] = amax > 0.f ? amax / 448.f : 1.f;
+      if (wscale) wscale[c] = sc[c];
+    }
+    uint8_t* bytes = reinterpret_cast<uint8_t*>(out);
+    const size_t split_bytes = (size_t)v->w_bytes;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      uint8_t* img = bytes + sp * split_bytes;
+      std::memset(img, 0, split_bytes);
+      for (int kb = 0; kb < nkb; ++kb)
+        for (int n = 0; n < ncta; ++n) {
+          const int co = v->pair ? out_channel_of_column(sp * ncta + n, v->ncol) : sp * ncta + n;
+          for (int k = 0; k < ch; ++k) {
+            const int tap = kb / nch, ci = (kb % nch) * ch + k;
+            const float val = w[((size_t)tap * cin + ci) * cout + co] / sc[co];
+            const int qq = k / 16, within = k % 16;
+            const int pq = qq ^ (n & 7);
+            img[(size_t)kb * ncta * rowb + (size_t)n * rowb + pq * 16 + within] =
+                (uint8_t)__nv_cvt_float_to_fp8(val, __NV_SATFINITE, __NV_E4M3);
+          }
+        }
+    }
+    return;
+  }
   if (v->win == 2 && cin == 32) {
     // pair windows: block ky*2 + tap; K element k = (dx, c) of a pixel pair; tap 0 (pair
     // offset -1) holds kx = 0 in its odd half, tap 1 (offset 0) kx = 1 / kx = 2 in its halves
@@ -1310,11 +1404,24 @@ static PFN_encodeTiled get_encode() {
 // with element strides {1, S, S, 1} so that one box is the strided im2col slice of one
 // tap for one tile.
 cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s,
-                              int mode) {
+                              int mode, int q) {
   const Variant* v = nullptr;
   for (const auto& c : variants())
-    if (c.cin == cin && c.t == t && c.s == s && c.win == (mode & 7)) { v = &c; break; }
+    if (c.cin == cin && c.t == t && c.s == s && c.win == (mode & 7) && (q == 2) == (c.q == 2)) { v = &c; break; }
   if (!v) return cudaErrorInvalidValue;
+  if (q == 2) {
+    // e4m3 cache [n][hx][wx][cin] bytes, row windows: 10 px x t rows of ch channels per box
+    PFN_encodeTiled enc = get_encode();
+    if (!enc) return cudaErrorNotSupported;
+    cuuint64_t dims[4] = {(cuuint64_t)cin, (cuuint64_t)wx, (cuuint64_t)hx, (cuuint64_t)n};
+    cuuint64_t strides[3] = {(cuuint64_t)cin, (cuuint64_t)wx * cin, (cuuint64_t)hx * wx * cin};
+    cuuint32_t box[4] = {(cuuint32_t)v->ch, 10u, (cuuint32_t)v->box_rows, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(src), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+  }
   const bool win = v->win != 0;
   if (cin < 16) {
     // first layer: the image cache as [N][H][W*cin] fp16, one box = one M-tile's window
@@ -1387,18 +1494,18 @@ cudaError_t conv_tc_make_tmap_out(CUtensorMap* map, void* dst, int n, int ho, in
 }
 
 cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, const CUtensorMap* map_y, int grid_x,
-                           cudaStream_t st) {
-  const Variant* v = find_variant(a.cin, a.cout, a.t, a.s, mode);
+                           cudaStream_t st, int q) {
+  const Variant* v = find_variant(a.cin, a.cout, a.t, a.s, mode, q);
   // every variant loads through TMA; staged-output variants also store through map_y
   if (!v || map == nullptr || map_y == nullptr || a.cout > kMaxCout) return cudaErrorInvalidValue;
-  static bool attr_done[32] = {};
+  static bool attr_done[64] = {};
   const int idx = (int)(v - variants().data());
   if (!attr_done[idx]) {
     cudaError_t e = cudaFuncSetAttribute(v->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v->smem);
     if (e != cudaSuccess) return e;
     attr_done[idx] = true;
   }
-  static int occ[32] = {};
+  static int occ[64] = {};
   if (occ[idx] == 0) {
     int o = 1;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, v->fn, v->threads, v->smem) != cudaSuccess || o < 1) o = 1;
@@ -1420,7 +1527,7 @@ cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, 
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;  // occupancy query with the cluster shape only
-    static int max_clusters[32] = {};
+    static int max_clusters[64] = {};
     if (max_clusters[idx] == 0) {
       cfg.gridDim = dim3(2 * (grid_x / 2 > 0 ? grid_x / 2 : 1), 1, 1);
       int n = 0;

@@ -78,6 +78,14 @@ struct sb_engine {
   int layer_t[SB_MAX_LAYERS] = {};
   void* cache[SB_MAX_LAYERS + 1] = {};
   int64_t shape[SB_MAX_LAYERS + 1][4] = {};
+  // e4m3 caches (SB_CREATE_FP8_S8): element bytes and activation scale of each cache
+  // (value = code * scale), and per layer its e4m3 variant (0 fp16, 1 fp16 in / e4m3 out,
+  // 2 e4m3 in and out) and the per-output-channel scales of its e4m3 weights
+  int cache_esz[SB_MAX_LAYERS + 1] = {};
+  bool cache_f8[SB_MAX_LAYERS + 1] = {};
+  float act_scale[SB_MAX_LAYERS + 1] = {};
+  int layer_q[SB_MAX_LAYERS] = {};
+  std::vector<float> wscale[SB_MAX_LAYERS];
   uint8_t* changed = nullptr;
   uint8_t* extra = nullptr;
   uint8_t* masks = nullptr;
@@ -263,6 +271,11 @@ int launch_convs(sb_engine* e, cudaStream_t s, int first = 0, int last = -1) {
     a.res = L.res >= 0 ? e->cache[L.res] : nullptr;
     a.bias = e->bias[i];
     std::memcpy(a.bias_v, e->bias_h[i], sizeof(a.bias_v));
+    const int q = e->layer_q[i];
+    for (int c = 0; c < 128; ++c)
+      a.dq_v[c] = q == 2 && c < L.cout ? e->act_scale[L.src] * e->wscale[i][c] : 1.f;
+    a.res_scale = L.res >= 0 && e->cache_f8[L.res] ? e->act_scale[L.res] : 1.f;
+    a.out_inv_scale = e->cache_f8[i + 1] ? 1.f / e->act_scale[i + 1] : 1.f;
     a.wimg = e->wdev[i];
     const int di = e->layer_di[i];
     a.lcam = e->lists + (size_t)di * 3 * e->n_blocks;
@@ -299,7 +312,7 @@ int launch_convs(sb_engine* e, cudaStream_t s, int first = 0, int last = -1) {
     cudaError_t err;
     if (e->dtype == SB_F16) {
       err = launch_conv_tc(a, e->layer_mode[i], e->has_tmap[i] ? &e->tmap[i] : nullptr,
-                           e->has_tmap[i] ? &e->tmap_y[i] : nullptr, e->n_sms, s);
+                           e->has_tmap[i] ? &e->tmap_y[i] : nullptr, e->n_sms, s, q);
     } else {
       err = launch_conv_simt(a, e->n_sms * 4, s);
     }
@@ -490,7 +503,9 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
 int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width, int block,
                  int dtype, double tau, int refresh, int dense_check_every, int flags, sb_engine** out) {
   if (!out || !layers) return fail(SB_EINVAL, "null argument");
-  if (flags & ~SB_CREATE_BLOCK_UNITS) return fail(SB_EINVAL, "unknown creation flags");
+  if (flags & ~(SB_CREATE_BLOCK_UNITS | SB_CREATE_FP8_S8)) return fail(SB_EINVAL, "unknown creation flags");
+  if ((flags & SB_CREATE_FP8_S8) && (dtype != SB_F16 || (flags & SB_CREATE_BLOCK_UNITS)))
+    return fail(SB_EINVAL, "e4m3 stride-8 caches need an fp16 engine without block units");
   *out = nullptr;
   if (n_layers < 1 || n_layers > SB_MAX_LAYERS) return fail(SB_EINVAL, "n_layers out of range");
   if (n_streams < 1 || height < 1 || width < 1) return fail(SB_EINVAL, "bad frame geometry");
@@ -567,10 +582,25 @@ int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int h
     for (int j = 0; j < e->nd; ++j)
       if (e->ds[j] == d) e->layer_di[i] = j;
   }
+  // element type of every cache: e4m3 for the outputs of the stride-8 stage when asked
+  for (int i = 0; i <= n_layers; ++i) {
+    e->cache_f8[i] = (flags & SB_CREATE_FP8_S8) && i > 0 && layers[i - 1].out_stride >= 8;
+    e->cache_esz[i] = e->cache_f8[i] ? 1 : e->esz;
+    e->act_scale[i] = 1.f;
+  }
+  for (int i = 0; i < n_layers; ++i) {
+    const sb_layer_desc& L = layers[i];
+    const bool in8 = e->cache_f8[L.src], out8 = e->cache_f8[i + 1];
+    e->layer_q[i] = in8 ? 2 : out8 ? 1 : 0;
+    if (in8 && !out8) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": e4m3 input, fp16 output"));
+    if (e->layer_q[i] && L.res >= 0 && !e->cache_f8[L.res])
+      return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": e4m3 output with an fp16 residual"));
+  }
   // device memory
   int rc;
   for (int i = 0; i <= n_layers; ++i) {
-    const size_t bytes = (size_t)e->shape[i][0] * e->shape[i][1] * e->shape[i][2] * e->shape[i][3] * e->esz;
+    const size_t bytes =
+        (size_t)e->shape[i][0] * e->shape[i][1] * e->shape[i][2] * e->shape[i][3] * e->cache_esz[i];
     if ((rc = alloc_dev(e, &e->cache[i], bytes))) return bail(rc);
   }
   e->n_chunks = (e->n_blocks + SB_LIST_CHUNK - 1) / SB_LIST_CHUNK;
@@ -592,6 +622,11 @@ int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int h
         if (m < 0) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": no block-unit tile conv"));
         e->layer_mode[i] = m;
       }
+    }
+    if (e->layer_q[i]) {
+      const int m = conv_tc_q_mode(layers[i].cin, layers[i].cout, e->layer_t[i], layers[i].stride, e->layer_q[i]);
+      if (m < 0) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": no e4m3 tile conv for its shape"));
+      e->layer_mode[i] = m;
     }
     const int win = e->layer_mode[i] & 7;  // bit 3: CTA pairs
     if (win == 0) continue;
@@ -631,13 +666,14 @@ int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int h
   for (int i = 0; i < n_layers; ++i) {
     const sb_layer_desc& L = layers[i];
     if ((rc = alloc_dev(e, (void**)&e->bias[i], (size_t)L.cout * 4))) return bail(rc);
-    const size_t wbytes = dtype == SB_F16 ? conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[i], L.stride, e->layer_mode[i])
+    const size_t wbytes = dtype == SB_F16 ? conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[i], L.stride, e->layer_mode[i],
+                                                               e->layer_q[i])
                                           : (size_t)9 * L.cin * L.cout * 4;
     if ((rc = alloc_dev(e, &e->wdev[i], wbytes))) return bail(rc);
     if (dtype == SB_F16) {  // every fp16 layer loads its input by TMA (the first layer: window boxes)
       cudaError_t err = conv_tc_make_tmap(&e->tmap[i], e->cache[L.src], n_streams, (int)e->shape[L.src][1],
                                           (int)e->shape[L.src][2], L.cin, e->layer_t[i], L.stride,
-                                          e->layer_mode[i]);
+                                          e->layer_mode[i], e->layer_q[i] == 2 ? 2 : 0);
       if (err == cudaSuccess)
         err = conv_tc_make_tmap_out(&e->tmap_y[i], e->cache[i + 1], n_streams, (int)e->shape[i + 1][1],
                                     (int)e->shape[i + 1][2], L.cin, L.cout, e->layer_t[i], L.stride,
@@ -659,9 +695,12 @@ int sb_upload_weights(sb_engine* e, int layer, const float* w, const float* bias
   SB_CUDA(cudaMemcpy(e->bias[layer], bias, (size_t)L.cout * 4, cudaMemcpyHostToDevice));
   for (int c = 0; c < L.cout && c < 128; ++c) e->bias_h[layer][c] = bias[c];
   if (e->dtype == SB_F16) {
-    const size_t bytes = conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer]);
-    std::vector<uint16_t> img(bytes / 2);
-    conv_tc_build_wimg(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer], w, bias, img.data());
+    const int q = e->layer_q[layer];
+    const size_t bytes = conv_tc_wimg_bytes(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer], q);
+    std::vector<uint16_t> img((bytes + 1) / 2);
+    e->wscale[layer].assign(L.cout, 1.f);
+    conv_tc_build_wimg(L.cin, L.cout, e->layer_t[layer], L.stride, e->layer_mode[layer], w, bias, img.data(), q,
+                       e->wscale[layer].data());
     SB_CUDA(cudaMemcpy(e->wdev[layer], img.data(), bytes, cudaMemcpyHostToDevice));
   } else {
     SB_CUDA(cudaMemcpy(e->wdev[layer], w, (size_t)9 * L.cin * L.cout * 4, cudaMemcpyHostToDevice));
@@ -916,6 +955,33 @@ int sb_debug_withhold_lookback(sb_engine* e, int withhold_chunk, int spin_limit)
   return SB_OK;
 }
 
+int sb_cache_dtype(sb_engine* e, int cache_id, int* dtype, float* scale) {
+  if (!e || !dtype) return fail(SB_EINVAL, "null argument");
+  if (cache_id < 0 || cache_id > e->n_layers) return fail(SB_EINVAL, "cache id out of range");
+  *dtype = e->cache_f8[cache_id] ? SB_F8 : e->dtype;
+  if (scale) *scale = e->act_scale[cache_id];
+  return SB_OK;
+}
+
+int sb_set_act_scale(sb_engine* e, int cache_id, float scale) {
+  if (!e) return fail(SB_EINVAL, "null engine");
+  if (cache_id < 0 || cache_id > e->n_layers || !e->cache_f8[cache_id])
+    return fail(SB_EINVAL, "not an e4m3 cache");
+  if (!(scale > 0.f) || !std::isfinite(scale)) return fail(SB_EINVAL, "scale must be positive and finite");
+  drop_graphs(e);  // the scales are kernel arguments
+  e->act_scale[cache_id] = scale;
+  return SB_OK;
+}
+
+int sb_layer_wscale(sb_engine* e, int layer, float* out, int n) {
+  if (!e || !out) return fail(SB_EINVAL, "null argument");
+  if (layer < 0 || layer >= e->n_layers) return fail(SB_EINVAL, "layer out of range");
+  if (e->layer_q[layer] != 2) return fail(SB_EINVAL, "layer has no e4m3 weights");
+  if (n < (int)e->wscale[layer].size()) return fail(SB_EINVAL, "output too small");
+  std::memcpy(out, e->wscale[layer].data(), e->wscale[layer].size() * 4);
+  return SB_OK;
+}
+
 int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]) {
   if (!e || !ptr) return fail(SB_EINVAL, "null argument");
   if (cache_id < 0 || cache_id > e->n_layers) return fail(SB_EINVAL, "cache id out of range");
@@ -928,7 +994,7 @@ int sb_cache_ptr(sb_engine* e, int cache_id, void** ptr, int64_t shape[4]) {
 int sb_layer_variant(sb_engine* e, int layer, int* mode) {
   if (!e || !mode) return fail(SB_EINVAL, "null argument");
   if (layer < 0 || layer >= e->n_layers) return fail(SB_EINVAL, "layer out of range");
-  *mode = e->dtype == SB_F16 ? e->layer_mode[layer] : -1;
+  *mode = e->dtype == SB_F16 ? e->layer_mode[layer] | (e->layer_q[layer] << 4) : -1;
   return SB_OK;
 }
 

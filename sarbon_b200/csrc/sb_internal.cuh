@@ -126,6 +126,11 @@ struct ConvArgs {
   // bias by value (kernel parameter space): epilogue reads are warp-uniform and go through
   // the constant cache, off the shared-memory path the tensor pipe saturates
   alignas(16) float bias_v[128];
+  // e4m3 caches (Q > 0 variants): per output channel s_in * s_w[c] (Q = 2), the residual
+  // cache's activation scale and 1 / the output cache's activation scale
+  alignas(16) float dq_v[128];
+  float res_scale;
+  float out_inv_scale;
 };
 
 // ---------------------------------------------------------------- launchers
@@ -141,6 +146,9 @@ cudaError_t launch_cell_masks(const uint8_t* cells, int n, int hc, int wc, int k
 
 // fp16 tcgen05 path.  Returns cudaErrorInvalidValue for shapes without an instantiation.
 bool conv_tc_supported(int cin, int cout, int t, int s);  // some mode exists for the shape
+// the e4m3 variant of a layer: q = 1 (fp16 input, e4m3 output) or 2 (e4m3 input, weights,
+// residual and output); returns its mode, or -1 when the shape has none
+int conv_tc_q_mode(int cin, int cout, int t, int s, int q);
 // mode the engine runs a layer with: window mode 0 per-tap im2col (or first-layer gather),
 // 1 per-ky row windows over (8/t)x1-block regions, 3 full windows over (8/t)x(16/t)
 // regions; plus 8 when 2-CTA clusters run M=256 cta_group::2 MMAs
@@ -148,18 +156,20 @@ int conv_tc_pick_mode(int cin, int cout, int t, int s);
 // a mode whose units are single blocks (window mode 0, or a window mode whose region is one
 // block), CTA pairs preferred; -1 when the shape has none
 int conv_tc_block_mode(int cin, int cout, int t, int s);
-int conv_tc_nsplit(int cin, int cout, int t, int s, int mode);   // CTA splits of cout
-size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode);  // all splits
+int conv_tc_nsplit(int cin, int cout, int t, int s, int mode, int q = 0);   // CTA splits of cout
+size_t conv_tc_wimg_bytes(int cin, int cout, int t, int s, int mode, int q = 0);  // all splits
+// weight image (fp16 bits, or e4m3 codes for q = 2 with wscale[c] = the scale of output
+// channel c: w = code * wscale[c])
 void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* w /*[3][3][cin][cout]*/,
-                        const float* bias /*[cout]*/, uint16_t* out /* fp16 bits */);
+                        const float* bias /*[cout]*/, uint16_t* out, int q = 0, float* wscale = nullptr);
 cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, int wx, int cin, int t, int s,
-                              int mode);
+                              int mode, int q = 0);
 // the destination cache's map for the variants whose epilogue stages its output in shared
 // memory and writes it with TMA tile stores (zero-filled and unused for the others)
 cudaError_t conv_tc_make_tmap_out(CUtensorMap* map, void* dst, int n, int ho, int wo, int cin, int cout, int t, int s,
                                   int mode);
 cudaError_t launch_conv_tc(const ConvArgs& a, int mode, const CUtensorMap* map, const CUtensorMap* map_y, int grid_x,
-                           cudaStream_t s);
+                           cudaStream_t s, int q = 0);
 int conv_tc_max_ctas_per_sm(int cin, int cout, int t, int s, int mode);
 
 // uint8 BGR frames at camera size -> bilinear resize (align_corners=False) -> RGB,

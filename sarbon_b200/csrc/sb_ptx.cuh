@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #define SB_DEV __device__ __forceinline__
 
@@ -278,6 +279,26 @@ SB_DEV void mma_f16_ss2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint3
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
       : "memory");
 }
+// The same with e4m3 A and B (kind::f8f6f4; format code 0 of the instruction descriptor is
+// E4M3 there), fp32 accumulate; one instruction covers K = 32 (32 bytes of each row).
+SB_DEV void mma_f8_ss2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// Two floats -> two e4m3 codes (round to nearest even, saturated to +-448), x in the low byte.
+SB_DEV uint16_t e4m3x2_of(float x, float y) {
+  return (uint16_t)__nv_cvt_float2_to_fp8x2(make_float2(x, y), __NV_SATFINITE, __NV_E4M3);
+}
+// Two e4m3 codes (low byte first) -> two floats (exact: e4m3 values are fp16 values).
+SB_DEV float2 float2_of_e4m3x2(uint16_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v, __NV_E4M3);
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
 // Arrive once on the mbarrier at shared::cluster address `bar` (this CTA's or the peer's)
 // when all prior cta_group::2 tcgen05 ops of this thread have completed.
 SB_DEV void mma_commit2(uint32_t bar) {

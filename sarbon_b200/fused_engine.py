@@ -15,6 +15,8 @@ unchanged:
   inside the step
 * added: ``block_units=True`` and ``set_m0(on, capacity)``, the M0 engine's semantics
   (``sarbon/sparse/block_sparse.py:196-295``) on this engine
+* added: ``fp8=True``: e4m3 caches and weights in the stride-8 stage (``calibrate_fp8``
+  sets the activation scales; ``outputs_nchw`` dequantises)
 * attributes ``n, h, w, block, hb, wb, n_blocks, dtype, tau, refresh, layers, ds,
   outputs, cache, frames, changed, extra, masks, buckets, fallback,
   dense_check_every, dense_graph, stats``.
@@ -133,7 +135,7 @@ class FusedSparseEngine:
     MODES = _lib.MODE_NAMES
 
     def __init__(self, net, n_cams, height, width, block=32, dtype=torch.float16, tau=0.0, refresh=0,
-                 dense_check_every=4, device="cuda", block_units=False):
+                 dense_check_every=4, device="cuda", block_units=False, fp8=False):
         assert height % block == 0 and width % block == 0
         if dtype not in (torch.float16, torch.float32):
             raise ValueError("dtype must be torch.float16 or torch.float32")
@@ -147,6 +149,7 @@ class FusedSparseEngine:
             raise ValueError("the engine runs on CUDA devices only")
         if self.dev.index is None:
             self.dev = torch.device("cuda", torch.cuda.current_device())
+        self._net = net
         self.layers = fuse_layers(net)
         self.ds = sorted({self.dilation(l.radius) for l in self.layers})
         self.outputs = tuple(net.program()[1])
@@ -164,7 +167,8 @@ class FusedSparseEngine:
             check(L.sb_create_ex(descs, len(self.layers), n_cams, height, width, block,
                                  _lib.SB_F16 if dtype == torch.float16 else _lib.SB_F32, float(tau),
                                  int(refresh), int(dense_check_every),
-                                 _lib.SB_CREATE_BLOCK_UNITS if block_units else 0, C.byref(handle)), "sb_create_ex")
+                                 (_lib.SB_CREATE_BLOCK_UNITS if block_units else 0)
+                                 | (_lib.SB_CREATE_FP8_S8 if fp8 else 0), C.byref(handle)), "sb_create_ex")
         self._h = _Handle(handle.value)
         for i, l in enumerate(self.layers):
             w = np.ascontiguousarray(l.w_tile.numpy(), np.float32)
@@ -173,10 +177,17 @@ class FusedSparseEngine:
                                       b.ctypes.data_as(C.POINTER(C.c_float))), "sb_upload_weights")
         typ = "<f2" if dtype == torch.float16 else "<f4"
         self.cache = {}
+        self.fp8_caches = set()  # caches holding e4m3 codes (fp8=True: the stride-8 stage)
         for name, cid in ids.items():
             ptr, shape = C.c_void_p(), (C.c_int64 * 4)()
             check(L.sb_cache_ptr(self._h.ptr, cid, C.byref(ptr), shape), "sb_cache_ptr")
-            self.cache[name] = _view(ptr.value, list(shape), typ, self._h, self.dev)
+            dt = C.c_int()
+            check(L.sb_cache_dtype(self._h.ptr, cid, C.byref(dt), None), "sb_cache_dtype")
+            if dt.value == _lib.SB_F8:
+                self.cache[name] = _view(ptr.value, list(shape), "|u1", self._h, self.dev).view(torch.float8_e4m3fn)
+                self.fp8_caches.add(name)
+            else:
+                self.cache[name] = _view(ptr.value, list(shape), typ, self._h, self.dev)
         chg, masks, extra, nd, dl = C.c_void_p(), C.c_void_p(), C.c_void_p(), C.c_int(), (C.c_int * 4)()
         check(L.sb_gate_buffers(self._h.ptr, C.byref(chg), C.byref(masks), C.byref(extra), C.byref(nd), dl),
               "sb_gate_buffers")
@@ -249,7 +260,50 @@ class FusedSparseEngine:
         return math.ceil(radius / self.block)
 
     def outputs_nchw(self):
-        return [self.cache[o].permute(0, 3, 1, 2) for o in self.outputs]
+        """p4, p8 as NCHW views of the caches; an e4m3 cache is returned dequantised (a new
+        fp16 tensor: code * its activation scale)."""
+        return [self.dequantized(o).permute(0, 3, 1, 2) for o in self.outputs]
+
+    def act_scale(self, name):
+        """Activation scale of an e4m3 cache (value = code * scale)."""
+        dt, sc = C.c_int(), C.c_float()
+        check(lib().sb_cache_dtype(self._h.ptr, self._ids[name], C.byref(dt), C.byref(sc)), "sb_cache_dtype")
+        return float(sc.value)
+
+    def set_act_scale(self, name, scale):
+        """Activation scale of the e4m3 cache `name` for the next steps."""
+        check(lib().sb_set_act_scale(self._h.ptr, self._ids[name], float(scale)), "sb_set_act_scale")
+
+    def dequantized(self, name):
+        """Cache `name` in the engine dtype: itself, or for an e4m3 cache code * scale."""
+        c = self.cache[name]
+        if name not in self.fp8_caches:
+            return c
+        return c.to(self.dtype) * self.act_scale(name)
+
+    def weight_scales(self, layer):
+        """Per-output-channel scales of layer `layer`'s e4m3 weights (fp8 engines)."""
+        n = self.layers[layer].w_tile.shape[3]
+        out = (C.c_float * n)()
+        check(lib().sb_layer_wscale(self._h.ptr, int(layer), out, n), "sb_layer_wscale")
+        return np.array(list(out), np.float32)
+
+    @torch.no_grad()
+    def calibrate_fp8(self, frames, net=None, headroom=2.0):
+        """Activation scales of the e4m3 caches from a dense fp16 pass over `frames`:
+        scale = the power of two at or above headroom * max|activation| / 448 (so that
+        scaling is exact and a value `headroom` times the largest seen still fits e4m3).
+        `net` is the stem the engine was built from (default: the one it was given)."""
+        ref = FusedSparseEngine(net if net is not None else self._net, self.n, self.h, self.w, block=self.block,
+                                dtype=torch.float16, device=self.dev)
+        ref.reset(frames.to(torch.float16))
+        out = {}
+        for name in sorted(self.fp8_caches):
+            amax = float(ref.cache[name].float().abs().max())
+            sc = 2.0 ** math.ceil(math.log2(max(headroom * amax / 448.0, 2.0 ** -30)))
+            self.set_act_scale(name, sc)
+            out[name] = sc
+        return out
 
     def _bucket(self, k):
         """fused_engine.py:188-193 (used by calibrate)."""
@@ -402,7 +456,8 @@ class FusedSparseEngine:
 
     def layer_variants(self):
         """Per layer, the tile-conv variant it runs: window mode (0 per-tap boxes / first-layer
-        gather, 1 row, 2 strided, 3 full windows) + 8 for CTA pairs; -1 on fp32 engines."""
+        gather, 1 row, 2 strided, 3 full windows) + 8 for CTA pairs + 16 * its e4m3 mode (1:
+        e4m3 output, 2: e4m3 input and output); -1 on fp32 engines."""
         out = []
         for i in range(len(self.layers)):
             m = C.c_int()
