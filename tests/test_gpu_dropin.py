@@ -55,7 +55,9 @@ def test_sarbon_video_runs_on_the_b200_engine(monkeypatch):
     det = build("s", 6, halo_zero=False)
     randomize_bn(det, torch.Generator().manual_seed(1))
     video = SarbonVideo(det, n_cams=2, size=(640, 1152), device="cuda", keep_score=0.3)
-    src = scenes.Streams(2, 720, 1280, seed=71, n_rects=4)
+    # moving objects over a static background without sensor noise: at the pipeline's
+    # default tau = 0 (lossless) only the objects' blocks change
+    src = scenes.Streams(2, 720, 1280, seed=71, n_rects=4, noise=0.0)
     worst, modes = 0.0, []
     for t in range(12):
         frames = [f.flip(-1).contiguous().numpy() for f in src.next()]  # uint8 BGR, HWC
@@ -72,4 +74,4 @@ def test_sarbon_video_runs_on_the_b200_engine(monkeypatch):
     print(f"\nSarbonVideo on the B200 engine, 12 frames: max rel err of p8 vs the dense fp16 stem {worst:.1e}; "
           f"engine stats {modes[-1]}; active blocks {[round(a, 3) for a in video.stats['active_blocks']]}")
     assert worst < 2e-2
-    assert modes[-1]["sparse"] + modes[-1]["skip"] > 0
+    assert modes[-1]["sparse"] >= 6, modes[-1]
