@@ -320,6 +320,17 @@ SB_API int sb_block_lists_static(const uint8_t* changed_dev, int n_cams, int hb,
  * sb_block_lists_static.  The lists and features of such a step are invalid.  Synchronous. */
 SB_API int sb_debug_withhold_lookback(sb_engine* e, int withhold_chunk, int spin_limit);
 
+/* Multi-scale deformable attention core of the detector on the cached p8
+ * (sarbon/models/deform_attn.py:14-28, `ms_deform_attn_core`; its docstring names it as the
+ * place for a fused kernel).  value [B][S][H][D] (SB_F32 or SB_F16, S = sum of the levels'
+ * h*w, level l's rows starting after the earlier levels'), level_hw [L][2] (h, w; host
+ * memory, L <= 8), loc [B][Q][H][L][P][2] fp32 (x, y in [0, 1]), weight [B][Q][H][L][P] fp32
+ * -> out [B][Q][H*D] in the value's type: per (b, q, h) the sum over levels and points of
+ * weight * bilinear sample, sampled as grid_sample(align_corners=False, padding_mode="zeros")
+ * at grid = 2*loc - 1.  One kernel on `stream`, no allocation. */
+SB_API int sb_ms_deform_attn(const void* value, int value_dtype, int B, int S, int H, int D, const int* level_hw,
+                             int L, const float* loc, const float* weight, int Q, int P, void* out, void* stream);
+
 /* Counters (fused_engine.py:92,239) and sticky device errors (synchronises). */
 SB_API int sb_stats(sb_engine* e, void* stream, sb_stats_t* out);
 

@@ -82,6 +82,7 @@ PROTOTYPES = {
     "sb_boxes_to_block_mask": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _P, _P]),
     "sb_gate_buffers": (_I, [_P, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_I), C.POINTER(_I)]),
     "sb_debug_lists": (_I, [_P, _I, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_I64), _P]),
+    "sb_ms_deform_attn": (_I, [_P, _I, _I, _I, _I, _I, C.POINTER(_I), _I, _P, _P, _I, _I, _P, _P]),
     "sb_block_lists_static": (_I, [_P, _I, _I, _I, C.POINTER(_I), _I, _P, _P, _P, _P]),
     "sb_stats": (_I, [_P, _P, C.POINTER(Stats)]),
     "sb_last_launch_count": (_I, [_P]),
