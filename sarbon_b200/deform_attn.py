@@ -30,6 +30,11 @@ def ms_deform_attn_core(value, shapes, loc, weights):
     if value.dtype not in (torch.float16, torch.float32):
         value = value.float()
     value = value.contiguous()
+    if loc.dtype != torch.float32:
+        # the reference forms grid = 2 * loc - 1 in loc's own type (fp16 under autocast) before
+        # grid_sample; the kernel forms it in fp32 from loc, so pass the fp32 loc whose grid is
+        # exactly that rounded grid ((g + 1) / 2 and back are exact for an fp16 g)
+        loc = ((2 * loc - 1).float() + 1) / 2
     loc = loc.float().contiguous()
     weights = weights.float().contiguous()
     out = torch.empty(b, q, nh * dh, device=value.device, dtype=value.dtype)

@@ -43,6 +43,7 @@ def test_core_matches_reference(ref_deform, dtype, tol):
     value = torch.randn(b, s, nh, dh, device="cuda", generator=g).to(dtype)
     # locations mostly inside [0, 1], some outside: zero padding at the map borders
     loc = torch.rand(b, q, nh, len(shapes), npnt, 2, device="cuda", generator=g) * 1.2 - 0.1
+    loc = loc.to(dtype)  # under autocast the sampling locations come in the value's type too
     w = torch.rand(b, q, nh, len(shapes) * npnt, device="cuda", generator=g).softmax(-1)
     w = w.view(b, q, nh, len(shapes), npnt)
     ref = ref_deform.ms_deform_attn_core(value, shapes, loc, w)
