@@ -77,9 +77,9 @@ def parse():
     p.add_argument("--no-masks", action="store_true", help="skip timing the mask utility kernels")
     p.add_argument("--cell", type=int, default=0,
                    help="gate at cell level with this cell size (px; 0 = block level, the reference's rule)")
-    p.add_argument("--fp8", action="store_true",
-                   help="e4m3 caches and weights in the stride-8 stage (SB_CREATE_FP8_S8; BASELINE config 5's "
-                        "weight format)")
+    p.add_argument("--fp8", nargs="?", const="s8", default=None, choices=["s8", "all"],
+                   help="e4m3 caches and weights (BASELINE config 5's weight format): in the stride-8 stage "
+                        "(s8, SB_CREATE_FP8_S8) or in the stride-4 stage too (all)")
     p.add_argument("--cpu-seconds", type=float, default=20.0)
     p.add_argument("--no-reference-gpu", action="store_true",
                    help="skip timing the reference's own Triton engine on the GPU (rank 0, N = 1)")
@@ -508,7 +508,8 @@ def run_b200(args):
         raise SystemExit(f"--total-streams {args.total_streams} does not split evenly over {world} GPUs")
     S = len(shard_streams(job_streams(args, world), world, rank))
     H, W = args.height, args.width
-    eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev, fp8=args.fp8)
+    eng = FusedSparseEngine(net, S, H, W, dtype=torch.float16, tau=tau, device=dev,
+                            fp8={None: False, "s8": True, "all": "all"}[args.fp8])
     if args.cell:
         eng.set_cell_gating(args.cell)  # the u8 end-to-end step gates per block only
         args.no_e2e = True
@@ -591,7 +592,7 @@ def run_b200(args):
     ph_flops, nph = 0, 0
     ph_ideal_s = 0.0  # the conv FLOPs at each layer's tensor peak (e4m3 layers: twice fp16)
     peaks0, _ = load_peaks()
-    layer_peak = [peaks0["bf16_tflops"] * (2.0 if (m >> 4) == 2 else 1.0) for m in eng.layer_variants()]
+    layer_peak = [peaks0["bf16_tflops"] * (2.0 if (m >> 4) >= 2 else 1.0) for m in eng.layer_variants()]
     eng.reset(seq[0])
     for i in range(args.profile_steps):
         f = seq[1 + i % (len(seq) - 1)]
@@ -725,7 +726,8 @@ def run_b200(args):
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "strong" if args.total_streams else "weak", "vs_baseline": None,
-            "dtype": "f16 + e4m3 stride-8 stage (fp32 accumulate)" if args.fp8 else "f16 (fp32 accumulate)",
+            "dtype": {None: "f16 (fp32 accumulate)", "s8": "f16 + e4m3 stride-8 stage (fp32 accumulate)",
+                      "all": "f16 + e4m3 stride-4 and stride-8 stages (fp32 accumulate)"}[args.fp8],
             "data": "synthetic (seeded moving-rectangle camera streams, random-init Sarbon-S stem)",
             "config": {"workload": workload_name(args, world), "job_streams": job_streams(args, world),
                        "height": H, "width": W, "block": 32, "streams_per_gpu": S, "rects_per_stream": rects,

@@ -430,12 +430,13 @@ def e4m3_codes(x):
 
 
 def conv_dense_e4m3(x, w, bias, stride, act, res, s_out, w_scale=None):
-    """One layer of the e4m3 stage, densely: x and res are dequantised float inputs; with
+    """One layer of an e4m3 stage, densely: x and res are dequantised float inputs; with
     `w_scale` (per output channel) the weights are first quantised as the engine quantises
-    them, code = e4m3(w / s), value = code * s.  Returns the e4m3 codes of y / s_out."""
+    them, code = e4m3(w / s), value = code * s.  Returns the e4m3 codes of y / s_out, or with
+    s_out = None the fp32 result (for the layer whose output leaves the stage in fp16)."""
     w = np.asarray(w, np.float32)
     if w_scale is not None:
         w = e4m3(w / w_scale[None, None, None, :]) * w_scale[None, None, None, :]
     y = conv_dense(np.asarray(x, np.float32), w, bias, stride, act, None if res is None else np.asarray(res, np.float32),
                    np.float32)
-    return e4m3_codes(y / np.float32(s_out))
+    return y if s_out is None else e4m3_codes(y / np.float32(s_out))

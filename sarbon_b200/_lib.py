@@ -16,6 +16,7 @@ SB_MODE_SKIP, SB_MODE_SPARSE, SB_MODE_DENSE = 0, 1, 2
 MODE_NAMES = ("skip", "sparse", "dense")
 SB_CREATE_BLOCK_UNITS = 1
 SB_CREATE_FP8_S8 = 2
+SB_CREATE_FP8_S4 = 4
 SB_MAX_LAYERS = 32
 SB_MAX_DILATIONS = 4
 

@@ -62,10 +62,14 @@ constexpr int kMaxCout = 128;     // widest layer of the stem (ConvArgs::bias_v 
 // Q = 2: e4m3 input cache, weights (per output channel scale), residual and output caches;
 //        kind::f8f6f4 MMAs (K = 32 per instruction) and the dequantisation in the fp32 epilogue:
 //        y = acc * (s_in * s_w[c]) + bias[c] + s_res * res, ReLU, e4m3(y / s_out).
+// Q = 3: as Q = 2 with an fp16 output cache (the last layer of an e4m3 stage, whose output
+//        leaves the stage).
 template <int CIN, int NCTA, int T, int S, int WIN, int PAIR = 0, int Q = 0>
 struct TcCfg {
-  static constexpr int AE = Q == 2 ? 1 : 2;            // bytes per A / B element
-  static constexpr int OE = Q >= 1 ? 1 : 2;            // bytes per output (and residual) element
+  static constexpr bool F8IN = Q >= 2;                 // e4m3 A / B and kind::f8f6f4 MMAs
+  static constexpr int AE = F8IN ? 1 : 2;              // bytes per A / B element
+  static constexpr int OE = (Q == 1 || Q == 2) ? 1 : 2;  // bytes per output element
+  static constexpr int RE = F8IN ? 1 : 2;              // bytes per residual element
   static constexpr bool MANUAL = CIN < 16;            // gathered by threads (first layer)
   static constexpr int KPAD = MANUAL ? ((9 * CIN + 15) / 16) * 16 : 0;
   // first layer: K slots per ky (its 3*CIN (kx, c) elements rounded up to even, so that each
@@ -118,7 +122,7 @@ struct TcCfg {
   // parameters (ConvArgs::bias_v, warp-uniform constant-cache reads) -- measured faster there
   static constexpr bool BIAS_SMEM = PAIR != 0;
   // pairs: the bias, and for Q = 2 the per-channel dequantisation scales after it
-  static constexpr int BIAS_BYTES = BIAS_SMEM ? kMaxCout * 4 * (Q == 2 ? 2 : 1) : 0;
+  static constexpr int BIAS_BYTES = BIAS_SMEM ? kMaxCout * 4 * (F8IN ? 2 : 1) : 0;
   static constexpr int A_OFF = ((W_BYTES + 1023) / 1024) * 1024;
   // Epilogue output through shared memory: each epilogue warp writes its 32 output pixels
   // (NCOL channels each) into its own staging buffer and stores them with one TMA tile
@@ -182,12 +186,12 @@ struct TcCfg {
   static_assert(!PAIR || !MANUAL, "CTA pairs need TMA-loaded A stages");
   static_assert(!MANUAL || KPAD <= 64, "first-layer K too large");
   static_assert(Q == 0 || (PAIR && !MANUAL), "e4m3 caches: CTA-pair layers only");
-  static_assert(Q != 2 || (WIN == 1 && ROWB == 128), "e4m3 inputs: row windows over 128-byte pixel rows");
+  static_assert(!F8IN || (WIN == 1 && (ROWB == 128 || ROWB == 64)), "e4m3 inputs: row windows over 64/128-byte rows");
   static_assert(!MANUAL || ((NISS * SUB) % NGW == 0 && NWB % NGW == 0), "gather warp per stage / window slot");
   static_assert(!MANUAL || TT >= 128, "first layer: an M-tile must lie within one tile");
   static_assert(!MANUAL || (S == 2 && CIN <= 8 && WIN_COLS <= 256 && WIN_COLS % 2 == 0), "first-layer window box");
   static_assert(!WIN || ((((WIN == 1 || WIN == 3) && S == 1) || (WIN == 2 && S == 2 && (CIN == 32 || CIN == 64))) &&
-                         8 % T == 0 && T <= 8 && ROWB == 128 && !MANUAL),
+                         8 % T == 0 && T <= 8 && (ROWB == 128 || (F8IN && ROWB == 64)) && !MANUAL),
                 "window mode geometry");
 };
 
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS,
   if (C::BIAS_SMEM)
     for (int i = threadIdx.x; i < a.cout; i += blockDim.x) {
       sBias[i] = a.bias_v[i];
-      if (Q == 2) sBias[kMaxCout + i] = a.dq_v[i];
+      if (C::F8IN) sBias[kMaxCout + i] = a.dq_v[i];
     }
   if (!C::MANUAL && warp == C::PROD_WARP && lane == 0) prefetch_tmap(&tmap);
   if (C::TSTORE && warp == 0 && lane == 0) prefetch_tmap(&tmap_y);
@@ -670,7 +674,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS,
                     const int wk = C::NBOX == 2 ? kb * 3 + (kx == 0 ? 0 : kx == 1 ? 2 : 1)
                                    : WIN == 2 ? kb * 2 + kx : ((ky0 + dy) * 3 + kx) * C::NCH + ch;
                     const uint32_t b_off = wk * C::B_KB + kk * 32;
-                    if (PAIR && Q == 2)
+                    if (PAIR && C::F8IN)
                       mma_f8_ss2(d_tmem, a_desc + (a_off >> 4), b_desc0 + (b_off >> 4), C::IDESC,
                                  (kb | dy | kx | kk) != 0 ? 1u : 0u);
                     else if (PAIR)
@@ -739,11 +743,11 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS,
       // this thread's output channels are the same for every item of the launch
       const int n0 = (PAIR ? 0 : ((int)blockIdx.x % (a.cout / NCTA)) * NCTA) + col0 + CPT * m;
       float bias[CPT];
-      float dq[Q == 2 ? CPT : 1];  // e4m3 inputs: s_in * s_w[c] of each channel
+      float dq[C::F8IN ? CPT : 1];  // e4m3 inputs: s_in * s_w[c] of each channel
 #pragma unroll
       for (int t = 0; t < CPT; ++t) {
         bias[t] = C::BIAS_SMEM ? sBias[n0 + t] : a.bias_v[n0 + t];
-        if constexpr (Q == 2) dq[t] = sBias[kMaxCout + n0 + t];
+        if constexpr (C::F8IN) dq[t] = sBias[kMaxCout + n0 + t];
       }
       const float res_scale = a.res_scale, out_inv = a.out_inv_scale;
       // Pixel sr (0..3) of this thread is accumulator row q*32 + k + 8*sr.  When a warp's 32
@@ -756,7 +760,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS,
         size_t pix[ONEUNIT ? 1 : 4];  // element of channel n0: pixel 0 (ONEUNIT) or each pixel
         int p;                        // pixel 0's index within its unit (ONEUNIT)
         unsigned okm;                 // bit sr: pixel sr is stored
-        uint4 rr[4][CPT * C::OE / 16];  // residual: CPT channels of each pixel
+        uint4 rr[4][CPT * C::RE / 16];  // residual: CPT channels of each pixel
       };
       const size_t rowstride = (size_t)a.wo * a.cout;
       // offset of pixel sr from pixel 0 (ONEUNIT): unit pixel p + 8 sr, UW pixels per row
@@ -809,8 +813,8 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS,
           const bool st = valid && inb;
           if (st) o.okm |= 1u << sr;
           if (res != nullptr) {
-            const uint8_t* rp = res + pix_of(o, sr) * C::OE;
-            if constexpr (CPT * C::OE == 32) {
+            const uint8_t* rp = res + pix_of(o, sr) * C::RE;
+            if constexpr (CPT * C::RE == 32) {
               if (st) ld_global_nc_v8(rp, o.rr[sr][0], o.rr[sr][1]);
               else o.rr[sr][0] = o.rr[sr][1] = make_uint4(0, 0, 0, 0);
             } else {
@@ -830,7 +834,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS,
 #pragma unroll
         for (int jj = 0; jj < REP; ++jj) {
           float f0, f1;
-          if constexpr (Q == 2) {  // dequantise the e4m3 x e4m3 accumulation per channel
+          if constexpr (C::F8IN) {  // dequantise the e4m3 x e4m3 accumulation per channel
             f0 = fmaf(__uint_as_float(f[4 * jj]), dq[2 * jj], bias[2 * jj]);
             f1 = fmaf(__uint_as_float(f[4 * jj + 1]), dq[2 * jj + 1], bias[2 * jj + 1]);
           } else {
@@ -838,7 +842,7 @@ __global__ void __launch_bounds__(TcCfg<CIN, NCTA, T, S, WIN, PAIR, Q>::THREADS,
             f1 = __uint_as_float(f[4 * jj + 1]) + bias[2 * jj + 1];
           }
           if (res != nullptr) {
-            if constexpr (C::OE == 1) {
+            if constexpr (C::RE == 1) {
               const float2 t2 = float2_of_e4m3x2(rw8[jj]);
               f0 = fmaf(t2.x, res_scale, f0);
               f1 = fmaf(t2.y, res_scale, f1);
@@ -1173,6 +1177,11 @@ const std::vector<Variant>& variants() {
       // e4m3 caches of the stride-8 stage: fp16 in / e4m3 out, then e4m3 in and out
       make_variant<64, 64, 4, 2, 2, 1, 1>(128),
       make_variant<128, 64, 4, 1, 1, 1, 2>(128),
+      // e4m3 caches of the stride-4 stage: t1 fp16 in / e4m3 out, the 64->64 layers e4m3 in
+      // and out (64-byte rows), the stage's last layer e4m3 in / fp16 out
+      make_variant<32, 32, 8, 2, 2, 1, 1>(64),
+      make_variant<64, 32, 8, 1, 1, 1, 2>(64),
+      make_variant<64, 32, 8, 1, 1, 1, 3>(64),
       // block 64
       make_variant<3, 32, 32, 2>(32),
       make_variant<32, 64, 16, 2>(64),
@@ -1286,7 +1295,7 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* 
                         uint16_t* out, int q, float* wscale) {
   const Variant* v = picked(cin, cout, t, s, mode, q);
   if (!v) return;
-  if (q == 2) {
+  if (q >= 2) {
     // e4m3 codes, one scale per output channel: wscale[c] = max |w[., ., ., c]| / 448 (the
     // largest e4m3 magnitude), code = e4m3(w / wscale[c]) rounded to nearest even.  Layout
     // as the fp16 image (tap-major K-blocks of ch input channels, one 128-byte row per
@@ -1311,7 +1320,7 @@ void conv_tc_build_wimg(int cin, int cout, int t, int s, int mode, const float* 
             const int tap = kb / nch, ci = (kb % nch) * ch + k;
             const float val = w[((size_t)tap * cin + ci) * cout + co] / sc[co];
             const int qq = k / 16, within = k % 16;
-            const int pq = qq ^ (n & 7);
+            const int pq = rowb == 128 ? (qq ^ (n & 7)) : (qq ^ ((n >> 1) & 3));
             img[(size_t)kb * ncta * rowb + (size_t)n * rowb + pq * 16 + within] =
                 (uint8_t)__nv_cvt_float_to_fp8(val, __NV_SATFINITE, __NV_E4M3);
           }
@@ -1407,9 +1416,9 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
                               int mode, int q) {
   const Variant* v = nullptr;
   for (const auto& c : variants())
-    if (c.cin == cin && c.t == t && c.s == s && c.win == (mode & 7) && (q == 2) == (c.q == 2)) { v = &c; break; }
+    if (c.cin == cin && c.t == t && c.s == s && c.win == (mode & 7) && (q >= 2) == (c.q >= 2)) { v = &c; break; }
   if (!v) return cudaErrorInvalidValue;
-  if (q == 2) {
+  if (q >= 2) {
     // e4m3 cache [n][hx][wx][cin] bytes, row windows: 10 px x t rows of ch channels per box
     PFN_encodeTiled enc = get_encode();
     if (!enc) return cudaErrorNotSupported;
@@ -1418,8 +1427,9 @@ cudaError_t conv_tc_make_tmap(CUtensorMap* map, const void* src, int n, int hx, 
     cuuint32_t box[4] = {(cuuint32_t)v->ch, 10u, (cuuint32_t)v->box_rows, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(src), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     v->ch == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
   }
   const bool win = v->win != 0;

@@ -273,7 +273,7 @@ int launch_convs(sb_engine* e, cudaStream_t s, int first = 0, int last = -1) {
     std::memcpy(a.bias_v, e->bias_h[i], sizeof(a.bias_v));
     const int q = e->layer_q[i];
     for (int c = 0; c < 128; ++c)
-      a.dq_v[c] = q == 2 && c < L.cout ? e->act_scale[L.src] * e->wscale[i][c] : 1.f;
+      a.dq_v[c] = q >= 2 && c < L.cout ? e->act_scale[L.src] * e->wscale[i][c] : 1.f;
     a.res_scale = L.res >= 0 && e->cache_f8[L.res] ? e->act_scale[L.res] : 1.f;
     a.out_inv_scale = e->cache_f8[i + 1] ? 1.f / e->act_scale[i + 1] : 1.f;
     a.wimg = e->wdev[i];
@@ -503,9 +503,10 @@ int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, int heig
 int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int height, int width, int block,
                  int dtype, double tau, int refresh, int dense_check_every, int flags, sb_engine** out) {
   if (!out || !layers) return fail(SB_EINVAL, "null argument");
-  if (flags & ~(SB_CREATE_BLOCK_UNITS | SB_CREATE_FP8_S8)) return fail(SB_EINVAL, "unknown creation flags");
-  if ((flags & SB_CREATE_FP8_S8) && (dtype != SB_F16 || (flags & SB_CREATE_BLOCK_UNITS)))
-    return fail(SB_EINVAL, "e4m3 stride-8 caches need an fp16 engine without block units");
+  if (flags & ~(SB_CREATE_BLOCK_UNITS | SB_CREATE_FP8_S8 | SB_CREATE_FP8_S4))
+    return fail(SB_EINVAL, "unknown creation flags");
+  if ((flags & (SB_CREATE_FP8_S8 | SB_CREATE_FP8_S4)) && (dtype != SB_F16 || (flags & SB_CREATE_BLOCK_UNITS)))
+    return fail(SB_EINVAL, "e4m3 caches need an fp16 engine without block units");
   *out = nullptr;
   if (n_layers < 1 || n_layers > SB_MAX_LAYERS) return fail(SB_EINVAL, "n_layers out of range");
   if (n_streams < 1 || height < 1 || width < 1) return fail(SB_EINVAL, "bad frame geometry");
@@ -583,18 +584,23 @@ int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int h
       if (e->ds[j] == d) e->layer_di[i] = j;
   }
   // element type of every cache: e4m3 for the outputs of the stride-8 stage when asked
+  // the stride-4 stage's last cache (its output, p4) stays fp16
+  int last_s4 = -1;
+  for (int i = 0; i < n_layers; ++i)
+    if (layers[i].out_stride == 4) last_s4 = i;
   for (int i = 0; i <= n_layers; ++i) {
-    e->cache_f8[i] = (flags & SB_CREATE_FP8_S8) && i > 0 && layers[i - 1].out_stride >= 8;
+    const int os = i > 0 ? layers[i - 1].out_stride : 1;
+    e->cache_f8[i] = i > 0 && (((flags & SB_CREATE_FP8_S8) && os >= 8) ||
+                               ((flags & SB_CREATE_FP8_S4) && os == 4 && i - 1 != last_s4));
     e->cache_esz[i] = e->cache_f8[i] ? 1 : e->esz;
     e->act_scale[i] = 1.f;
   }
   for (int i = 0; i < n_layers; ++i) {
     const sb_layer_desc& L = layers[i];
     const bool in8 = e->cache_f8[L.src], out8 = e->cache_f8[i + 1];
-    e->layer_q[i] = in8 ? 2 : out8 ? 1 : 0;
-    if (in8 && !out8) return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": e4m3 input, fp16 output"));
-    if (e->layer_q[i] && L.res >= 0 && !e->cache_f8[L.res])
-      return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": e4m3 output with an fp16 residual"));
+    e->layer_q[i] = in8 ? (out8 ? 2 : 3) : (out8 ? 1 : 0);
+    if (L.res >= 0 && e->cache_f8[L.res] != in8)
+      return bail(fail(SB_EINVAL, "layer " + std::to_string(i) + ": the residual's type differs from the input's"));
   }
   // device memory
   int rc;
@@ -673,7 +679,7 @@ int sb_create_ex(const sb_layer_desc* layers, int n_layers, int n_streams, int h
     if (dtype == SB_F16) {  // every fp16 layer loads its input by TMA (the first layer: window boxes)
       cudaError_t err = conv_tc_make_tmap(&e->tmap[i], e->cache[L.src], n_streams, (int)e->shape[L.src][1],
                                           (int)e->shape[L.src][2], L.cin, e->layer_t[i], L.stride,
-                                          e->layer_mode[i], e->layer_q[i] == 2 ? 2 : 0);
+                                          e->layer_mode[i], e->layer_q[i] >= 2 ? 2 : 0);
       if (err == cudaSuccess)
         err = conv_tc_make_tmap_out(&e->tmap_y[i], e->cache[i + 1], n_streams, (int)e->shape[i + 1][1],
                                     (int)e->shape[i + 1][2], L.cin, L.cout, e->layer_t[i], L.stride,
@@ -976,7 +982,7 @@ int sb_set_act_scale(sb_engine* e, int cache_id, float scale) {
 int sb_layer_wscale(sb_engine* e, int layer, float* out, int n) {
   if (!e || !out) return fail(SB_EINVAL, "null argument");
   if (layer < 0 || layer >= e->n_layers) return fail(SB_EINVAL, "layer out of range");
-  if (e->layer_q[layer] != 2) return fail(SB_EINVAL, "layer has no e4m3 weights");
+  if (e->layer_q[layer] < 2) return fail(SB_EINVAL, "layer has no e4m3 weights");
   if (n < (int)e->wscale[layer].size()) return fail(SB_EINVAL, "output too small");
   std::memcpy(out, e->wscale[layer].data(), e->wscale[layer].size() * 4);
   return SB_OK;

@@ -15,8 +15,9 @@ unchanged:
   inside the step
 * added: ``block_units=True`` and ``set_m0(on, capacity)``, the M0 engine's semantics
   (``sarbon/sparse/block_sparse.py:196-295``) on this engine
-* added: ``fp8=True``: e4m3 caches and weights in the stride-8 stage (``calibrate_fp8``
-  sets the activation scales; ``outputs_nchw`` dequantises)
+* added: ``fp8=True``: e4m3 caches and weights in the stride-8 stage, ``fp8="all"`` in the
+  stride-4 stage too (p4 stays fp16); ``calibrate_fp8`` sets the activation scales,
+  ``outputs_nchw`` dequantises
 * attributes ``n, h, w, block, hb, wb, n_blocks, dtype, tau, refresh, layers, ds,
   outputs, cache, frames, changed, extra, masks, buckets, fallback,
   dense_check_every, dense_graph, stats``.
@@ -168,7 +169,8 @@ class FusedSparseEngine:
                                  _lib.SB_F16 if dtype == torch.float16 else _lib.SB_F32, float(tau),
                                  int(refresh), int(dense_check_every),
                                  (_lib.SB_CREATE_BLOCK_UNITS if block_units else 0)
-                                 | (_lib.SB_CREATE_FP8_S8 if fp8 else 0), C.byref(handle)), "sb_create_ex")
+                                 | (_lib.SB_CREATE_FP8_S8 if fp8 else 0)
+                                 | (_lib.SB_CREATE_FP8_S4 if fp8 == "all" else 0), C.byref(handle)), "sb_create_ex")
         self._h = _Handle(handle.value)
         for i, l in enumerate(self.layers):
             w = np.ascontiguousarray(l.w_tile.numpy(), np.float32)
