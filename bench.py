@@ -103,12 +103,23 @@ def pingpong(n):
 
 
 # DRAM bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum) of one capture of
-# the default workload (16 streams x 1920x1088, ~5 % changed blocks); they describe the
-# kernels as they were at that capture, named in "capture".  None: not captured.
-TRAFFIC = {"conv": 71.9e6, "gate": 419.0e6,
+# the default workload (16 streams x 1920x1088, ~5 % changed blocks) per cache format (key:
+# the --fp8 choice); they describe the kernels as they were at that capture, named in
+# "capture".  None: not captured.
+TRAFFIC = {
+    None: {"conv": 71.9e6, "gate": 419.0e6,
            "capture": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, 16 streams x "
                       "1920x1088 (--frames 4), two timed steps, commit fc1b017: conv = the mean over "
-                      "its 22 launches, gate = the mean over 2"}
+                      "its 22 launches, gate = the mean over 2"},
+    "s8": {"conv": 68.4e6, "gate": 419.7e6,
+           "capture": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, 16 streams x "
+                      "1920x1088 (--frames 4, --fp8 s8), one sparse step of the profile pass, commit "
+                      "534d084: conv = the mean over its 11 launches, gate = the mean over 2"},
+    "all": {"conv": 51.2e6, "gate": 419.7e6,
+            "capture": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, 16 streams x "
+                       "1920x1088 (--frames 4, --fp8 all), one sparse step of the profile pass, commit "
+                       "534d084: conv = the mean over its 11 launches, gate = the mean over 2"},
+}
 
 
 def load_peaks():
@@ -607,7 +618,7 @@ def run_b200(args):
         nph += 1
     peaks, src = load_peaks()
     default_workload = (S, H, W) == (16, 1088, 1920) and not args.cell
-    traffic = TRAFFIC if default_workload else {"conv": None, "gate": None, "capture": None}
+    traffic = TRAFFIC[args.fp8] if default_workload else {"conv": None, "gate": None, "capture": None}
     n_conv = nprof * len(eng.layers)
     conv_tflops = conv_flops / (prof["conv"] * 1e-3) / 1e12
     pipe_tflops = ph_flops / (ph["conv"] * 1e-3) / 1e12
