@@ -335,6 +335,118 @@ SB_API int sb_debug_withhold_lookback(sb_engine* e, int withhold_chunk, int spin
 SB_API int sb_ms_deform_attn(const void* value, int value_dtype, int B, int S, int H, int D, const int* level_hw,
                              int L, const float* loc, const float* weight, int Q, int P, void* out, void* stream);
 
+/* ---------------------------------------------------------------- detector kernels
+ * The detector after the stem (sarbon/models/sarbon_det.py:118-356) runs on these entry
+ * points; each is one kernel on `stream`, allocates nothing and may be captured in a CUDA
+ * graph (after a first call outside capture on the device). */
+
+/* One NHWC fp16 source of sb_gemm_conv: element (b, y, x, c) at
+ * ptr[((b * img_stride) + y * W + x) * ld + c], c < C. */
+typedef struct {
+  const void* ptr;       /* 16-byte aligned */
+  int C;                 /* channels read, a multiple of 64 */
+  long long ld;          /* elements between pixels (>= C, a multiple of 8) */
+  long long img_stride;  /* pixels between images (>= H * W) */
+} sb_gemm_src;
+
+/* Every nn.Linear / nn.Conv2d of the detector as one tcgen05 implicit GEMM with its
+ * epilogue (under the reference's autocast each is an fp16 product with fp32 accumulation;
+ * sarbon_det.py:118-171,294-356, deform_attn.py:57-66):
+ *   out[b, yo, xo, n] = act(sum_{tap, c} src[b, yo*stride + ky - pad, xo*stride + kx - pad, c]
+ *                                     * weight[n][tap * Ctot + c] + bias[n] + res[b, yo, xo, n])
+ * over nsrc (1 or 2) sources of B x H x W pixels whose channels are concatenated (Ctot =
+ * sum of C; torch.cat([a, b], 1)), taps = 1 (stride 1, pad 0) or 9 (3x3, pad 1, stride 1
+ * or 2; tap = ky * 3 + kx); out-of-map pixels read as zero.  weight: fp16 [N][taps * Ctot]
+ * row-major (16-byte aligned).  bias: fp32 [N] or NULL.  act: 0 none, 1 ReLU, 2 GELU (erf).
+ * res (NULL for none) and out: rows of res_dtype / out_dtype (SB_F16 or SB_F32), element
+ * (b, yo, xo, n) at [(b * img + yo * Wo + xo) * ld + n] (ld >= N; rows of a multiple of 16
+ * bytes on a 16-byte aligned base take vector accesses, others element accesses).  A linear
+ * layer over a [rows][C] matrix is B = 1, H = 1, W = rows. */
+SB_API int sb_gemm_conv(const sb_gemm_src* src, int nsrc, int B, int H, int W, int taps, int stride,
+                        const void* weight, int N, const float* bias, int act, const void* res, int res_dtype,
+                        long long res_ld, long long res_img, void* out, int out_dtype, long long out_ld,
+                        long long out_img, void* stream);
+
+/* Sticky error flags (SB_ERR_* bits of the bounded waits) of the detector kernels; clear != 0
+ * resets them.  Synchronous. */
+SB_API int sb_kernels_error(int clear, int* flags);
+
+/* In the functions below a "row" argument is a matrix of rows `ld` elements apart; *_dtype
+ * is SB_F16 or SB_F32. */
+
+/* nn.LayerNorm (sarbon_det.py:150,171,317 under autocast: fp32 statistics and output) of
+ * the rows of a (+ b if non-NULL), D channels (32 <= D <= 1024, D % 32 == 0), eps; writes
+ * any of y32 (fp32), y16 (fp16) and yp16 = fp16(y + sign * pos[row % period]) (pos fp16:
+ * the decoder's `tgt + pos` query :169-170, the encoder's `aifi(t + pos) - pos` :146).  The
+ * sum a + b of two fp16 operands is rounded to fp16 first (it is an fp16 tensor there). */
+SB_API int sb_layernorm(const void* a, int a_dtype, long long lda, const void* b, int b_dtype, long long ldb,
+                        const float* gamma, const float* beta, float eps, int rows, int D, float* y32, long long ld32,
+                        void* y16, long long ld16, const void* pos, long long ldpos, int period, float sign, void* yp16,
+                        long long ldp, void* stream);
+
+/* out (fp16 rows) = fp16(a + sign * b[row % period]) over rows x D. */
+SB_API int sb_add_rows(const void* a, int a_dtype, long long lda, const void* b, int b_dtype, long long ldb, int period,
+                       float sign, int rows, int D, void* out, long long ldo, void* stream);
+
+/* Depthwise 3x3 conv, padding 1, + bias (BatchNorm folded into w [9][C] fp32 and bias [C])
+ * + ReLU if relu, on NHWC fp16 maps (x: pixels ldx elements apart, images imgx pixels
+ * apart; C and the lds multiples of 8) -- fuse()'s depthwise half, sarbon_det.py:73-77. */
+SB_API int sb_dwconv3x3(const void* x, long long ldx, long long imgx, int B, int H, int W, int C, const float* w,
+                        const float* bias, int relu, void* y, long long ldy, long long imgy, void* stream);
+
+/* Nearest 2x upsampling of an NHWC fp16 map B x H x W x C into B x 2H x 2W x C
+ * (F.interpolate(scale_factor=2.0), sarbon_det.py:147-148). */
+SB_API int sb_upsample2x(const void* x, long long ldx, long long imgx, int B, int H, int W, int C, void* y,
+                         long long ldy, long long imgy, void* stream);
+
+/* Multi-head attention core softmax(q k^T / sqrt(dh)) v, H heads of dh = 32 channels (head h
+ * = columns 32h..32h+31), Tq queries and Tk keys per image, fp16 rows (16-byte aligned,
+ * rows apart by ld, images by img rows), fp32 softmax -- the attention of the encoder's
+ * nn.TransformerEncoderLayer and the decoder's nn.MultiheadAttention (sarbon_det.py:129,160). */
+SB_API int sb_attention(const void* q, long long ldq, long long imgq, const void* k, long long ldk, long long imgk,
+                        const void* v, long long ldv, long long imgv, int B, int H, int dh, int Tq, int Tk, void* out,
+                        long long ldo, long long imgo, void* stream);
+
+/* Query selection (sarbon_det.py:314): per image, the K (<= 1024) rows of the S (<= 65536)
+ * rows of fp16 logits [rows][C] (image b's rows start at b * img) with the largest
+ * max-over-classes value, rows with valid[row] == 0 excluded (valid may be NULL); int32
+ * row indices idx[b * ldi + i], ordered by value (descending), equal values by row. */
+SB_API int sb_topk_rows(const void* logits, long long ld, long long img, int B, int S, int C, const void* valid, int K,
+                        void* idx, long long ldi, void* stream);
+
+/* out[b][i] = src[b][idx[b * ldi + i]] over D columns (sarbon_det.py:315-320); fp32 (o32)
+ * and/or fp16 (o16) outputs. */
+SB_API int sb_gather_rows(const void* src, int src_dtype, long long lds, long long imgs, const void* idx, long long ldi,
+                          int B, int K, int D, float* o32, long long ld32, long long img32, void* o16, long long ld16,
+                          long long img16, void* stream);
+
+/* MSDeformAttn after its three projections (deform_attn.py:57-66 and the core :14-28):
+ * value fp16 [B][S][H*32] (L levels of level_hw[l] = (h, w), host memory), sampling offsets
+ * fp16 [B][Q][H*L*P*2], attention logits fp16 [B][Q][H*L*P], reference boxes cxcywh [B][Q][4]
+ * (ref_dtype: SB_F16 evaluates the location expression with fp16 roundings, as the
+ * reference does for an fp16 box); writes fp16 [B][Q][H*32]. */
+SB_API int sb_deform_sample(const void* value, long long ldv, long long imgv, const int* level_hw, int L, const void* off,
+                            long long ldoff, long long imgoff, const void* att, long long ldatt, long long imgatt,
+                            const void* ref, int ref_dtype, long long ldref, long long imgref, int B, int Q, int H, int P,
+                            void* out, long long ldo, long long imgo, void* stream);
+
+/* Encoder proposals of the selected rows (sarbon_det.py:316-321): ref16 [B*K][4] =
+ * fp16(sigmoid(fp16(encbox + anchors[idx]))) (anchors fp16 [S][4]); qin [B*K][ldq] gets the
+ * same 4 values (the query_pos input). */
+SB_API int sb_box_enc(const void* encbox, long long ldb, const void* anchors, const void* idx, int B, int K, void* ref16,
+                      void* qin, long long ldq, void* stream);
+
+/* Decoder box of one layer (sarbon_det.py:336-350, box_ops.py:78-106): first != 0 computes
+ * ref_init = sigmoid(prebox + inverse_sigmoid(ref16)) and corners = head, else corners =
+ * fp16(head + corners); then box [rows][4] = distance2bbox(ref_init, integral(corners),
+ * reg_scale) with R1 bins per edge (project[R1] fp32), and qin = fp16(box) if non-NULL. */
+SB_API int sb_box_dec(int first, const void* prebox, long long ldp, const void* ref16, const void* head, long long ldh,
+                      void* corners, long long ldc, int R1, const float* project, float reg_scale, float* ref_init,
+                      float* box, void* qin, long long ldq, int rows, void* stream);
+
+/* F.normalize(x.float(), dim=-1) of fp16 rows into fp32 rows (sarbon_det.py:359-360). */
+SB_API int sb_l2norm_rows(const void* x, long long ldx, int rows, int D, float* out, long long ldo, void* stream);
+
 /* Counters (fused_engine.py:92,239) and sticky device errors (synchronises). */
 SB_API int sb_stats(sb_engine* e, void* stream, sb_stats_t* out);
 

@@ -32,6 +32,11 @@ class SarbonLibraryError(RuntimeError):
         self.status = status
 
 
+class GemmSrc(C.Structure):
+    """sb_gemm_src: one NHWC fp16 source of sb_gemm_conv."""
+    _fields_ = [("ptr", C.c_void_p), ("C", C.c_int), ("ld", C.c_longlong), ("img_stride", C.c_longlong)]
+
+
 class LayerDesc(C.Structure):
     _fields_ = [("src", C.c_int32), ("res", C.c_int32), ("cin", C.c_int32), ("cout", C.c_int32),
                 ("stride", C.c_int32), ("out_stride", C.c_int32), ("radius", C.c_int32),
@@ -48,6 +53,7 @@ class Stats(C.Structure):
 _P = C.c_void_p
 _I = C.c_int
 _I64 = C.c_int64
+_LL = C.c_longlong
 # name -> (restype, argtypes); every symbol declared in include/sarbon_sparse.h
 PROTOTYPES = {
     "sb_create": (_I, [C.POINTER(LayerDesc), _I, _I, _I, _I, _I, _I, C.c_double, _I, _I, C.POINTER(_P)]),
@@ -85,6 +91,22 @@ PROTOTYPES = {
     "sb_debug_lists": (_I, [_P, _I, C.POINTER(_P), C.POINTER(_P), C.POINTER(_P), C.POINTER(_I64), _P]),
     "sb_ms_deform_attn": (_I, [_P, _I, _I, _I, _I, _I, C.POINTER(_I), _I, _P, _P, _I, _I, _P, _P]),
     "sb_block_lists_static": (_I, [_P, _I, _I, _I, C.POINTER(_I), _I, _P, _P, _P, _P]),
+    "sb_gemm_conv": (_I, [C.POINTER(GemmSrc), _I, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _I,
+                          C.c_longlong, C.c_longlong, _P, _I, C.c_longlong, C.c_longlong, _P]),
+    "sb_kernels_error": (_I, [_I, C.POINTER(_I)]),
+    "sb_layernorm": (_I, [_P, _I, _LL, _P, _I, _LL, _P, _P, C.c_float, _I, _I, _P, _LL, _P, _LL, _P, _LL, _I, C.c_float,
+                          _P, _LL, _P]),
+    "sb_add_rows": (_I, [_P, _I, _LL, _P, _I, _LL, _I, C.c_float, _I, _I, _P, _LL, _P]),
+    "sb_dwconv3x3": (_I, [_P, _LL, _LL, _I, _I, _I, _I, _P, _P, _I, _P, _LL, _LL, _P]),
+    "sb_upsample2x": (_I, [_P, _LL, _LL, _I, _I, _I, _I, _P, _LL, _LL, _P]),
+    "sb_attention": (_I, [_P, _LL, _LL, _P, _LL, _LL, _P, _LL, _LL, _I, _I, _I, _I, _I, _P, _LL, _LL, _P]),
+    "sb_topk_rows": (_I, [_P, _LL, _LL, _I, _I, _I, _P, _I, _P, _LL, _P]),
+    "sb_gather_rows": (_I, [_P, _I, _LL, _LL, _P, _LL, _I, _I, _I, _P, _LL, _LL, _P, _LL, _LL, _P]),
+    "sb_deform_sample": (_I, [_P, _LL, _LL, C.POINTER(_I), _I, _P, _LL, _LL, _P, _LL, _LL, _P, _I, _LL, _LL, _I, _I, _I,
+                              _I, _P, _LL, _LL, _P]),
+    "sb_box_enc": (_I, [_P, _LL, _P, _P, _I, _I, _P, _P, _LL, _P]),
+    "sb_box_dec": (_I, [_I, _P, _LL, _P, _P, _LL, _P, _LL, _I, _P, C.c_float, _P, _P, _P, _LL, _I, _P]),
+    "sb_l2norm_rows": (_I, [_P, _LL, _I, _I, _P, _LL, _P]),
     "sb_stats": (_I, [_P, _P, C.POINTER(Stats)]),
     "sb_last_launch_count": (_I, [_P]),
     "sb_destroy": (_I, [_P]),
