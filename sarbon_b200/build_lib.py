@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 OBJ = PKG / "_build"
 LIB = PKG / "libsarbon_sparse.so"
 SOURCES = ["sb_engine.cu", "sb_gate.cu", "sb_conv_tc.cu", "sb_conv_simt.cu", "sb_noalloc.cu", "sb_cells.cu", "sb_boxes.cu",
-           "sb_prep.cu", "sb_deform.cu", "sb_gemm.cu", "sb_detops.cu"]
+           "sb_prep.cu", "sb_deform.cu", "sb_gemm.cu", "sb_detops.cu", "sb_attn.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", f"-I{PKG.parent / 'include'}"]

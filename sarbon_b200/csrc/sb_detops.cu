@@ -9,8 +9,6 @@
 //   sb_dwconv3x3      depthwise 3x3 conv (padding 1) + folded BatchNorm + ReLU, NHWC fp16
 //                     (fuse()'s second half, sarbon_det.py:73-77)
 //   sb_upsample2x     nearest 2x upsampling of an NHWC fp16 map (F.interpolate, scale 2)
-//   sb_attention      softmax(q k^T / sqrt(dh)) v per head, fp16 rows in and out, fp32 online
-//                     softmax (nn.MultiheadAttention / nn.TransformerEncoderLayer attention)
 //   sb_topk_rows      top-K rows of max-over-classes logits, masked rows excluded
 //                     (sarbon_det.py:314), ordered by value, ties by row index
 //   sb_gather_rows    rows of a matrix by per-image indices (sarbon_det.py:315-320)
@@ -20,6 +18,7 @@
 //   sb_box_*          the box heads of the encoder and decoder (sarbon_det.py:316-352,
 //                     box_ops.py:78-106)
 // Each kernel reads and writes caller memory on the caller's stream and allocates nothing.
+// (The attention core is in sb_attn.cu.)
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -87,6 +86,88 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const void* a, int a_f32
   }
 }
 
+// D = 256 with 16-byte aligned rows: lane l holds channels 8l..8l+7 (one 16-byte fp16 or two
+// 16-byte fp32 accesses per operand), otherwise the same arithmetic as layernorm_kernel
+SB_DEV void load8(const void* p, int f32, long long off, float (&v)[8]) {
+  if (f32) {
+    const float4 x0 = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + off);
+    const float4 x1 = *reinterpret_cast<const float4*>(static_cast<const float*>(p) + off + 4);
+    v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w; v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+  } else {
+    const uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p) + off);
+    const __half2* hh = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 f = __half22float2(hh[u]);
+      v[2 * u] = f.x;
+      v[2 * u + 1] = f.y;
+    }
+  }
+}
+SB_DEV uint4 pack8(const float (&v)[8]) {
+  uint4 o;
+  __half2* hh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) hh[u] = __floats2half2_rn(v[2 * u], v[2 * u + 1]);
+  return o;
+}
+
+__global__ void __launch_bounds__(256) layernorm256_kernel(const void* a, int a_f32, long long lda, const void* b,
+                                                           int b_f32, long long ldb, const float* gamma,
+                                                           const float* beta, float eps, int rows, float* y32,
+                                                           long long ld32, __half* y16, long long ld16,
+                                                           const __half* pos, long long ldpos, int period, float sign,
+                                                           __half* yp16, long long ldp) {
+  const int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int c = lane * 8;
+  float v[8];
+  load8(a, a_f32, (long long)row * lda + c, v);
+  if (b) {
+    float w[8];
+    load8(b, b_f32, (long long)row * ldb + c, w);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      v[u] += w[u];
+      if (!a_f32 && !b_f32) v[u] = r16(v[u]);  // an fp16 + fp16 sum is an fp16 tensor
+    }
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) s += v[u];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+  const float mean = s * (1.f / 256.f);
+  float q = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float d = v[u] - mean;
+    q += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+  const float rstd = rsqrtf(q * (1.f / 256.f) + eps);
+  float gm[8], bt[8], y[8];
+  load8(gamma, 1, c, gm);
+  load8(beta, 1, c, bt);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) y[u] = (v[u] - mean) * rstd * gm[u] + bt[u];
+  if (y32) {
+    float* p = y32 + (long long)row * ld32 + c;
+    *reinterpret_cast<float4*>(p) = make_float4(y[0], y[1], y[2], y[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(y[4], y[5], y[6], y[7]);
+  }
+  if (y16) *reinterpret_cast<uint4*>(y16 + (long long)row * ld16 + c) = pack8(y);
+  if (yp16) {
+    float pv[8];
+    load8(pos, 0, (long long)(row % period) * ldpos + c, pv);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) pv[u] = y[u] + sign * pv[u];
+    *reinterpret_cast<uint4*>(yp16 + (long long)row * ldp + c) = pack8(pv);
+  }
+}
+
 __global__ void add_rows_kernel(const void* a, int a_f32, long long lda, const void* pos, int p_f32, long long ldpos,
                                 int period, float sign, int rows, int D, __half* out, long long ldo) {
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -97,21 +178,22 @@ __global__ void add_rows_kernel(const void* a, int a_f32, long long lda, const v
 }
 
 // ------------------------------------------------------------------ depthwise conv, upsample
-// thread per (pixel, 8 channels); w [9][C] fp32 (BatchNorm folded), bias [C]
-__global__ void dwconv3x3_kernel(const __half* x, long long ldx, long long imgx, int B, int H, int W, int C,
-                                 const float* w, const float* bias, int relu, __half* y, long long ldy, long long imgy) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int cg = C / 8;
-  if (i >= (long long)B * H * W * cg) return;
-  const int c0 = (int)(i % cg) * 8;
-  long long p = i / cg;
-  const int xo = (int)(p % W);
-  p /= W;
-  const int yo = (int)(p % H);
-  const int b = (int)(p / H);
+// grid (x: pixels of a row x 8-channel groups, y: row, z: image); thread per (pixel, 8
+// channels); w [9][C] fp32 (BatchNorm folded), bias [C]
+__global__ void dwconv3x3_kernel(const __half* x, long long ldx, long long imgx, int H, int W, int C, const float* w,
+                                 const float* bias, int relu, __half* y, long long ldy, long long imgy) {
+  const int cg = C >> 3;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= W * cg) return;
+  const int xo = i / cg, c0 = (i - xo * cg) * 8;
+  const int yo = blockIdx.y, b = blockIdx.z;
   float acc[8];
-#pragma unroll
-  for (int u = 0; u < 8; ++u) acc[u] = bias[c0 + u];
+  {
+    const float4 b0 = *reinterpret_cast<const float4*>(bias + c0), b1 = *reinterpret_cast<const float4*>(bias + c0 + 4);
+    acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
+    acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
+  }
+  const __half* xb = x + (long long)b * imgx * ldx;
 #pragma unroll
   for (int ky = 0; ky < 3; ++ky) {
     const int yy = yo + ky - 1;
@@ -120,14 +202,16 @@ __global__ void dwconv3x3_kernel(const __half* x, long long ldx, long long imgx,
     for (int kx = 0; kx < 3; ++kx) {
       const int xx = xo + kx - 1;
       if (xx < 0 || xx >= W) continue;
-      const uint4 raw = *reinterpret_cast<const uint4*>(x + ((long long)b * imgx + (long long)yy * W + xx) * ldx + c0);
-      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+      const uint4 raw = *reinterpret_cast<const uint4*>(xb + ((long long)yy * W + xx) * ldx + c0);
+      const __half2* hh = reinterpret_cast<const __half2*>(&raw);
       const float* wt = w + (ky * 3 + kx) * C + c0;
+      const float4 w0 = *reinterpret_cast<const float4*>(wt), w1 = *reinterpret_cast<const float4*>(wt + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float2 f = __half22float2(h[u]);
-        acc[2 * u] = fmaf(f.x, wt[2 * u], acc[2 * u]);
-        acc[2 * u + 1] = fmaf(f.y, wt[2 * u + 1], acc[2 * u + 1]);
+        const float2 f = __half22float2(hh[u]);
+        acc[2 * u] = fmaf(f.x, wv[2 * u], acc[2 * u]);
+        acc[2 * u + 1] = fmaf(f.y, wv[2 * u + 1], acc[2 * u + 1]);
       }
     }
   }
@@ -145,113 +229,16 @@ __global__ void dwconv3x3_kernel(const __half* x, long long ldx, long long imgx,
   *reinterpret_cast<uint4*>(y + ((long long)b * imgy + (long long)yo * W + xo) * ldy + c0) = o;
 }
 
-__global__ void upsample2x_kernel(const __half* x, long long ldx, long long imgx, int B, int H, int W, int C, __half* y,
-                                  long long ldy, long long imgy) {
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int cg = C / 8, W2 = 2 * W, H2 = 2 * H;
-  if (i >= (long long)B * H2 * W2 * cg) return;
-  const int c0 = (int)(i % cg) * 8;
-  long long p = i / cg;
-  const int xo = (int)(p % W2);
-  p /= W2;
-  const int yo = (int)(p % H2);
-  const int b = (int)(p / H2);
+// grid (x: output pixels of a row x 8-channel groups, y: output row, z: image)
+__global__ void upsample2x_kernel(const __half* x, long long ldx, long long imgx, int W, int C, __half* y, long long ldy,
+                                  long long imgy) {
+  const int cg = C >> 3, W2 = 2 * W;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= W2 * cg) return;
+  const int xo = i / cg, c0 = (i - xo * cg) * 8;
+  const int yo = blockIdx.y, b = blockIdx.z;
   *reinterpret_cast<uint4*>(y + ((long long)b * imgy + (long long)yo * W2 + xo) * ldy + c0) =
       *reinterpret_cast<const uint4*>(x + ((long long)b * imgx + (long long)(yo >> 1) * W + (xo >> 1)) * ldx + c0);
-}
-
-// ------------------------------------------------------------------ attention
-// Thread per query, 128 queries per CTA, one (image, head) per blockIdx.(z, y); key / value
-// tiles of 64 rows staged in shared memory (fp16), scores of a tile in registers, one
-// rescale of the running sum per tile (online softmax, base-2 exponentials of pre-scaled
-// scores).  dh = 32.
-constexpr int kAttKT = 64;
-__global__ void __launch_bounds__(128) attention_kernel(const __half* q, long long ldq, long long imgq,
-                                                        const __half* k, long long ldk, long long imgk,
-                                                        const __half* v, long long ldv, long long imgv, int Tq, int Tk,
-                                                        float scale_log2, __half* out, long long ldo, long long imgo) {
-  constexpr int DH = 32;
-  __shared__ __align__(16) __half sk[kAttKT][DH];
-  __shared__ __align__(16) __half sv[kAttKT][DH];
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int qi = blockIdx.x * 128 + threadIdx.x;
-  const bool active = qi < Tq;
-  float qv[DH], acc[DH];
-  if (active) {
-    const __half* qp = q + ((long long)b * imgq + qi) * ldq + h * DH;
-#pragma unroll
-    for (int d = 0; d < DH; d += 8) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(qp + d);
-      const __half2* hh = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float2 f = __half22float2(hh[u]);
-        qv[d + 2 * u] = f.x * scale_log2;
-        qv[d + 2 * u + 1] = f.y * scale_log2;
-      }
-    }
-  }
-#pragma unroll
-  for (int d = 0; d < DH; ++d) acc[d] = 0.f;
-  float m = -INFINITY, l = 0.f;
-  for (int t0 = 0; t0 < Tk; t0 += kAttKT) {
-    __syncthreads();
-    // 64 rows x 64 B of K and of V: 256 16-byte pieces each, two per thread
-    for (int pce = threadIdx.x; pce < kAttKT * 4; pce += 128) {
-      const int r = pce >> 2, c = (pce & 3) * 8;
-      uint4 kr = make_uint4(0, 0, 0, 0), vr = make_uint4(0, 0, 0, 0);
-      if (t0 + r < Tk) {
-        kr = *reinterpret_cast<const uint4*>(k + ((long long)b * imgk + t0 + r) * ldk + h * DH + c);
-        vr = *reinterpret_cast<const uint4*>(v + ((long long)b * imgv + t0 + r) * ldv + h * DH + c);
-      }
-      *reinterpret_cast<uint4*>(&sk[r][c]) = kr;
-      *reinterpret_cast<uint4*>(&sv[r][c]) = vr;
-    }
-    __syncthreads();
-    const int nk = Tk - t0 < kAttKT ? Tk - t0 : kAttKT;
-    float s[kAttKT];
-    float tmax = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kAttKT; ++j) {
-      float d0 = 0.f;
-#pragma unroll
-      for (int d = 0; d < DH; d += 2) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&sk[j][d]));
-        d0 = fmaf(qv[d], f.x, d0);
-        d0 = fmaf(qv[d + 1], f.y, d0);
-      }
-      s[j] = j < nk ? d0 : -INFINITY;
-      tmax = fmaxf(tmax, s[j]);
-    }
-    const float mnew = fmaxf(m, tmax);
-    const float corr = exp2f(m - mnew);  // m = -inf on the first tile: corr = 0
-    l *= corr;
-#pragma unroll
-    for (int d = 0; d < DH; ++d) acc[d] *= corr;
-#pragma unroll
-    for (int j = 0; j < kAttKT; ++j) {
-      const float p = exp2f(s[j] - mnew);
-      l += p;
-#pragma unroll
-      for (int d = 0; d < DH; d += 2) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&sv[j][d]));
-        acc[d] = fmaf(p, f.x, acc[d]);
-        acc[d + 1] = fmaf(p, f.y, acc[d + 1]);
-      }
-    }
-    m = mnew;
-  }
-  if (!active) return;
-  const float inv = 1.f / l;
-  __half* op = out + ((long long)b * imgo + qi) * ldo + h * DH;
-#pragma unroll
-  for (int d = 0; d < DH; d += 8) {
-    uint4 raw;
-    __half2* hh = reinterpret_cast<__half2*>(&raw);
-#pragma unroll
-    for (int u = 0; u < 4; ++u) hh[u] = __floats2half2_rn(acc[d + 2 * u] * inv, acc[d + 2 * u + 1] * inv);
-    *reinterpret_cast<uint4*>(op + d) = raw;
-  }
 }
 
 // ------------------------------------------------------------------ top-K
@@ -430,67 +417,90 @@ struct DeformSampleArgs {
   int lh[kMaxLevels], lw[kMaxLevels], lstart[kMaxLevels];
 };
 
+// Lane k < L*P first works out sampling point k (its softmax weight, location, the value rows
+// of its four bilinear corners and their weights, corners outside the map dropped); every
+// lane then takes each point's corners by shuffle and reads its own channel of them, so the
+// warp's corner loads are independent of one another.
 __global__ void __launch_bounds__(256) deform_sample_kernel(DeformSampleArgs a) {
   const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
-  if (gw >= a.B * a.Q * a.H) return;
+  if (gw >= a.B * a.Q * a.H) return;  // warp-uniform
   const int h = gw % a.H, qi = (gw / a.H) % a.Q, b = gw / (a.H * a.Q);
   const int LP = a.L * a.P;
-  // softmax over the L*P logits of this head
+  const bool mine = lane < LP;
+  const int k = mine ? lane : 0;
+  // softmax over the L*P logits of this head (lane k holds logit k)
   const __half* lg = a.att + ((long long)b * a.imgatt + qi) * a.ldatt + (long long)h * LP;
-  float mx = -INFINITY;
-  for (int k = 0; k < LP; ++k) mx = fmaxf(mx, __half2float(lg[k]));
-  float den = 0.f;
-  for (int k = 0; k < LP; ++k) den += expf(__half2float(lg[k]) - mx);
-  float rx, ry, rw, rh;
-  {
+  const float x = mine ? __half2float(lg[k]) : -INFINITY;
+  float mx = x;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  const float ex = mine ? expf(x - mx) : 0.f;
+  float den = ex;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) den += __shfl_xor_sync(0xFFFFFFFFu, den, o);
+  const float w = ex / den;
+  // geometry of point k
+  int row00 = -1, row01 = -1, row10 = -1, row11 = -1;
+  float w00 = 0.f, w01 = 0.f, w10 = 0.f, w11 = 0.f;
+  if (mine) {
+    const int l = k / a.P;
+    const int H_ = a.lh[l], W_ = a.lw[l];
     const long long ro = ((long long)b * a.imgref + qi) * a.ldref;
-    rx = ld_any(a.ref, a.ref_f32, ro);
-    ry = ld_any(a.ref, a.ref_f32, ro + 1);
-    rw = ld_any(a.ref, a.ref_f32, ro + 2);
-    rh = ld_any(a.ref, a.ref_f32, ro + 3);
+    const float rx = ld_any(a.ref, a.ref_f32, ro), ry = ld_any(a.ref, a.ref_f32, ro + 1);
+    const float rw = ld_any(a.ref, a.ref_f32, ro + 2), rh = ld_any(a.ref, a.ref_f32, ro + 3);
+    const __half* op = a.off + ((long long)b * a.imgoff + qi) * a.ldoff + (long long)h * LP * 2;
+    const float ox = __half2float(op[2 * k]), oy = __half2float(op[2 * k + 1]);
+    float gx, gy;
+    if (a.ref_f32) {
+      // off / P (fp16) * ref_wh (fp32) * 0.5 + ref_xy in fp32; grid in fp32
+      const float tx = r16(ox / (float)a.P), ty = r16(oy / (float)a.P);
+      const float lx = __fadd_rn(rx, __fmul_rn(__fmul_rn(tx, rw), 0.5f));
+      const float ly = __fadd_rn(ry, __fmul_rn(__fmul_rn(ty, rh), 0.5f));
+      gx = __fsub_rn(__fmul_rn(2.f, lx), 1.f);
+      gy = __fsub_rn(__fmul_rn(2.f, ly), 1.f);
+    } else {
+      // every op of the fp16 expression rounded to fp16
+      const float tx = r16(ox / (float)a.P), ty = r16(oy / (float)a.P);
+      const float lx = r16(rx + r16(r16(tx * rw) * 0.5f));
+      const float ly = r16(ry + r16(r16(ty * rh) * 0.5f));
+      gx = r16(r16(2.f * lx) - 1.f);
+      gy = r16(r16(2.f * ly) - 1.f);
+    }
+    const float ix = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gx, 1.f), (float)W_), 1.f), 2.f);
+    const float iy = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gy, 1.f), (float)H_), 1.f), 2.f);
+    const float fx = floorf(ix), fy = floorf(iy);
+    // the sampling point may lie far outside the map: clamp before the int conversion
+    const float cfx = fminf(fmaxf(fx, -2.f), (float)W_ + 1.f), cfy = fminf(fmaxf(fy, -2.f), (float)H_ + 1.f);
+    const int x0 = (int)cfx, y0 = (int)cfy;
+    const float tx1 = __fsub_rn(ix, fx), ty1 = __fsub_rn(iy, fy);
+    const float tx0 = __fsub_rn(__fadd_rn(fx, 1.f), ix), ty0 = __fsub_rn(__fadd_rn(fy, 1.f), iy);
+    const bool x0in = x0 >= 0 && x0 < W_, x1in = x0 + 1 >= 0 && x0 + 1 < W_;
+    const bool y0in = y0 >= 0 && y0 < H_, y1in = y0 + 1 >= 0 && y0 + 1 < H_;
+    const int base = a.lstart[l];
+    if (y0in && x0in) { row00 = base + y0 * W_ + x0; w00 = __fmul_rn(tx0, ty0); }
+    if (y0in && x1in) { row01 = base + y0 * W_ + x0 + 1; w01 = __fmul_rn(tx1, ty0); }
+    if (y1in && x0in) { row10 = base + (y0 + 1) * W_ + x0; w10 = __fmul_rn(tx0, ty1); }
+    if (y1in && x1in) { row11 = base + (y0 + 1) * W_ + x0 + 1; w11 = __fmul_rn(tx1, ty1); }
   }
-  const __half* op = a.off + ((long long)b * a.imgoff + qi) * a.ldoff + (long long)h * LP * 2;
   const __half* vb = a.value + (long long)b * a.imgv * a.ldv + h * 32 + lane;
   float acc = 0.f;
-  for (int l = 0; l < a.L; ++l) {
-    const int H_ = a.lh[l], W_ = a.lw[l];
-    const __half* vl = vb + (long long)a.lstart[l] * a.ldv;
-    for (int p = 0; p < a.P; ++p) {
-      const int k = l * a.P + p;
-      const float w = expf(__half2float(lg[k]) - mx) / den;
-      const float ox = __half2float(op[2 * k]), oy = __half2float(op[2 * k + 1]);
-      float gx, gy;
-      if (a.ref_f32) {
-        // off / P (fp16) * ref_wh (fp32) * 0.5 + ref_xy in fp32; grid in fp32
-        const float tx = r16(ox / (float)a.P), ty = r16(oy / (float)a.P);
-        const float lx = __fadd_rn(rx, __fmul_rn(__fmul_rn(tx, rw), 0.5f));
-        const float ly = __fadd_rn(ry, __fmul_rn(__fmul_rn(ty, rh), 0.5f));
-        gx = __fsub_rn(__fmul_rn(2.f, lx), 1.f);
-        gy = __fsub_rn(__fmul_rn(2.f, ly), 1.f);
-      } else {
-        // every op of the fp16 expression rounded to fp16
-        const float tx = r16(ox / (float)a.P), ty = r16(oy / (float)a.P);
-        const float lx = r16(rx + r16(r16(tx * rw) * 0.5f));
-        const float ly = r16(ry + r16(r16(ty * rh) * 0.5f));
-        gx = r16(r16(2.f * lx) - 1.f);
-        gy = r16(r16(2.f * ly) - 1.f);
-      }
-      const float ix = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gx, 1.f), (float)W_), 1.f), 2.f);
-      const float iy = __fdiv_rn(__fsub_rn(__fmul_rn(__fadd_rn(gy, 1.f), (float)H_), 1.f), 2.f);
-      const float fx = floorf(ix), fy = floorf(iy);
-      const int x0 = (int)fx, y0 = (int)fy;
-      const float tx1 = __fsub_rn(ix, fx), ty1 = __fsub_rn(iy, fy);
-      const float tx0 = __fsub_rn(__fadd_rn(fx, 1.f), ix), ty0 = __fsub_rn(__fadd_rn(fy, 1.f), iy);
-      float s = 0.f;
-      const bool x0in = x0 >= 0 && x0 < W_, x1in = x0 + 1 >= 0 && x0 + 1 < W_;
-      const bool y0in = y0 >= 0 && y0 < H_, y1in = y0 + 1 >= 0 && y0 + 1 < H_;
-      if (y0in && x0in) s = fmaf(__half2float(vl[((long long)y0 * W_ + x0) * a.ldv]), __fmul_rn(tx0, ty0), s);
-      if (y0in && x1in) s = fmaf(__half2float(vl[((long long)y0 * W_ + x0 + 1) * a.ldv]), __fmul_rn(tx1, ty0), s);
-      if (y1in && x0in) s = fmaf(__half2float(vl[((long long)(y0 + 1) * W_ + x0) * a.ldv]), __fmul_rn(tx0, ty1), s);
-      if (y1in && x1in) s = fmaf(__half2float(vl[((long long)(y0 + 1) * W_ + x0 + 1) * a.ldv]), __fmul_rn(tx1, ty1), s);
-      acc = fmaf(s, w, acc);
-    }
+  for (int j = 0; j < LP; ++j) {
+    const int i00 = __shfl_sync(0xFFFFFFFFu, row00, j), i01 = __shfl_sync(0xFFFFFFFFu, row01, j);
+    const int i10 = __shfl_sync(0xFFFFFFFFu, row10, j), i11 = __shfl_sync(0xFFFFFFFFu, row11, j);
+    const float c00 = __shfl_sync(0xFFFFFFFFu, w00, j), c01 = __shfl_sync(0xFFFFFFFFu, w01, j);
+    const float c10 = __shfl_sync(0xFFFFFFFFu, w10, j), c11 = __shfl_sync(0xFFFFFFFFu, w11, j);
+    const float wj = __shfl_sync(0xFFFFFFFFu, w, j);
+    const float v00 = i00 >= 0 ? __half2float(vb[(long long)i00 * a.ldv]) : 0.f;
+    const float v01 = i01 >= 0 ? __half2float(vb[(long long)i01 * a.ldv]) : 0.f;
+    const float v10 = i10 >= 0 ? __half2float(vb[(long long)i10 * a.ldv]) : 0.f;
+    const float v11 = i11 >= 0 ? __half2float(vb[(long long)i11 * a.ldv]) : 0.f;
+    float sv = 0.f;
+    sv = fmaf(v00, c00, sv);
+    sv = fmaf(v01, c01, sv);
+    sv = fmaf(v10, c10, sv);
+    sv = fmaf(v11, c11, sv);
+    acc = fmaf(sv, wj, acc);
   }
   a.out[((long long)b * a.imgo + qi) * a.ldo + h * 32 + lane] = __float2half_rn(acc);
 }
@@ -612,6 +622,18 @@ extern "C" int sb_layernorm(const void* a, int a_dtype, long long lda, const voi
   if (!a || !gamma || !beta || rows < 1 || D < 32 || D > 1024 || D % 32 != 0 || (!y32 && !y16 && !yp16) ||
       (yp16 && (!pos || period < 1)))
     return record_error(SB_EINVAL, "sb_layernorm: arguments");
+  auto al = [](const void* p, long long ld, int f32) {
+    return p == nullptr || ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld * (f32 ? 4 : 2)) % 16 == 0);
+  };
+  if (D == 256 && al(a, lda, a_dtype == SB_F32) && al(b, ldb, b_dtype == SB_F32) && al(y32, ld32, 1) &&
+      al(y16, ld16, 0) && al(pos, ldpos, 0) && al(yp16, ldp, 0) && al(gamma, 0, 1) && al(beta, 0, 1)) {
+    layernorm256_kernel<<<blocks_for((long long)rows * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+        a, a_dtype == SB_F32, lda, b, b_dtype == SB_F32, ldb, gamma, beta, eps, rows, y32, ld32,
+        static_cast<__half*>(y16), ld16, static_cast<const __half*>(pos), ldpos, period > 0 ? period : 1, sign,
+        static_cast<__half*>(yp16), ldp);
+    SB_LAUNCH_CHECK("sb_layernorm");
+    return SB_OK;
+  }
   layernorm_kernel<<<blocks_for((long long)rows * 32, 256), 256, 0, (cudaStream_t)stream>>>(
       a, a_dtype == SB_F32, lda, b, b_dtype == SB_F32, ldb, gamma, beta, eps, rows, D, y32, ld32,
       static_cast<__half*>(y16), ld16, static_cast<const __half*>(pos), ldpos, period > 0 ? period : 1, sign,
@@ -634,8 +656,11 @@ extern "C" int sb_dwconv3x3(const void* x, long long ldx, long long imgx, int B,
   if (!x || !w || !bias || !y || B < 1 || H < 1 || W < 1 || C < 8 || C % 8 != 0 || ldx % 8 != 0 || ldy % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
     return record_error(SB_EINVAL, "sb_dwconv3x3: arguments (C, ld multiples of 8, 16-byte aligned)");
-  dwconv3x3_kernel<<<blocks_for((long long)B * H * W * (C / 8), 256), 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const __half*>(x), ldx, imgx, B, H, W, C, w, bias, relu, static_cast<__half*>(y), ldy, imgy);
+  if ((long long)W * (C / 8) > (1ll << 30) || H > 65535 || B > 65535 || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(bias) & 15))
+    return record_error(SB_EINVAL, "sb_dwconv3x3: sizes (H, B <= 65535) or unaligned weights");
+  dwconv3x3_kernel<<<dim3(blocks_for((long long)W * (C / 8), 256), H, B), 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const __half*>(x), ldx, imgx, H, W, C, w, bias, relu, static_cast<__half*>(y), ldy, imgy);
   SB_LAUNCH_CHECK("sb_dwconv3x3");
   return SB_OK;
 }
@@ -645,25 +670,11 @@ extern "C" int sb_upsample2x(const void* x, long long ldx, long long imgx, int B
   if (!x || !y || B < 1 || H < 1 || W < 1 || C < 8 || C % 8 != 0 || ldx % 8 != 0 || ldy % 8 != 0 ||
       (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
     return record_error(SB_EINVAL, "sb_upsample2x: arguments");
-  upsample2x_kernel<<<blocks_for((long long)B * 4 * H * W * (C / 8), 256), 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const __half*>(x), ldx, imgx, B, H, W, C, static_cast<__half*>(y), ldy, imgy);
+  if ((long long)2 * W * (C / 8) > (1ll << 30) || 2 * H > 65535 || B > 65535)
+    return record_error(SB_EINVAL, "sb_upsample2x: sizes");
+  upsample2x_kernel<<<dim3(blocks_for((long long)2 * W * (C / 8), 256), 2 * H, B), 256, 0, (cudaStream_t)stream>>>(
+      static_cast<const __half*>(x), ldx, imgx, W, C, static_cast<__half*>(y), ldy, imgy);
   SB_LAUNCH_CHECK("sb_upsample2x");
-  return SB_OK;
-}
-
-extern "C" int sb_attention(const void* q, long long ldq, long long imgq, const void* k, long long ldk, long long imgk,
-                            const void* v, long long ldv, long long imgv, int B, int H, int dh, int Tq, int Tk,
-                            void* out, long long ldo, long long imgo, void* stream) {
-  if (!q || !k || !v || !out || dh != 32 || B < 1 || H < 1 || Tq < 1 || Tk < 1 || H > 65535 || B > 65535 ||
-      ldq % 8 || ldk % 8 || ldv % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(q) & 15) ||
-      (reinterpret_cast<uintptr_t>(k) & 15) || (reinterpret_cast<uintptr_t>(v) & 15) ||
-      (reinterpret_cast<uintptr_t>(out) & 15))
-    return record_error(SB_EINVAL, "sb_attention: arguments (dh = 32, 16-byte rows)");
-  const float scale_log2 = 1.4426950408889634f / sqrtf((float)dh);
-  attention_kernel<<<dim3(blocks_for(Tq, 128), H, B), 128, 0, (cudaStream_t)stream>>>(
-      static_cast<const __half*>(q), ldq, imgq, static_cast<const __half*>(k), ldk, imgk,
-      static_cast<const __half*>(v), ldv, imgv, Tq, Tk, scale_log2, static_cast<__half*>(out), ldo, imgo);
-  SB_LAUNCH_CHECK("sb_attention");
   return SB_OK;
 }
 
@@ -702,8 +713,9 @@ extern "C" int sb_deform_sample(const void* value, long long ldv, long long imgv
                                 const void* off, long long ldoff, long long imgoff, const void* att, long long ldatt,
                                 long long imgatt, const void* ref, int ref_dtype, long long ldref, long long imgref,
                                 int B, int Q, int H, int P, void* out, long long ldo, long long imgo, void* stream) {
-  if (!value || !level_hw || !off || !att || !ref || !out || L < 1 || L > kMaxLevels || B < 1 || Q < 1 || H < 1 || P < 1)
-    return record_error(SB_EINVAL, "sb_deform_sample: arguments");
+  if (!value || !level_hw || !off || !att || !ref || !out || L < 1 || L > kMaxLevels || B < 1 || Q < 1 || H < 1 ||
+      P < 1 || L * P > 32)
+    return record_error(SB_EINVAL, "sb_deform_sample: arguments (L * P <= 32)");
   DeformSampleArgs a{};
   a.value = static_cast<const __half*>(value);
   a.ldv = ldv;

@@ -211,8 +211,8 @@ class B200Detector:
         self.f32b = e(B, h32, w32, d, **f16)
         # encoder
         self.enc_lin = e(B, S, d, **f16)
-        self.enc32 = e(B, S, d, **f32)
         self.enc16 = e(B, S, d, **f16)
+        self.enc_sel = e(B, K, d, **f16)  # enc_proj rows of the selected queries, before the LayerNorm
         self.enc_logits = e(B, S, self.nc, **f16)
         self.top = e(B, K, device=dev, dtype=torch.int32)
         self.tgt32 = [e(B, K, d, **f32), e(B, K, d, **f32)]
@@ -325,13 +325,16 @@ class B200Detector:
         B, S, d, K = self.B, self.S, self.d, self.K
         g = ops.gemm_conv
         g(self.mem.view(B * S, d), *self.w_encp, out=self.enc_lin.view(B * S, d))
-        ops.layernorm(self.enc_lin, *self.n_enc, y32=self.enc32, y16=self.enc16)
+        # fp16 rows for the class head; the fp32 rows are needed for the selected queries only,
+        # whose LayerNorm (row-local, the same kernel) is recomputed after the selection
+        ops.layernorm(self.enc_lin, *self.n_enc, y16=self.enc16)
         g(self.enc16.view(B * S, d), *self.w_enc_cls, out=self.enc_logits.view(B * S, self.nc))
         if self.force_top is not None:
             self.top.copy_(self.force_top)
         else:
             ops.topk_rows(self.enc_logits, K, self.valid, out=self.top)
-        ops.gather_rows(self.enc32, self.top, o32=self.tgt32[0], o16=self.tgt16)
+        ops.gather_rows(self.enc_lin, self.top, o16=self.enc_sel)
+        ops.layernorm(self.enc_sel, *self.n_enc, y32=self.tgt32[0], y16=self.tgt16)
         ops.gather_rows(self.enc_logits, self.top, o32=self.enc_logits_sel)
         self._mlp(self.w_enc_box, self.tgt16, [self.h1, self.h2], self.encbox)
         ops.box_enc(self.encbox.view(B * K, 4), self.anchors, self.top, self.ref16, self.qin.view(B * K, 64))
