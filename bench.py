@@ -84,6 +84,9 @@ def parse():
     p.add_argument("--no-reference-gpu", action="store_true",
                    help="skip timing the reference's own Triton engine on the GPU (rank 0, N = 1)")
     p.add_argument("--reference-gpu-steps", type=int, default=60)
+    p.add_argument("--no-detector", action="store_true",
+                   help="skip timing the detector after the stem (B200Detector vs the reference's own)")
+    p.add_argument("--detector-iters", type=int, default=20)
     return p.parse_args()
 
 
@@ -373,6 +376,97 @@ def gpu_reference_run(ref, net, seq, tau, steps, dev):
     return {"value": S * steps / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms / steps, "steps": steps,
             "modes_warmup": modes, "what": "the reference FusedSparseEngine (its Triton tile kernel, "
             "CUDA graphs and per-step host sync) on the same frames and weights, this GPU"}
+
+
+def detector_run(eng, S, H, W, dev, iters, seed=0):
+    """The detector after the stem on the engine's p8 (rank 0, N = 1): this library's
+    B200Detector (one CUDA graph of sb_gemm_conv / sb_attention / ... launches) against the
+    reference's own SarbonDetector under autocast, captured as a CUDA graph the way
+    SarbonVideo._detect does (sarbon/inference/video.py:116-137), on the same p8 and weights
+    (random-init Sarbon-S with non-trivial BatchNorm statistics and heads).  Both are timed
+    with CUDA events over `iters` replays after 3 warm-up replays."""
+    if not (REF_DIR / "sarbon").is_dir():
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import sarbon.models.sarbon_det as sd
+    from sarbon_b200 import det_ops
+    from sarbon_b200.detector import B200Detector
+    torch.manual_seed(seed)
+    det = sd.build("s", 6, halo_zero=False)
+    gen = torch.Generator().manual_seed(seed + 1)
+    with torch.no_grad():
+        for m in det.modules():
+            if isinstance(m, torch.nn.BatchNorm2d):
+                c = m.num_features
+                m.running_mean.copy_(torch.rand(c, generator=gen) * 0.4 - 0.2)
+                m.running_var.copy_(torch.rand(c, generator=gen) * 1.5 + 0.5)
+                m.weight.copy_(torch.rand(c, generator=gen) + 0.5)
+                m.bias.copy_(torch.rand(c, generator=gen) * 0.4 - 0.2)
+            elif isinstance(m, torch.nn.Linear) and not m.weight.any():
+                m.weight.copy_(torch.randn(m.weight.shape, generator=gen) * 0.02)
+    det = det.to(dev).eval()
+    p8 = eng.outputs_nchw()[1]
+    if p8.dtype != torch.float16:
+        p8 = p8.half()
+    h8, w8 = p8.shape[-2:]
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / iters
+
+    mine = B200Detector(det, S, h8, w8, device=dev)
+    det_ops.LAUNCHES[0] = 0
+    mine.run(p8)
+    launches = det_ops.LAUNCHES[0]
+    mine.capture(p8)
+    ms_mine = timed(mine.replay)
+    out = {k: v.clone() for k, v in mine.outputs().items() if torch.is_tensor(v)}
+    # the reference, graph-captured under autocast (SarbonVideo._detect)
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st), torch.no_grad(), torch.autocast("cuda", torch.float16):
+        for _ in range(3):
+            det(None, p8=p8)
+    torch.cuda.current_stream().wait_stream(st)
+    with torch.cuda.graph(g), torch.no_grad(), torch.autocast("cuda", torch.float16):
+        ref_out = det(None, p8=p8)
+    ms_ref = timed(g.replay)
+    # agreement on these inputs: the selected queries, and the boxes / logits with the
+    # reference's selection forced (top-K rows of equal scores may order differently)
+    with torch.no_grad(), torch.autocast("cuda", torch.float16):
+        feats = det.core(p8)
+        shapes = [f.shape[-2:] for f in feats]
+        memory = torch.cat([f.flatten(2).transpose(1, 2) for f in feats], 1)
+        _, valid = det.anchors(shapes, memory.device, memory.dtype)
+        enc = det.enc_proj(memory * valid.to(memory.dtype))
+        top = det.enc_cls(enc).max(-1).values.masked_fill(~valid[..., 0], float("-inf")).topk(det.cfg.queries, 1).indices
+    shared = sum(len(set(out["top"][b].tolist()) & set(top[b].tolist())) for b in range(S)) / top.numel()
+    mine.force_top = top.to(torch.int32)
+    forced = mine.run(p8)
+    torch.cuda.synchronize()
+    dbox = (forced["pred_boxes"].float() - ref_out["pred_boxes"].float()).abs().max().item()
+    dlog = (forced["pred_logits"].float() - ref_out["pred_logits"].float()).abs().max().item()
+    res = {"ms_per_batch": ms_mine, "frames_per_s": S / (ms_mine * 1e-3),
+           "reference_ms_per_batch": ms_ref, "reference_frames_per_s": S / (ms_ref * 1e-3),
+           "batch": S, "p8": [int(h8), int(w8)], "queries": det.cfg.queries, "gpu_launches_per_batch": launches,
+           "top_k_rows_shared_with_reference": round(shared, 4),
+           "pred_boxes_max_abs_diff_forced_top_k": dbox, "pred_logits_max_abs_diff_forced_top_k": dlog,
+           "timing": f"CUDA events over {iters} graph replays after 3 warm-up replays, both arms",
+           "reference": "SarbonDetector (build('s', 6, halo_zero=False)) under torch.autocast(float16), "
+                        "captured as one CUDA graph (SarbonVideo._detect)"}
+    del mine, g, ref_out, det
+    torch.cuda.empty_cache()
+    return res
 
 
 def time_mask_kernels(dev, S, H, W, block, seconds=2.0):
@@ -711,6 +805,18 @@ def run_b200(args):
             except Exception as ex:  # report, do not fail the bench
                 ref_gpu = {"unavailable": f"{type(ex).__name__}: {str(ex)[:200]}"}
             torch.cuda.empty_cache()
+    detector = None
+    if rank == 0 and world == 1 and not args.no_detector:
+        try:
+            detector = detector_run(eng, S, H, W, dev, args.detector_iters)
+            if ref_gpu and "ms_per_step" in ref_gpu and "ms_per_batch" in detector:
+                # the stem step and the detector on its p8, per batch of S frames (device time)
+                detector["stem_plus_detector_frames_per_s"] = S / ((ms_max / args.steps + detector["ms_per_batch"]) * 1e-3)
+                detector["reference_stem_plus_detector_frames_per_s"] = S / (
+                    (ref_gpu["ms_per_step"] + detector["reference_ms_per_batch"]) * 1e-3)
+        except Exception as ex:  # report, do not fail the bench
+            detector = {"unavailable": f"{type(ex).__name__}: {str(ex)[:200]}"}
+        torch.cuda.empty_cache()
     if rank == 0 and world == 1 and not args.no_cpu:
         order = pingpong(min(args.frames, 8))
         if ref is not None:
@@ -759,7 +865,7 @@ def run_b200(args):
             "conv_mma_over_alg_per_layer": {l.dst: round(m / f, 3) if f else None
                                             for l, f, m in zip(eng.layers, flops_layer, mma_layer)},
             "cpu_baseline": cpu, "reference_gpu": ref_gpu, "e2e": e2e, "gpu_launches": launches,
-            "mask_kernels": masks, "clocks": clock_info}
+            "mask_kernels": masks, "detector": detector, "clocks": clock_info}
     print(json.dumps(line), flush=True)
 
 

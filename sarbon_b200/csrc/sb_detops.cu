@@ -178,55 +178,75 @@ __global__ void add_rows_kernel(const void* a, int a_f32, long long lda, const v
 }
 
 // ------------------------------------------------------------------ depthwise conv, upsample
-// grid (x: pixels of a row x 8-channel groups, y: row, z: image); thread per (pixel, 8
-// channels); w [9][C] fp32 (BatchNorm folded), bias [C]
-__global__ void dwconv3x3_kernel(const __half* x, long long ldx, long long imgx, int H, int W, int C, const float* w,
-                                 const float* bias, int relu, __half* y, long long ldy, long long imgy) {
-  const int cg = C >> 3;
+// grid (x: groups of kDwCols pixels of a row x 8-channel groups, y: row, z: image); a thread
+// computes kDwCols neighbouring output pixels of one row and 8 channels: per kernel row it
+// loads the kDwCols + 2 input pixels once and each tap's 8 weights once for all of them;
+// w [9][C] fp32 (BatchNorm folded), bias [C]
+constexpr int kDwCols = 4;
+__global__ void __launch_bounds__(256) dwconv3x3_kernel(const __half* x, long long ldx, long long imgx, int H, int W,
+                                                        int C, const float* w, const float* bias, int relu, __half* y,
+                                                        long long ldy, long long imgy) {
+  const int cg = C >> 3, ng = (W + kDwCols - 1) / kDwCols;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= W * cg) return;
-  const int xo = i / cg, c0 = (i - xo * cg) * 8;
-  const int yo = blockIdx.y, b = blockIdx.z;
-  float acc[8];
+  if (i >= ng * cg) return;
+  const int xg = i / cg, c0 = (i - xg * cg) * 8;
+  const int x0 = xg * kDwCols, yo = blockIdx.y, b = blockIdx.z;
+  float acc[kDwCols][8];
   {
     const float4 b0 = *reinterpret_cast<const float4*>(bias + c0), b1 = *reinterpret_cast<const float4*>(bias + c0 + 4);
-    acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
-    acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
+#pragma unroll
+    for (int o = 0; o < kDwCols; ++o) {
+      acc[o][0] = b0.x; acc[o][1] = b0.y; acc[o][2] = b0.z; acc[o][3] = b0.w;
+      acc[o][4] = b1.x; acc[o][5] = b1.y; acc[o][6] = b1.z; acc[o][7] = b1.w;
+    }
   }
   const __half* xb = x + (long long)b * imgx * ldx;
 #pragma unroll
   for (int ky = 0; ky < 3; ++ky) {
-    const int yy = yo + ky - 1;
-    if (yy < 0 || yy >= H) continue;
+    const int yi = yo + ky - 1;
+    if (yi < 0 || yi >= H) continue;
+    __half2 col[kDwCols + 2][4];
+#pragma unroll
+    for (int cidx = 0; cidx < kDwCols + 2; ++cidx) {
+      const int xx = x0 + cidx - 1;
+      uint4 raw = make_uint4(0, 0, 0, 0);
+      if (xx >= 0 && xx < W) raw = *reinterpret_cast<const uint4*>(xb + ((long long)yi * W + xx) * ldx + c0);
+      const __half2* hh = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) col[cidx][u] = hh[u];
+    }
 #pragma unroll
     for (int kx = 0; kx < 3; ++kx) {
-      const int xx = xo + kx - 1;
-      if (xx < 0 || xx >= W) continue;
-      const uint4 raw = *reinterpret_cast<const uint4*>(xb + ((long long)yy * W + xx) * ldx + c0);
-      const __half2* hh = reinterpret_cast<const __half2*>(&raw);
       const float* wt = w + (ky * 3 + kx) * C + c0;
       const float4 w0 = *reinterpret_cast<const float4*>(wt), w1 = *reinterpret_cast<const float4*>(wt + 4);
       const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float2 f = __half22float2(hh[u]);
-        acc[2 * u] = fmaf(f.x, wv[2 * u], acc[2 * u]);
-        acc[2 * u + 1] = fmaf(f.y, wv[2 * u + 1], acc[2 * u + 1]);
-      }
-    }
-  }
-  uint4 o;
-  __half2* oh = reinterpret_cast<__half2*>(&o);
+      for (int o = 0; o < kDwCols; ++o)
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    float a0 = acc[2 * u], a1 = acc[2 * u + 1];
-    if (relu) {
-      a0 = fmaxf(a0, 0.f);
-      a1 = fmaxf(a1, 0.f);
+        for (int u = 0; u < 4; ++u) {
+          const float2 f = __half22float2(col[o + kx][u]);
+          acc[o][2 * u] = fmaf(f.x, wv[2 * u], acc[o][2 * u]);
+          acc[o][2 * u + 1] = fmaf(f.y, wv[2 * u + 1], acc[o][2 * u + 1]);
+        }
     }
-    oh[u] = __floats2half2_rn(a0, a1);
   }
-  *reinterpret_cast<uint4*>(y + ((long long)b * imgy + (long long)yo * W + xo) * ldy + c0) = o;
+#pragma unroll
+  for (int o = 0; o < kDwCols; ++o) {
+    const int xo = x0 + o;
+    if (xo >= W) break;
+    uint4 ov;
+    __half2* oh = reinterpret_cast<__half2*>(&ov);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float a0 = acc[o][2 * u], a1 = acc[o][2 * u + 1];
+      if (relu) {
+        a0 = fmaxf(a0, 0.f);
+        a1 = fmaxf(a1, 0.f);
+      }
+      oh[u] = __floats2half2_rn(a0, a1);
+    }
+    *reinterpret_cast<uint4*>(y + ((long long)b * imgy + (long long)yo * W + xo) * ldy + c0) = ov;
+  }
 }
 
 // grid (x: output pixels of a row x 8-channel groups, y: output row, z: image)
@@ -659,7 +679,8 @@ extern "C" int sb_dwconv3x3(const void* x, long long ldx, long long imgx, int B,
   if ((long long)W * (C / 8) > (1ll << 30) || H > 65535 || B > 65535 || (reinterpret_cast<uintptr_t>(w) & 15) ||
       (reinterpret_cast<uintptr_t>(bias) & 15))
     return record_error(SB_EINVAL, "sb_dwconv3x3: sizes (H, B <= 65535) or unaligned weights");
-  dwconv3x3_kernel<<<dim3(blocks_for((long long)W * (C / 8), 256), H, B), 256, 0, (cudaStream_t)stream>>>(
+  dwconv3x3_kernel<<<dim3(blocks_for((long long)((W + kDwCols - 1) / kDwCols) * (C / 8), 256), H, B), 256, 0,
+                     (cudaStream_t)stream>>>(
       static_cast<const __half*>(x), ldx, imgx, H, W, C, w, bias, relu, static_cast<__half*>(y), ldy, imgy);
   SB_LAUNCH_CHECK("sb_dwconv3x3");
   return SB_OK;

@@ -22,8 +22,8 @@
 //   warp 1     tcgen05.mma issuer (M = 128, N = BN, K = 16 per instruction) into one of two
 //              TMEM accumulators (2 x 256 columns), so the epilogue of tile i overlaps the
 //              MMAs of tile i + 1;
-//   warps 2-9  epilogue: TMEM lane quadrant (warp % 4) = 32 tile rows, two warps per
-//              quadrant on alternate 16-column chunks (one tcgen05.ld each), bias /
+//   warps 2-17 epilogue: TMEM lane quadrant (warp % 4) = 32 tile rows, four warps per
+//              quadrant on every fourth 16-column chunk (one tcgen05.ld each), bias /
 //              residual / activation in fp32, fp16 or fp32 stores.
 // A tile holds R rows of Wt output pixels (R * Wt <= 128) chosen on the host so that few
 // of the 128 MMA rows idle; rows past R * Wt hold stale shared memory and are never stored.
@@ -44,7 +44,8 @@ constexpr int kMaxBN = 256;
 constexpr int kAStage = 128 * 128;            // 128 rows x 64 fp16
 constexpr int kBStage = kMaxBN * 128;         // BN rows x 64 fp16
 constexpr int kStageBytes = kAStage + kBStage;
-constexpr int kThreads = 320;  // producer, MMA issuer, 8 epilogue warps
+constexpr int kEpiWarps = 16;   // four per TMEM lane quadrant
+constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA issuer, epilogue warps
 constexpr int kBarBytes = 256;
 constexpr int kSmem = 1024 + kStages * kStageBytes + kBarBytes;
 constexpr uint32_t kTmemCols = 512;           // two accumulators of up to 256 columns
@@ -61,6 +62,7 @@ struct GemmArgs {
   uint32_t a_bytes;           // bytes one A box writes: R * Wt rows of 128 B
   long long total_tiles;
   const float* bias;          // [N] or null
+  int bias_vec;               // bias 16-byte aligned (vector loads)
   const void* res;            // residual rows (fp16 or fp32) or null
   int res_f32, res_vec;       // res_vec: rows 16-byte aligned (vector loads)
   long long res_ld, res_img;  // elements between pixels; pixels between images
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], 8);  // one arrival per epilogue warp
+      mbar_init(&acce[i], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(dbar, 1);
     *abort_flag = 0;
@@ -209,11 +211,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2-9)
+    // ---------------------------------------------------------------- epilogue (warps 2..)
     grid_dep_wait();  // residual rows written by the previous kernel of the stream
-    // warp w reads TMEM lane quadrant w % 4 (tile rows 32q..32q+31); the two warps of a
-    // quadrant take alternate 16-column chunks
-    const int q = warp & 3, half = (warp - 2) >> 2;
+    // warp w reads TMEM lane quadrant w % 4 (tile rows 32q..32q+31); the four warps of a
+    // quadrant take every fourth 16-column chunk
+    const int q = warp & 3, part = (warp - 2) >> 2;
     const int row = q * 32 + lane;
     const int r = row / a.Wt, j = row - r * a.Wt;
     for (int i = 0; i < my_tiles; ++i) {
@@ -231,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long rpix = (long long)c.b * a.res_img + (long long)yo * a.Wo + xo;
       const int nbase = c.nt * a.BN;
       const int nch = a.BN / 16;
-      for (int cc = half; cc < nch; cc += 2) {
+      for (int cc = part; cc < nch; cc += kEpiWarps / 4) {
         uint32_t v[16];
         tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * kMaxBN + cc * 16), v);
         tmem_ld_wait();
@@ -242,9 +244,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < 16; ++t) f[t] = __uint_as_float(v[t]);
         if (a.bias) {
+          if (nv == 16 && a.bias_vec) {
 #pragma unroll
-          for (int t = 0; t < 16; ++t)
-            if (t < nv) f[t] += __ldg(a.bias + n0 + t);
+            for (int t = 0; t < 16; t += 4) {
+              const float4 bb = __ldg(reinterpret_cast<const float4*>(a.bias + n0 + t));
+              f[t] += bb.x;
+              f[t + 1] += bb.y;
+              f[t + 2] += bb.z;
+              f[t + 3] += bb.w;
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              if (t < nv) f[t] += __ldg(a.bias + n0 + t);
+          }
         }
         if (a.res) {
           if (a.res_f32) {
@@ -420,6 +433,7 @@ extern "C" int sb_gemm_conv(const sb_gemm_src* src, int nsrc, int B, int H, int 
   a.a_bytes = (uint32_t)(a.R * a.Wt * 128);
   a.total_tiles = (long long)B * a.tiles_y * a.tiles_x * a.n_tiles;
   a.bias = bias;
+  a.bias_vec = bias && (reinterpret_cast<uintptr_t>(bias) & 15) == 0;
   a.res = res;
   a.res_f32 = res_dtype == SB_F32;
   a.res_vec = res && (res_ld * esz_r) % 16 == 0 && (reinterpret_cast<uintptr_t>(res) & 15) == 0;

@@ -19,8 +19,12 @@ from ._lib import check, lib
 
 ACT = {None: 0, "none": 0, "relu": 1, "gelu": 2}
 
+# kernel launches issued through this module (each op is one launch)
+LAUNCHES = [0]
+
 
 def _stream(t):
+    LAUNCHES[0] += 1
     return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
 
 
@@ -88,6 +92,16 @@ def gemm_conv(srcs, weight, bias=None, act=None, taps=1, stride=1, res=None, out
         r_ptr, r_dt = rm.data_ptr(), (_lib.SB_F32 if rm.dtype == torch.float32 else _lib.SB_F16)
     if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
         raise ValueError("bias: contiguous fp32 [N]")
+    if taps == 1 and b * h * w > w:
+        # a 1x1 conv whose operands are dense over the images is one [B*H*W, C] matrix product
+        # (its tiles are then full 128-row blocks)
+        dense = all(arr[i].img_stride == h * w for i in range(len(maps))) and o_img == h * w and \
+            (res is None or r_img == h * w)
+        if dense:
+            for i in range(len(maps)):
+                arr[i].img_stride = b * h * w
+            b, h, w = 1, 1, b * h * w
+            o_img = r_img = h * w
     check(lib().sb_gemm_conv(arr, len(maps), b, h, w, taps, stride, C.c_void_p(weight.data_ptr()), n,
                              C.c_void_p(bias.data_ptr() if bias is not None else None), ACT[act],
                              C.c_void_p(r_ptr), r_dt, r_ld, r_img, C.c_void_p(om.data_ptr()),

@@ -45,10 +45,10 @@ def test_layernorm_outputs():
     assert (y32 - ref).abs().max().item() < 1e-4
 
 
-def test_dwconv_and_upsample():
+@pytest.mark.parametrize("b,h,w,c", [(2, 24, 40, 256), (1, 23, 7, 64), (3, 1, 5, 8)])
+def test_dwconv_and_upsample(b, h, w, c):
     from sarbon_b200 import det_ops as ops
-    g = gen(2)
-    b, h, w, c = 2, 24, 40, 256
+    g = gen(2 + h)
     x = torch.randn(b, h, w, c, device="cuda", generator=g).half()
     wt = torch.randn(c, 1, 3, 3, device="cuda", generator=g) / 3
     bias = torch.randn(c, device="cuda", generator=g)

@@ -64,6 +64,11 @@ def test_linear_residual_and_strided_views(res_dtype):
     ref = x.float() @ w.float().t() + b + res.float()
     _close(out[:, 256:], ref, 1e-4)
     assert not out[:, :256].any()
+    # fp16 rows of a wider matrix (bulk tensor stores with a row pitch of 512)
+    out16 = torch.zeros(m, 512, device="cuda", dtype=torch.float16)
+    gemm_conv(x, w, b, res=res, out=out16[:, :256])
+    _close(out16[:, :256], ref, 2e-3)
+    assert not out16[:, 256:].any()
 
 
 @pytest.mark.parametrize("b,h,w,cin,cout,stride", [(2, 24, 40, 128, 256, 2), (2, 24, 40, 256, 256, 1),
@@ -132,3 +137,18 @@ def test_rejects_bad_arguments():
     w = torch.randn(16, 64, device="cuda").half()
     with pytest.raises(SarbonLibraryError):
         gemm_conv(x, w, taps=1, stride=2)
+
+
+def test_conv1x1_dense_maps_as_one_matrix():
+    """1x1 convs over dense maps (two sources, B > 1) run as one [B*H*W, C] product."""
+    from sarbon_b200.det_ops import gemm_conv
+    g = torch.Generator(device="cuda").manual_seed(17)
+    b, h, w = 3, 17, 23
+    a = torch.randn(b, h, w, 128, device="cuda", generator=g).half()
+    c = torch.randn(b, h, w, 256, device="cuda", generator=g).half()
+    wt = (torch.randn(256, 384, device="cuda", generator=g) / 384 ** 0.5).half()
+    bias = torch.randn(256, device="cuda", generator=g)
+    got = gemm_conv([a, c], wt, bias, act="relu")
+    ref = F.relu(torch.cat([a, c], -1).float() @ wt.float().t() + bias)
+    assert got.shape == (b, h, w, 256)
+    _close(got, ref, 2e-3)
