@@ -278,3 +278,46 @@ def l2norm_rows(x, out):
                                out.stride(-2), _stream(x)),
           "sb_l2norm_rows")
     return out
+
+
+def _time_one(argv):
+    """Time one sb_gemm_conv shape with CUDA events (10 launches after 4 warm-up launches):
+    ``python -m sarbon_b200.det_ops linear M K N`` or ``... conv B H W CIN COUT STRIDE``."""
+    kind, dims = argv[0], [int(x) for x in argv[1:]]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    if kind == "linear":
+        m, k, n = dims
+        x = torch.randn(m, k, device="cuda", generator=g).half()
+        w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).half()
+        out = torch.empty(m, n, device="cuda", dtype=torch.float16)
+        taps, stride, flops, act = 1, 1, 2 * m * k * n, None
+    else:
+        b, h, wd, c, n, stride = dims
+        x = torch.randn(b, h, wd, c, device="cuda", generator=g).half()
+        w = (torch.randn(n, 9 * c, device="cuda", generator=g) / (9 * c) ** 0.5).half()
+        ho, wo = (h - 1) // stride + 1, (wd - 1) // stride + 1
+        out = torch.empty(b, ho, wo, n, device="cuda", dtype=torch.float16)
+        taps, flops, act = 9, 2 * b * ho * wo * n * 9 * c, "relu"
+    bias = torch.randn(n, device="cuda", generator=g)
+
+    def run():
+        gemm_conv(x, w, bias, act=act, taps=taps, stride=stride, out=out)
+
+    for _ in range(4):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 10
+    moved = (x.numel() + out.numel()) * 2
+    print(f"{kind} {dims}: {ms * 1e3:.1f} us per launch, {flops / ms / 1e9:.1f} TFLOP/s, "
+          f"{moved / ms / 1e6:.1f} GB/s of input + output; error flags {kernels_error()}")
+
+
+if __name__ == "__main__":
+    import sys
+    _time_one(sys.argv[1:])

@@ -433,3 +433,25 @@ class B200Detector:
         if self.graph is not None and p8 is self._graph_in:
             return self.replay()
         return self.run(p8)
+
+
+def install(video):
+    """Run a reference ``SarbonVideo``'s detector on B200Detector.
+
+    ``SarbonVideo._detect`` (sarbon/inference/video.py:120-137) calls ``self._run_det(p8)``,
+    which runs ``self.det(None, p8=p8)`` under autocast, and captures it as a CUDA graph.
+    This replaces ``_run_det`` on the instance: the first call builds a B200Detector over
+    ``video.det``'s weights for p8's shape (outside the graph capture: ``_detect`` warms up
+    first), and every call launches its kernels on the current stream, so the video's own
+    graph captures and replays them.  Returns the video."""
+    state = {}
+
+    def run_det(p8):
+        d = state.get("det")
+        if d is None or (d.B, *d.shapes[0]) != (p8.shape[0], p8.shape[2], p8.shape[3]):
+            d = state["det"] = B200Detector(video.det, p8.shape[0], p8.shape[2], p8.shape[3], device=p8.device)
+        return d.run(p8)
+
+    video._run_det = run_det
+    video.b200_detector = state
+    return video
