@@ -87,6 +87,8 @@ def parse():
     p.add_argument("--no-detector", action="store_true",
                    help="skip timing the detector after the stem (B200Detector vs the reference's own)")
     p.add_argument("--detector-iters", type=int, default=20)
+    p.add_argument("--dec-layers", type=int, default=4,
+                   help="decoder layers of the detector (the 's' preset has 4; BASELINE config 5 asks for 6)")
     return p.parse_args()
 
 
@@ -378,7 +380,7 @@ def gpu_reference_run(ref, net, seq, tau, steps, dev):
             "CUDA graphs and per-step host sync) on the same frames and weights, this GPU"}
 
 
-def detector_run(eng, S, H, W, dev, iters, seed=0):
+def detector_run(eng, S, H, W, dev, iters, dec_layers=4, seed=0):
     """The detector after the stem on the engine's p8 (rank 0, N = 1): this library's
     B200Detector (one CUDA graph of sb_gemm_conv / sb_attention / ... launches) against the
     reference's own SarbonDetector under autocast, captured as a CUDA graph the way
@@ -393,7 +395,7 @@ def detector_run(eng, S, H, W, dev, iters, seed=0):
     from sarbon_b200 import det_ops
     from sarbon_b200.detector import B200Detector
     torch.manual_seed(seed)
-    det = sd.build("s", 6, halo_zero=False)
+    det = sd.build("s", 6, halo_zero=False, dec_layers=dec_layers)
     gen = torch.Generator().manual_seed(seed + 1)
     with torch.no_grad():
         for m in det.modules():
@@ -461,9 +463,10 @@ def detector_run(eng, S, H, W, dev, iters, seed=0):
            "batch": S, "p8": [int(h8), int(w8)], "queries": det.cfg.queries, "gpu_launches_per_batch": launches,
            "top_k_rows_shared_with_reference": round(shared, 4),
            "pred_boxes_max_abs_diff_forced_top_k": dbox, "pred_logits_max_abs_diff_forced_top_k": dlog,
+           "decoder_layers": dec_layers,
            "timing": f"CUDA events over {iters} graph replays after 3 warm-up replays, both arms",
-           "reference": "SarbonDetector (build('s', 6, halo_zero=False)) under torch.autocast(float16), "
-                        "captured as one CUDA graph (SarbonVideo._detect)"}
+           "reference": f"SarbonDetector (build('s', 6, halo_zero=False, dec_layers={dec_layers})) under "
+                        "torch.autocast(float16), captured as one CUDA graph (SarbonVideo._detect)"}
     del mine, g, ref_out, det
     torch.cuda.empty_cache()
     return res
@@ -808,7 +811,7 @@ def run_b200(args):
     detector = None
     if rank == 0 and world == 1 and not args.no_detector:
         try:
-            detector = detector_run(eng, S, H, W, dev, args.detector_iters)
+            detector = detector_run(eng, S, H, W, dev, args.detector_iters, args.dec_layers)
             if ref_gpu and "ms_per_step" in ref_gpu and "ms_per_batch" in detector:
                 # the stem step and the detector on its p8, per batch of S frames (device time)
                 detector["stem_plus_detector_frames_per_s"] = S / ((ms_max / args.steps + detector["ms_per_batch"]) * 1e-3)
