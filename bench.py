@@ -260,9 +260,10 @@ def make_frames(args, rank, dev, world=1):
 def workload_name(args, world):
     cam_h = args.camera_height or args.height
     res = f"{args.width}x{cam_h}" + (f" padded to {args.width}x{args.height}" if cam_h < args.height else "")
+    change = "~5% changed blocks" if not args.rects else f"{args.rects} moving rectangles per stream"
     if args.total_streams:
-        return f"{res} x {args.total_streams} streams over {world} GPU(s), ~5% changed blocks"
-    return f"{res} x {args.streams} streams/GPU, ~5% changed blocks"
+        return f"{res} x {args.total_streams} streams over {world} GPU(s), {change}"
+    return f"{res} x {args.streams} streams/GPU, {change}"
 
 
 # ----------------------------------------------------------------------------- CPU (reference algorithm)
