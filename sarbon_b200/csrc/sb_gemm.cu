@@ -422,12 +422,33 @@ extern "C" int sb_gemm_conv(const sb_gemm_src* src, int nsrc, int B, int H, int 
   a.Wo = taps == 9 ? (W + 2 - 3) / stride + 1 : W;
   if (out_img < (long long)a.Ho * a.Wo || (res && res_img < (long long)a.Ho * a.Wo))
     return record_error(SB_EINVAL, "sb_gemm_conv: out/res image stride < Ho*Wo");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return record_error(SB_ECUDA, "sb_gemm_conv: cudaGetDevice");
+  static DeviceInfo info[64];
+  static std::mutex mu;
+  int sms;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    DeviceInfo& d = info[dev & 63];
+    if (!d.attr) {
+      if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+          cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+        return record_error(SB_ECUDA, "sb_gemm_conv: device setup");
+      d.attr = true;
+    }
+    sms = d.sms;
+  }
   pick_tile(a.Ho, a.Wo, a.R, a.Wt);
   a.tiles_y = (a.Ho + a.R - 1) / a.R;
   a.tiles_x = (a.Wo + a.Wt - 1) / a.Wt;
   a.N = N;
+  // N per tile: up to 256; when the M tiles alone cannot occupy the SMs, narrower N tiles (down
+  // to 64 columns) spread the work over more CTAs, each with a shorter epilogue
+  const long long m_tiles = (long long)B * a.tiles_y * a.tiles_x;
   a.n_tiles = (N + kMaxBN - 1) / kMaxBN;
+  while (m_tiles * a.n_tiles < sms && (N + 2 * a.n_tiles - 1) / (2 * a.n_tiles) >= 64) a.n_tiles *= 2;
   a.BN = ((N + a.n_tiles - 1) / a.n_tiles + 15) / 16 * 16;
+  a.n_tiles = (N + a.BN - 1) / a.BN;
   a.KB = taps * (kch[0] + kch[1]);
   a.idesc = idesc_f16(128, a.BN);
   a.a_bytes = (uint32_t)(a.R * a.Wt * 128);
@@ -476,22 +497,6 @@ extern "C" int sb_gemm_conv(const sb_gemm_src* src, int nsrc, int B, int H, int 
       return record_error(SB_EINVAL, "sb_gemm_conv: weight tensor map");
   }
 
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return record_error(SB_ECUDA, "sb_gemm_conv: cudaGetDevice");
-  static DeviceInfo info[64];
-  static std::mutex mu;
-  int sms;
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    DeviceInfo& d = info[dev & 63];
-    if (!d.attr) {
-      if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-          cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
-        return record_error(SB_ECUDA, "sb_gemm_conv: device setup");
-      d.attr = true;
-    }
-    sms = d.sms;
-  }
   const long long grid = std::min<long long>(a.total_tiles, sms);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)grid);
