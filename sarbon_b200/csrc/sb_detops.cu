@@ -547,7 +547,9 @@ __global__ void box_enc_kernel(const __half* encbox, long long ldb, const __half
 //   layer i > 0: corners = fp16(head(x) + corners)
 //   box = distance2bbox(ref_init, integral(corners), reg_scale)   [fp32 points]
 // integral: softmax over the R+1 bins of each edge (fp32), then the fp16 product with the
-// bin values (fp32 accumulation of fp16 operands).  Thread per (row, edge).
+// bin values (fp32 accumulation of fp16 operands).  Thread per (row, edge); with RC > 0 bins
+// known at compile time the edge's bins stay in registers (independent loads, one exp each).
+template <int RC>
 __global__ void box_dec_kernel(int first, const __half* prebox, long long ldp, const __half* ref16,
                                const __half* head, long long ldh, __half* corners, long long ldc, int R1,
                                const float* project, float reg_scale, float* ref_init, float* box, __half* qin,
@@ -557,31 +559,56 @@ __global__ void box_dec_kernel(int first, const __half* prebox, long long ldp, c
   const int r = active ? t >> 2 : 0, e = t & 3;
   float dist = 0.f;
   if (active) {
-  // this thread's edge distribution
-  float mx = -INFINITY;
-  for (int j = 0; j < R1; ++j) {
-    const long long o = (long long)r * ldc + e * R1 + j;
-    float c = __half2float(head[(long long)r * ldh + e * R1 + j]);
-    if (!first) c = r16(c + __half2float(corners[o]));
-    corners[o] = __float2half_rn(c);
-    mx = fmaxf(mx, c);
-  }
-  float den = 0.f;
-  for (int j = 0; j < R1; ++j) den += expf(__half2float(corners[(long long)r * ldc + e * R1 + j]) - mx);
-  for (int j = 0; j < R1; ++j) {
-    const float p = expf(__half2float(corners[(long long)r * ldc + e * R1 + j]) - mx) / den;
-    dist = fmaf(r16(p), r16(project[j]), dist);
-  }
-  dist = r16(dist);
-  if (first) {
-    // pre = sigmoid(prebox + inverse_sigmoid(ref)); inverse_sigmoid on the fp16 box:
-    // clamp(1e-5, 1 - 1e-5) and x / (1 - x) in fp16, the log in fp32
-    const float x = __half2float(ref16[(long long)r * 4 + e]);
-    const float xc = r16(fminf(fmaxf(x, 1e-5f), 1.f - 1e-5f));
-    const float inv = logf(r16(xc / r16(1.f - xc)));
-    const float pre = 1.f / (1.f + expf(-(__half2float(prebox[(long long)r * ldp + e]) + inv)));
-    ref_init[(long long)r * 4 + e] = pre;
-  }
+    const __half* hp = head + (long long)r * ldh + e * R1;
+    __half* cp = corners + (long long)r * ldc + e * R1;
+    if constexpr (RC > 0) {
+      float c[RC];
+#pragma unroll
+      for (int j = 0; j < RC; ++j) c[j] = __half2float(hp[j]);
+      if (!first) {
+#pragma unroll
+        for (int j = 0; j < RC; ++j) c[j] = r16(c[j] + __half2float(cp[j]));
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < RC; ++j) {
+        cp[j] = __float2half_rn(c[j]);
+        c[j] = __half2float(__float2half_rn(c[j]));
+        mx = fmaxf(mx, c[j]);
+      }
+      float den = 0.f;
+#pragma unroll
+      for (int j = 0; j < RC; ++j) {
+        c[j] = expf(c[j] - mx);
+        den += c[j];
+      }
+#pragma unroll
+      for (int j = 0; j < RC; ++j) dist = fmaf(r16(c[j] / den), r16(project[j]), dist);
+    } else {
+      float mx = -INFINITY;
+      for (int j = 0; j < R1; ++j) {
+        float c = __half2float(hp[j]);
+        if (!first) c = r16(c + __half2float(cp[j]));
+        cp[j] = __float2half_rn(c);
+        mx = fmaxf(mx, c);
+      }
+      float den = 0.f;
+      for (int j = 0; j < R1; ++j) den += expf(__half2float(cp[j]) - mx);
+      for (int j = 0; j < R1; ++j) {
+        const float p = expf(__half2float(cp[j]) - mx) / den;
+        dist = fmaf(r16(p), r16(project[j]), dist);
+      }
+    }
+    dist = r16(dist);
+    if (first) {
+      // pre = sigmoid(prebox + inverse_sigmoid(ref)); inverse_sigmoid on the fp16 box:
+      // clamp(1e-5, 1 - 1e-5) and x / (1 - x) in fp16, the log in fp32
+      const float x = __half2float(ref16[(long long)r * 4 + e]);
+      const float xc = r16(fminf(fmaxf(x, 1e-5f), 1.f - 1e-5f));
+      const float inv = logf(r16(xc / r16(1.f - xc)));
+      const float pre = 1.f / (1.f + expf(-(__half2float(prebox[(long long)r * ldp + e]) + inv)));
+      ref_init[(long long)r * 4 + e] = pre;
+    }
   }
   __syncwarp();
   // the four edges of the row are the four consecutive threads t = 4r + e
@@ -789,7 +816,8 @@ extern "C" int sb_box_dec(int first, const void* prebox, long long ldp, const vo
   if (!head || !corners || !project || !ref_init || !box || rows < 1 || R1 < 2 || (first && (!prebox || !ref16)))
     return record_error(SB_EINVAL, "sb_box_dec: arguments");
   // four threads per row, rows never straddle a warp (256 threads = 64 rows per block)
-  box_dec_kernel<<<blocks_for((long long)rows * 4, 256), 256, 0, (cudaStream_t)stream>>>(
+  auto kern = R1 == 33 ? box_dec_kernel<33> : box_dec_kernel<0>;  // 33 bins: reg_max = 32, the config default
+  kern<<<blocks_for((long long)rows * 4, 256), 256, 0, (cudaStream_t)stream>>>(
       first, static_cast<const __half*>(prebox), ldp, static_cast<const __half*>(ref16),
       static_cast<const __half*>(head), ldh, static_cast<__half*>(corners), ldc, R1, project, reg_scale, ref_init, box,
       static_cast<__half*>(qin), ldq, rows);
