@@ -414,9 +414,10 @@ SB_API int sb_attention(const void* q, long long ldq, long long imgq, const void
 SB_API int sb_topk_rows(const void* logits, long long ld, long long img, int B, int S, int C, const void* valid, int K,
                         void* idx, long long ldi, void* stream);
 
-/* out[b][i] = src[b][idx[b * ldi + i]] over D columns (sarbon_det.py:315-320); fp32 (o32)
- * and/or fp16 (o16) outputs. */
-SB_API int sb_gather_rows(const void* src, int src_dtype, long long lds, long long imgs, const void* idx, long long ldi,
+/* out[b][i] = src[b][idx[b * ldi + i]] over D columns (sarbon_det.py:315-320) for the S rows
+ * of each image (an index outside [0, S) gives a zero row); fp32 (o32) and/or fp16 (o16)
+ * outputs. */
+SB_API int sb_gather_rows(const void* src, int src_dtype, long long lds, long long imgs, int S, const void* idx, long long ldi,
                           int B, int K, int D, float* o32, long long ld32, long long img32, void* o16, long long ld16,
                           long long img16, void* stream);
 
@@ -431,9 +432,9 @@ SB_API int sb_deform_sample(const void* value, long long ldv, long long imgv, co
                             void* out, long long ldo, long long imgo, void* stream);
 
 /* Encoder proposals of the selected rows (sarbon_det.py:316-321): ref16 [B*K][4] =
- * fp16(sigmoid(fp16(encbox + anchors[idx]))) (anchors fp16 [S][4]); qin [B*K][ldq] gets the
- * same 4 values (the query_pos input). */
-SB_API int sb_box_enc(const void* encbox, long long ldb, const void* anchors, const void* idx, int B, int K, void* ref16,
+ * fp16(sigmoid(fp16(encbox + anchors[idx]))) (anchors fp16 [S][4]; an index outside [0, S)
+ * takes a zero anchor); qin [B*K][ldq] gets the same 4 values (the query_pos input). */
+SB_API int sb_box_enc(const void* encbox, long long ldb, const void* anchors, int S, const void* idx, int B, int K, void* ref16,
                       void* qin, long long ldq, void* stream);
 
 /* Decoder box of one layer (sarbon_det.py:336-350, box_ops.py:78-106): first != 0 computes

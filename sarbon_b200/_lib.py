@@ -101,10 +101,10 @@ PROTOTYPES = {
     "sb_upsample2x": (_I, [_P, _LL, _LL, _I, _I, _I, _I, _P, _LL, _LL, _P]),
     "sb_attention": (_I, [_P, _LL, _LL, _P, _LL, _LL, _P, _LL, _LL, _I, _I, _I, _I, _I, _P, _LL, _LL, _P]),
     "sb_topk_rows": (_I, [_P, _LL, _LL, _I, _I, _I, _P, _I, _P, _LL, _P]),
-    "sb_gather_rows": (_I, [_P, _I, _LL, _LL, _P, _LL, _I, _I, _I, _P, _LL, _LL, _P, _LL, _LL, _P]),
+    "sb_gather_rows": (_I, [_P, _I, _LL, _LL, _I, _P, _LL, _I, _I, _I, _P, _LL, _LL, _P, _LL, _LL, _P]),
     "sb_deform_sample": (_I, [_P, _LL, _LL, C.POINTER(_I), _I, _P, _LL, _LL, _P, _LL, _LL, _P, _I, _LL, _LL, _I, _I, _I,
                               _I, _P, _LL, _LL, _P]),
-    "sb_box_enc": (_I, [_P, _LL, _P, _P, _I, _I, _P, _P, _LL, _P]),
+    "sb_box_enc": (_I, [_P, _LL, _P, _I, _P, _I, _I, _P, _P, _LL, _P]),
     "sb_box_dec": (_I, [_I, _P, _LL, _P, _P, _LL, _P, _LL, _I, _P, C.c_float, _P, _P, _P, _LL, _I, _P]),
     "sb_l2norm_rows": (_I, [_P, _LL, _I, _I, _P, _LL, _P]),
     "sb_stats": (_I, [_P, _P, C.POINTER(Stats)]),

@@ -400,17 +400,18 @@ __global__ void __launch_bounds__(kTopkThreads) topk_kernel(const __half* logits
 }
 
 // ------------------------------------------------------------------ gather
-// out[b, i, :] = src[b, idx[b, i], :] for D columns; fp32 and/or fp16 outputs
-__global__ void gather_rows_kernel(const void* src, int s_f32, long long lds, long long imgs, const int32_t* idx,
-                                   long long ldi, int B, int K, int D, float* o32, long long ld32, long long img32,
-                                   __half* o16, long long ld16, long long img16) {
+// out[b, i, :] = src[b, idx[b, i], :] for D columns (zeros for an index outside [0, S));
+// fp32 and/or fp16 outputs
+__global__ void gather_rows_kernel(const void* src, int s_f32, long long lds, long long imgs, int S,
+                                   const int32_t* idx, long long ldi, int B, int K, int D, float* o32, long long ld32,
+                                   long long img32, __half* o16, long long ld16, long long img16) {
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= (long long)B * K * D) return;
   const int c = (int)(t % D);
   const long long r = t / D;
   const int i = (int)(r % K), b = (int)(r / K);
   const int row = idx[(long long)b * ldi + i];
-  const float x = ld_any(src, s_f32, ((long long)b * imgs + row) * lds + c);
+  const float x = row >= 0 && row < S ? ld_any(src, s_f32, ((long long)b * imgs + row) * lds + c) : 0.f;
   if (o32) o32[((long long)b * img32 + i) * ld32 + c] = x;
   if (o16) o16[((long long)b * img16 + i) * ld16 + c] = __float2half_rn(x);
 }
@@ -528,14 +529,15 @@ __global__ void __launch_bounds__(256) deform_sample_kernel(DeformSampleArgs a) 
 // ------------------------------------------------------------------ box heads
 // Encoder proposals (sarbon_det.py:316-321): ref_logit = fp16(enc_box(x) + anchor[row]);
 // ref = fp16(sigmoid(ref_logit)); also the query_pos input (ref as fp16 in a 64-wide row).
-__global__ void box_enc_kernel(const __half* encbox, long long ldb, const __half* anchors, const int32_t* idx, int B,
-                               int K, __half* ref16, __half* qin, long long ldq) {
+// (an index outside [0, S) takes an anchor of 0)
+__global__ void box_enc_kernel(const __half* encbox, long long ldb, const __half* anchors, int S, const int32_t* idx,
+                               int B, int K, __half* ref16, __half* qin, long long ldq) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= B * K * 4) return;
-  const int c = t & 3, r = t >> 2, b = r / K;
+  const int c = t & 3, r = t >> 2;
   const int row = idx[r];
-  (void)b;
-  const float lg = r16(__half2float(encbox[(long long)r * ldb + c]) + __half2float(anchors[(long long)row * 4 + c]));
+  const float an = row >= 0 && row < S ? __half2float(anchors[(long long)row * 4 + c]) : 0.f;
+  const float lg = r16(__half2float(encbox[(long long)r * ldb + c]) + an);
   const __half v = __float2half_rn(1.f / (1.f + expf(-lg)));
   ref16[(long long)r * 4 + c] = v;
   qin[(long long)r * ldq + c] = v;
@@ -746,12 +748,13 @@ extern "C" int sb_topk_rows(const void* logits, long long ld, long long img, int
   return SB_OK;
 }
 
-extern "C" int sb_gather_rows(const void* src, int src_dtype, long long lds, long long imgs, const void* idx,
+extern "C" int sb_gather_rows(const void* src, int src_dtype, long long lds, long long imgs, int S, const void* idx,
                               long long ldi, int B, int K, int D, float* o32, long long ld32, long long img32, void* o16,
                               long long ld16, long long img16, void* stream) {
-  if (!src || !idx || B < 1 || K < 1 || D < 1 || (!o32 && !o16)) return record_error(SB_EINVAL, "sb_gather_rows: arguments");
+  if (!src || !idx || B < 1 || K < 1 || D < 1 || S < 1 || S > imgs || (!o32 && !o16))
+    return record_error(SB_EINVAL, "sb_gather_rows: arguments");
   gather_rows_kernel<<<blocks_for((long long)B * K * D, 256), 256, 0, (cudaStream_t)stream>>>(
-      src, src_dtype == SB_F32, lds, imgs, static_cast<const int32_t*>(idx), ldi, B, K, D, o32, ld32, img32,
+      src, src_dtype == SB_F32, lds, imgs, S, static_cast<const int32_t*>(idx), ldi, B, K, D, o32, ld32, img32,
       static_cast<__half*>(o16), ld16, img16);
   SB_LAUNCH_CHECK("sb_gather_rows");
   return SB_OK;
@@ -800,12 +803,13 @@ extern "C" int sb_deform_sample(const void* value, long long ldv, long long imgv
   return SB_OK;
 }
 
-extern "C" int sb_box_enc(const void* encbox, long long ldb, const void* anchors, const void* idx, int B, int K,
+extern "C" int sb_box_enc(const void* encbox, long long ldb, const void* anchors, int S, const void* idx, int B, int K,
                           void* ref16, void* qin, long long ldq, void* stream) {
-  if (!encbox || !anchors || !idx || !ref16 || !qin || B < 1 || K < 1) return record_error(SB_EINVAL, "sb_box_enc: arguments");
+  if (!encbox || !anchors || !idx || !ref16 || !qin || B < 1 || K < 1 || S < 1)
+    return record_error(SB_EINVAL, "sb_box_enc: arguments");
   box_enc_kernel<<<blocks_for((long long)B * K * 4, 256), 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const __half*>(encbox), ldb, static_cast<const __half*>(anchors), static_cast<const int32_t*>(idx), B,
-      K, static_cast<__half*>(ref16), static_cast<__half*>(qin), ldq);
+      static_cast<const __half*>(encbox), ldb, static_cast<const __half*>(anchors), S,
+      static_cast<const int32_t*>(idx), B, K, static_cast<__half*>(ref16), static_cast<__half*>(qin), ldq);
   SB_LAUNCH_CHECK("sb_box_enc");
   return SB_OK;
 }

@@ -226,8 +226,10 @@ def gather_rows(src, idx, o32=None, o16=None):
     ps, ls, is_ = _rows(src, "src")
     a32 = _rows(o32, "o32") if o32 is not None else (None, 0, 0)
     a16 = _rows(o16, "o16") if o16 is not None else (None, 0, 0)
-    check(lib().sb_gather_rows(C.c_void_p(ps), _dt(src), ls, is_, C.c_void_p(idx.data_ptr()), idx.stride(0), b, kk, d,
-                               C.c_void_p(a32[0]), a32[1], a32[2], C.c_void_p(a16[0]), a16[1], a16[2], _stream(src)),
+    rows = src.shape[-2]
+    check(lib().sb_gather_rows(C.c_void_p(ps), _dt(src), ls, is_, rows, C.c_void_p(idx.data_ptr()), idx.stride(0), b,
+                               kk, d, C.c_void_p(a32[0]), a32[1], a32[2], C.c_void_p(a16[0]), a16[1], a16[2],
+                               _stream(src)),
           "sb_gather_rows")
 
 
@@ -254,8 +256,8 @@ def deform_sample(value, shapes, off, att, ref, heads, points, out=None):
 def box_enc(encbox, anchors, idx, ref16, qin):
     b, kk = idx.shape
     check(lib().sb_box_enc(C.c_void_p(encbox.data_ptr()), encbox.stride(-2), C.c_void_p(anchors.data_ptr()),
-                           C.c_void_p(idx.data_ptr()), b, kk, C.c_void_p(ref16.data_ptr()), C.c_void_p(qin.data_ptr()),
-                           qin.stride(-2), _stream(encbox)),
+                           anchors.shape[0], C.c_void_p(idx.data_ptr()), b, kk, C.c_void_p(ref16.data_ptr()),
+                           C.c_void_p(qin.data_ptr()), qin.stride(-2), _stream(encbox)),
           "sb_box_enc")
 
 

@@ -394,6 +394,9 @@ class B200Detector:
     def run(self, p8):
         """p8: [B, C8, h8, w8] (NCHW view of an NHWC map, as the engine's outputs_nchw gives,
         or any layout; fp16 or fp32) -> output dict (views of this object's buffers)."""
+        want = (self.B, self.c8, *self.shapes[0])
+        if tuple(p8.shape) != want or not p8.is_cuda:
+            raise ValueError(f"p8: expected a CUDA tensor of shape {want}, got {tuple(p8.shape)}")
         x = p8.permute(0, 2, 3, 1)
         if x.dtype != torch.float16 or not x.is_contiguous():
             x = x.contiguous().half()

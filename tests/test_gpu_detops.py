@@ -110,6 +110,11 @@ def test_gather_rows():
     ops.gather_rows(src, idx, o32=o32, o16=o16)
     ref = torch.gather(src, 1, idx.long()[..., None].expand(-1, -1, 256))
     assert torch.equal(o32, ref) and torch.equal(o16, ref.half())
+    # an index outside the image's rows gives a zero row, not a read past them
+    idx[0, 0], idx[1, 5] = 500, -1
+    ops.gather_rows(src, idx, o32=o32)
+    assert not o32[0, 0].any() and not o32[1, 5].any()
+    assert torch.equal(o32[0, 1:], ref[0, 1:])
 
 
 @pytest.mark.parametrize("ref_dtype", [torch.float16, torch.float32])
