@@ -49,6 +49,12 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;  // producer, MMA issuer, epilogue
 constexpr int kBarBytes = 256;
 constexpr int kSmem = 1024 + kStages * kStageBytes + kBarBytes;
 constexpr uint32_t kTmemCols = 512;           // two accumulators of up to 256 columns
+// Weights-resident mode (KB * BN * 128 bytes <= kBResBytes, several tiles per CTA): the grid is
+// a multiple of n_tiles so every CTA keeps one N tile; its whole B tile (all K-blocks) is
+// loaded once into the upper part of the stage area and only A boxes stream through a
+// ring of kStages 16 KB stages below it.
+constexpr int kBResOff = kStages * kAStage;                   // 64 KB
+constexpr int kBResBytes = kStages * kStageBytes - kBResOff;  // 128 KB
 
 // sticky error word of the detector kernels (SB_ERR_* bits), read by sb_kernels_error
 __device__ int g_kernel_error;
@@ -70,6 +76,7 @@ struct GemmArgs {
   int out_f32, out_vec;       // out_vec: rows 16-byte aligned (vector stores)
   long long out_ld, out_img;
   int act;                    // 0 none, 1 ReLU, 2 GELU (erf form)
+  int bres;                   // weights resident: the CTA's whole B tile loaded once (see below)
 };
 
 SB_DEV float act_of(float v, int act) {
@@ -103,7 +110,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accf = empty + kStages;  // [2] accumulator ready
   uint64_t* acce = accf + 2;         // [2] accumulator drained by the epilogue
   uint64_t* dbar = acce + 2;         // drain of the MMA issuer
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(dbar + 1);
+  uint64_t* wfull = dbar + 1;        // weights-resident mode: the B tile has landed
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(wfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   const int warp = warp_id(), lane = lane_id();
 
@@ -117,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acce[i], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(dbar, 1);
+    mbar_init(wfull, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -142,6 +151,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     grid_dep_wait();  // inputs written by the previous kernel of the stream are complete
     uint32_t g = 0;
     bool ok = true;
+    const int stage_bytes = a.bres ? kAStage : kStageBytes;
+    if (a.bres && my_tiles > 0) {
+      if (lane == 0) {  // this CTA's N tile, every K-block, once
+        const int nt = (int)(blockIdx.x % a.n_tiles);
+        mbar_arrive_expect_tx(wfull, (uint32_t)(a.KB * a.BN * 128));
+        for (int kb = 0; kb < a.KB; ++kb)
+          tma_load_2d(smem + kBResOff + kb * a.BN * 128, &mapw, wfull, kb * 64, nt * a.BN);
+      }
+      __syncwarp();
+    }
     for (int i = 0; ok && i < my_tiles; ++i) {
       const TileCoord c = tile_coord(a, (long long)blockIdx.x + (long long)i * gridDim.x);
       const int xs = c.tx * a.Wt * a.stride - a.pad, ys = c.ty * a.R * a.stride - a.pad;
@@ -156,11 +175,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const int tap = kb / kch, cc = kb - tap * kch;
           const int ky = a.taps == 9 ? tap / 3 : 0, kx = a.taps == 9 ? tap % 3 : 0;
-          uint8_t* sa = smem + s * kStageBytes;
-          mbar_arrive_expect_tx(&full[s], a.a_bytes + (uint32_t)a.BN * 128u);
+          uint8_t* sa = smem + s * stage_bytes;
+          mbar_arrive_expect_tx(&full[s], a.a_bytes + (a.bres ? 0u : (uint32_t)a.BN * 128u));
           if (cc < a.kch0) tma_load_4d(sa, &map0, &full[s], cc * 64, xs + kx, ys + ky, c.b);
           else tma_load_4d(sa, &map1, &full[s], (cc - a.kch0) * 64, xs + kx, ys + ky, c.b);
-          tma_load_2d(sa + kAStage, &mapw, &full[s], kb * 64, c.nt * a.BN);
+          if (!a.bres) tma_load_2d(sa + kAStage, &mapw, &full[s], kb * 64, c.nt * a.BN);
         }
         __syncwarp();
       }
@@ -169,14 +188,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int never = 0;
     const uint32_t first = g > (uint32_t)kStages ? g - kStages : 0u;
     for (uint32_t q = first; q < g; ++q) warp_wait(&full[q % kStages], (q / kStages) & 1u, &never);
+    if (a.bres && my_tiles > 0) warp_wait(wfull, 0, &never);
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint64_t a_desc0 = smem_desc(smem_u32(smem), 1024, 2);
-      const uint64_t b_desc0 = smem_desc(smem_u32(smem + kAStage), 1024, 2);
-      constexpr uint32_t SSTEP = kStageBytes >> 4;
+      const uint64_t b_desc0 = smem_desc(smem_u32(smem + (a.bres ? kBResOff : kAStage)), 1024, 2);
+      const uint32_t SSTEP = (uint32_t)(a.bres ? kAStage : kStageBytes) >> 4;
+      const uint32_t BSTEP = a.bres ? (uint32_t)(a.BN * 128) >> 4 : 0u;  // resident B: per K-block
       uint32_t g = 0;
-      bool ok = true;
+      bool ok = my_tiles == 0 || !a.bres || mbar_wait(wfull, 0, abort_flag);
+      if (!ok) {
+        atomicOr(&g_kernel_error, SB_ERR_TIMEOUT_WGT);
+        *abort_flag = 1;
+      }
       for (int i = 0; ok && i < my_tiles; ++i) {
         const int ab = i & 1;
         if (!mbar_wait(&acce[ab], ((i >> 1) & 1) ^ 1, abort_flag)) {
@@ -195,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t ad = a_desc0 + s * SSTEP, bd = b_desc0 + s * SSTEP;
+          const uint64_t ad = a_desc0 + s * SSTEP, bd = a.bres ? b_desc0 + kb * BSTEP : b_desc0 + s * SSTEP;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // K = 16 per MMA: 32 bytes along the swizzled row
             mma_f16_ss(d_tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), a.idesc, (kb | kk) != 0 ? 1u : 0u);
@@ -497,7 +522,15 @@ extern "C" int sb_gemm_conv(const sb_gemm_src* src, int nsrc, int B, int H, int 
       return record_error(SB_EINVAL, "sb_gemm_conv: weight tensor map");
   }
 
-  const long long grid = std::min<long long>(a.total_tiles, sms);
+  long long grid = std::min<long long>(a.total_tiles, sms);
+  a.bres = 0;
+  if ((long long)a.KB * a.BN * 128 <= kBResBytes && grid >= a.n_tiles) {
+    const long long g2 = grid / a.n_tiles * a.n_tiles;  // every CTA keeps one N tile
+    if (a.total_tiles >= 2 * g2) {                      // worth it with several tiles per CTA
+      grid = g2;
+      a.bres = 1;
+    }
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3(kThreads);

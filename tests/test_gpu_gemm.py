@@ -152,3 +152,18 @@ def test_conv1x1_dense_maps_as_one_matrix():
     ref = F.relu(torch.cat([a, c], -1).float() @ wt.float().t() + bias)
     assert got.shape == (b, h, w, 256)
     _close(got, ref, 2e-3)
+
+
+@pytest.mark.parametrize("m,k,n", [(40000, 256, 256), (20000, 256, 1024), (30001, 128, 96)])
+def test_linear_weights_resident(m, k, n):
+    """Many tiles per CTA with K * BN <= 1024: every CTA keeps one N tile's weights resident
+    and streams only A (grid a multiple of the N tiles)."""
+    from sarbon_b200.det_ops import gemm_conv
+    g = torch.Generator(device="cuda").manual_seed(m + n)
+    x = torch.randn(m, k, device="cuda", generator=g).half()
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).half()
+    b = torch.randn(n, device="cuda", generator=g)
+    res = torch.randn(m, n, device="cuda", generator=g).half()
+    ref = F.relu(x.float() @ w.float().t() + b + res.float())
+    got = gemm_conv(x, w, b, act="relu", res=res, out_dtype=torch.float32)
+    _close(got, ref, 1e-4)
