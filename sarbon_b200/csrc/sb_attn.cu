@@ -7,11 +7,14 @@
 //
 // Flash-attention layout on the tensor cores (mma.sync m16n8k16, fp16 operands, fp32
 // accumulation), dh = 32: a CTA of 4 warps takes 64 queries of one (image, head), each warp
-// 16 of them with its Q fragments in registers; key / value tiles of 64 rows are staged in
-// shared memory (V transposed, rows padded so that fragment loads hit 32 distinct banks).
-// Per tile: S = Q K^T (8 x 2 MMAs), scaled to base 2, masked past Tk, online softmax in
-// fp32 with one rescale of the running row sums and outputs, P rounded to fp16 and reused
-// in registers as the A operand of O += P V (4 x 4 MMAs).
+// 16 of them with its Q fragments in registers.  Key / value tiles of 64 rows are
+// double-buffered in shared memory by cp.async (rows past Tk zero-filled), so the next
+// tile's copy overlaps this tile's math; K and V keep their row-major [key][dim] layout
+// (rows padded to 80 bytes, so the eight 16-byte rows an ldmatrix phase reads fall in
+// distinct banks) and the B fragments come from ldmatrix (K) and ldmatrix.trans (V).
+// Per tile: S = Q K^T (8 x 2 MMAs), masked past Tk on the last tile, online softmax in fp32
+// (p = 2^(s * scale * log2 e - m), one FFMA and one ex2 per score), P rounded to fp16 and
+// reused in registers as the A operand of O += P V (4 x 4 MMAs).
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -21,11 +24,10 @@
 namespace sb {
 namespace {
 
-constexpr int kQ = 64;      // queries per CTA
+constexpr int kQ = 64;      // queries per CTA (4 warps)
 constexpr int kKT = 64;     // keys per tile
 constexpr int kDH = 32;
-constexpr int kKPad = 40;   // sK row: 32 dims + 8 pad (halves)
-constexpr int kVPad = 72;   // sVt row: 64 keys + 8 pad (halves)
+constexpr int kPad = 40;    // shared row: 32 dims + 8 pad (halves)
 
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -39,13 +41,38 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+__device__ __forceinline__ uint32_t saddr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// 16-byte global -> shared copy; `bytes` = 0 writes zeros and reads nothing
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
 __global__ void __launch_bounds__(128) flash_attention_kernel(const __half* q, long long ldq, long long imgq,
                                                               const __half* k, long long ldk, long long imgk,
                                                               const __half* v, long long ldv, long long imgv, int Tq,
                                                               int Tk, float scale_log2, __half* out, long long ldo,
                                                               long long imgo) {
-  __shared__ __align__(16) __half sK[kKT][kKPad];
-  __shared__ __align__(16) __half sVt[kDH][kVPad];
+  __shared__ __align__(128) __half sK[2][kKT][kPad];
+  __shared__ __align__(128) __half sV[2][kKT][kPad];
   const int h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tig = lane & 3;
@@ -53,6 +80,20 @@ __global__ void __launch_bounds__(128) flash_attention_kernel(const __half* q, l
   const __half* qb = q + (long long)b * imgq * ldq + h * kDH;
   const __half* kb = k + (long long)b * imgk * ldk + h * kDH;
   const __half* vb = v + (long long)b * imgv * ldv + h * kDH;
+
+  // one tile: 64 rows x four 16-byte pieces of K and of V
+  auto load_tile = [&](int t0, int buf) {
+    for (int pce = threadIdx.x; pce < kKT * 4; pce += 128) {
+      const int r = pce >> 2, c = (pce & 3) * 8;
+      const bool ok = t0 + r < Tk;
+      const long long row = ok ? t0 + r : 0;
+      cp_async16(saddr(&sK[buf][r][c]), kb + row * ldk + c, ok ? 16 : 0);
+      cp_async16(saddr(&sV[buf][r][c]), vb + row * ldv + c, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  const int ntiles = (Tk + kKT - 1) / kKT;
+  load_tile(0, 0);
 
   // Q fragments of the two 16-dim k-steps
   uint32_t qa[2][4];
@@ -69,55 +110,54 @@ __global__ void __launch_bounds__(128) flash_attention_kernel(const __half* q, l
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[i][j] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // running maxima of the raw scores
+  // ldmatrix row addresses of this lane: K rows nt*8 + (lane & 7), dims (lane >> 3) * 8;
+  // V rows ks*16 + ((lane >> 3) & 1) * 8 + (lane & 7), dims p*16 + (lane >> 4) * 8
+  const int krow = lane & 7, kcol = (lane >> 3) * 8;
+  const int vrow = ((lane >> 3) & 1) * 8 + (lane & 7), vcol = (lane >> 4) * 8;
 
-  for (int t0 = 0; t0 < Tk; t0 += kKT) {
-    __syncthreads();  // the previous tile's fragments have been read
-    for (int pce = threadIdx.x; pce < kKT * 4; pce += 128) {
-      const int r = pce >> 2, c = (pce & 3) * 8;
-      uint4 kr = make_uint4(0, 0, 0, 0), vr = make_uint4(0, 0, 0, 0);
-      if (t0 + r < Tk) {
-        kr = *reinterpret_cast<const uint4*>(kb + (long long)(t0 + r) * ldk + c);
-        vr = *reinterpret_cast<const uint4*>(vb + (long long)(t0 + r) * ldv + c);
-      }
-      *reinterpret_cast<uint4*>(&sK[r][c]) = kr;
-      const __half* vh = reinterpret_cast<const __half*>(&vr);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) sVt[c + u][r] = vh[u];
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1, t0 = t * kKT;
+    if (t + 1 < ntiles) {
+      load_tile(t0 + kKT, buf ^ 1);  // that buffer was released by the barrier ending tile t - 1
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
-    __syncthreads();
+    __syncthreads();  // tile t is in shared memory for every thread
     // S = Q K^T for 8 groups of 8 keys
     float s[8][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
+      uint32_t kf[4];
+      ldsm_x4(saddr(&sK[buf][nt * 8 + krow][kcol]), kf);
       s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      mma16816(s[nt], qa[0], kf[0], kf[1]);
+      mma16816(s[nt], qa[1], kf[2], kf[3]);
+    }
+    if (t0 + kKT > Tk) {  // the last tile: keys past Tk do not take part
 #pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sK[nt * 8 + g][ks * 16 + 2 * tig]);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sK[nt * 8 + g][ks * 16 + 8 + 2 * tig]);
-        mma16816(s[nt], qa[ks], b0, b1);
+      for (int nt = 0; nt < 8; ++nt) {
+        const int key = t0 + nt * 8 + 2 * tig;
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          if (key + e >= Tk) s[nt][e] = s[nt][2 + e] = -INFINITY;
       }
     }
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      const int key = t0 + nt * 8 + 2 * tig;
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const bool ok = key + e < Tk;
-        s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
-        s[nt][2 + e] = ok ? s[nt][2 + e] * scale_log2 : -INFINITY;
-        mx0 = fmaxf(mx0, s[nt][e]);
-        mx1 = fmaxf(mx1, s[nt][2 + e]);
-      }
+      mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
     }
 #pragma unroll
     for (int x = 1; x <= 2; x <<= 1) {
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xFFFFFFFFu, mx0, x));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xFFFFFFFFu, mx1, x));
     }
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);  // 0 on the first tile
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);  // finite: a tile holds a key < Tk
+    const float ms0 = mn0 * scale_log2, ms1 = mn1 * scale_log2;
+    const float c0 = exp2f(m0 * scale_log2 - ms0), c1 = exp2f(m1 * scale_log2 - ms1);  // 0 on the first tile
     l0 *= c0;
     l1 *= c1;
 #pragma unroll
@@ -130,8 +170,8 @@ __global__ void __launch_bounds__(128) flash_attention_kernel(const __half* q, l
     uint32_t pa[8][2];  // P rounded to fp16: rows g (index 0) and g + 8 (index 1)
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      const float p0 = exp2f(s[nt][0] - mn0), p1 = exp2f(s[nt][1] - mn0);
-      const float p2 = exp2f(s[nt][2] - mn1), p3 = exp2f(s[nt][3] - mn1);
+      const float p0 = exp2f(fmaf(s[nt][0], scale_log2, -ms0)), p1 = exp2f(fmaf(s[nt][1], scale_log2, -ms0));
+      const float p2 = exp2f(fmaf(s[nt][2], scale_log2, -ms1)), p3 = exp2f(fmaf(s[nt][3], scale_log2, -ms1));
       l0 += p0 + p1;
       l1 += p2 + p3;
       pa[nt][0] = pack_half2(p0, p1);
@@ -139,17 +179,19 @@ __global__ void __launch_bounds__(128) flash_attention_kernel(const __half* q, l
     }
     m0 = mn0;
     m1 = mn1;
-    // O += P V over 4 k-steps of 16 keys
+    // O += P V over 4 k-steps of 16 keys, two 8-dim column groups per ldmatrix.trans
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
       const uint32_t a[4] = {pa[2 * ks][0], pa[2 * ks][1], pa[2 * ks + 1][0], pa[2 * ks + 1][1]};
 #pragma unroll
-      for (int nd = 0; nd < 4; ++nd) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sVt[nd * 8 + g][ks * 16 + 2 * tig]);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sVt[nd * 8 + g][ks * 16 + 8 + 2 * tig]);
-        mma16816(o[nd], a, b0, b1);
+      for (int p = 0; p < 2; ++p) {
+        uint32_t vf[4];
+        ldsm_x4_t(saddr(&sV[buf][ks * 16 + vrow][p * 16 + vcol]), vf);
+        mma16816(o[2 * p], a, vf[0], vf[1]);
+        mma16816(o[2 * p + 1], a, vf[2], vf[3]);
       }
     }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
   }
 #pragma unroll
   for (int x = 1; x <= 2; x <<= 1) {

@@ -74,6 +74,7 @@ struct GemmArgs {
   long long res_ld, res_img;  // elements between pixels; pixels between images
   void* out;
   int out_f32, out_vec;       // out_vec: rows 16-byte aligned (vector stores)
+  int out_v8;                 // rows 32-byte aligned: a lane stores whole 32-byte sectors
   long long out_ld, out_img;
   int act;                    // 0 none, 1 ReLU, 2 GELU (erf form)
   int bres;                   // weights resident: the CTA's whole B tile loaded once (see below)
@@ -326,7 +327,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < 16; ++t) f[t] = act_of(f[t], a.act);
         if (a.out_f32) {
           float* op = static_cast<float*>(a.out) + pix * a.out_ld + n0;
-          if (nv == 16 && a.out_vec) {
+          if (nv == 16 && a.out_v8) {
+#pragma unroll
+            for (int t = 0; t < 16; t += 8)
+              st_global_v8(op + t,
+                           make_uint4(__float_as_uint(f[t]), __float_as_uint(f[t + 1]), __float_as_uint(f[t + 2]),
+                                      __float_as_uint(f[t + 3])),
+                           make_uint4(__float_as_uint(f[t + 4]), __float_as_uint(f[t + 5]), __float_as_uint(f[t + 6]),
+                                      __float_as_uint(f[t + 7])));
+          } else if (nv == 16 && a.out_vec) {
 #pragma unroll
             for (int t = 0; t < 16; t += 4) *reinterpret_cast<float4*>(op + t) = make_float4(f[t], f[t + 1], f[t + 2], f[t + 3]);
           } else {
@@ -336,7 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else {
           __half* op = static_cast<__half*>(a.out) + pix * a.out_ld + n0;
-          if (nv == 16 && a.out_vec) {
+          if (nv == 16 && a.out_v8) {  // the chunk's 16 channels: one 32-byte sector
+            uint4 x[2];
+            __half2* h = reinterpret_cast<__half2*>(x);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) h[u] = __floats2half2_rn(f[2 * u], f[2 * u + 1]);
+            st_global_v8(op, x[0], x[1]);
+          } else if (nv == 16 && a.out_vec) {
 #pragma unroll
             for (int t = 0; t < 16; t += 8) {
               uint4 x;
@@ -484,6 +499,7 @@ extern "C" int sb_gemm_conv(const sb_gemm_src* src, int nsrc, int B, int H, int 
   a.res_f32 = res_dtype == SB_F32;
   a.res_vec = res && (res_ld * esz_r) % 16 == 0 && (reinterpret_cast<uintptr_t>(res) & 15) == 0;
   a.out_vec = (out_ld * esz_o) % 16 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  a.out_v8 = (out_ld * esz_o) % 32 == 0 && (reinterpret_cast<uintptr_t>(out) & 31) == 0;
   a.res_ld = res_ld;
   a.res_img = res_img;
   a.out = out;

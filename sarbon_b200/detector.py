@@ -158,7 +158,7 @@ class B200Detector:
                     qk=(wi[:2 * d].half().contiguous().to(dev), bi[:2 * d].float().contiguous().to(dev)),
                     v=(wi[2 * d:].half().contiguous().to(dev), bi[2 * d:].float().contiguous().to(dev)),
                     o=[t.to(dev) for t in _lin(sa.out_proj)],
-                    value=[t.to(dev) for t in _lin(cr.value_proj)],
+                    value=_lin(cr.value_proj),
                     offatt=(off_w.half().contiguous().to(dev), off_b.float().contiguous().to(dev)),
                     n_off=cr.offsets.out_features,
                     cout=[t.to(dev) for t in _lin(cr.out_proj)],
@@ -167,6 +167,11 @@ class B200Detector:
                        for n in (L.n1, L.n2, L.n3)]))
                 if cr.h != self.heads or cr.p != self.points or cr.l != 3:
                     raise NotImplementedError("MSDeformAttn with 3 levels and the config's heads / points")
+            # every layer's value projection reads the same memory: one GEMM with the layers'
+            # weights stacked along N (layer i's value = columns i*d .. (i+1)*d of its output)
+            vals = [w.pop("value") for w in self.w_layers]
+            self.w_value = (torch.cat([v[0] for v in vals], 0).contiguous().to(dev),
+                            torch.cat([v[1] for v in vals], 0).contiguous().to(dev))
             self.w_cls = [[t.to(dev) for t in _lin(h)] for h in det.cls_heads]
             self.w_pre = [[t.to(dev) for t in _lin(det.pre_box[i])] for i in (0, 2, 4)]
             self.w_corner = [[[t.to(dev) for t in _lin(h[i])] for i in (0, 2, 4)] for h in det.corner_heads]
@@ -233,7 +238,7 @@ class B200Detector:
         self.att_q = e(B, K, d, **f16)
         self.sa_q = e(B, K, d, **f16)
         self.qc16 = e(B, K, d, **f16)
-        self.value = e(B, S, d, **f16)
+        self.value = e(B, S, len(self.w_layers) * d, **f16)  # all layers' values of the memory
         n_oa = self.w_layers[0]["offatt"][0].shape[0]
         self.offatt = e(B, K, n_oa, **f16)
         self.samp = e(B, K, d, **f16)
@@ -345,6 +350,9 @@ class B200Detector:
         g = ops.gemm_conv
         rows = B * K
         cur = 0
+        # the deformable cross-attention's value projections of every layer, in one pass over
+        # the memory
+        g(self.mem.view(B * S, d), *self.w_value, out=self.value.view(B * S, -1))
         for i, w in enumerate(self.w_layers):
             tgt = self.tgt32[cur]
             # query position of the current boxes
@@ -360,12 +368,11 @@ class B200Detector:
             # the layer input tgt stays intact: the corner head of the next layer reads it
             ops.layernorm(tgt, n1[0], n1[1], n1[2], b=self.sa_q, y32=self.mid32, pos=self.pos, yp16=self.qc16)
             # deformable cross-attention on the memory
-            g(self.mem.view(B * S, d), *w["value"], out=self.value.view(B * S, d))
             g(self.qc16.view(rows, d), *w["offatt"], out=self.offatt.view(rows, -1))
             n_off = w["n_off"]
             ref = self.ref16 if i == 0 else self.box
-            ops.deform_sample(self.value, self.shapes, self.offatt[..., :n_off], self.offatt[..., n_off:], ref,
-                              self.heads, self.points, out=self.samp)
+            ops.deform_sample(self.value[..., i * d:(i + 1) * d], self.shapes, self.offatt[..., :n_off],
+                              self.offatt[..., n_off:], ref, self.heads, self.points, out=self.samp)
             g(self.samp.view(rows, d), *w["cout"], out=self.cross.view(rows, d))
             ops.layernorm(self.mid32, n2[0], n2[1], n2[2], b=self.cross, y32=self.mid32, y16=self.ffn_in)
             g(self.ffn_in.view(rows, d), *w["f1"], act="relu", out=self.ffn_q.view(rows, -1))

@@ -60,7 +60,9 @@ def test_dwconv_and_upsample(b, h, w, c):
     assert torch.equal(up, ref)
 
 
-@pytest.mark.parametrize("tq,tk,heads", [(300, 300, 8), (240, 240, 8), (2040, 2040, 8), (1, 77, 8), (130, 65, 4)])
+# (2341, 2333, 16): ragged query and key counts (37 CTAs x 16 heads x 2 images, 37 key tiles)
+@pytest.mark.parametrize("tq,tk,heads", [(300, 300, 8), (240, 240, 8), (2040, 2040, 8), (1, 77, 8), (130, 65, 4),
+                                         (2341, 2333, 16)])
 def test_attention(tq, tk, heads):
     from sarbon_b200 import det_ops as ops
     g = gen(tq + tk)
