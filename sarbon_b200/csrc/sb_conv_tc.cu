@@ -135,7 +135,7 @@ struct TcCfg {
   static constexpr int OBW = 8;                                    // staged box width (px)
   static constexpr int EPI_WARP_BYTES = TSTORE ? 32 * NCOL * 2 : 0;  // one warp's buffer
   static constexpr int EPI_BYTES = 8 * EPI_WARP_BYTES;
-  static constexpr int CRING = MANUAL ? 16 : 8;       // item-coordinate ring (producer -> epilogue)
+  static constexpr int CRING = MANUAL ? 32 : 8;       // item-coordinate ring (producer -> epilogue)
   static constexpr int CRING_BYTES = CRING * 8 * 4 * 4; // <= 8 units x (cam, row, col, pad) per item
   // first layer: the input window of one M-tile (BOX_ROWS output rows of one tile), loaded
   // by one 3-D TMA box from the image cache viewed as [N][H][W*CIN]; the box starts 8
@@ -145,7 +145,7 @@ struct TcCfg {
   static constexpr int WIN_COLS = ((8 + WIN_ELEMS + 7) / 8) * 8;     // box inner extent (elements)
   static constexpr int WIN_LEAD = 8 - CIN;                            // elements before the first used one
   static constexpr int WIN_BUF = ((WIN_ROWS * WIN_COLS * 2 + 127) / 128) * 128;
-  static constexpr int NWB = 8;                                       // window ring depth
+  static constexpr int NWB = 16;                                      // window ring depth
   static constexpr int NGW = 4;                                       // first layer: gather warps
   static constexpr int WIN_BYTES = MANUAL ? NWB * WIN_BUF : 0;
   // mbarriers (sized for the most stages that could fit) + TMEM address + abort flag
