@@ -1,7 +1,7 @@
 """Golden vectors for track-steered block masks, made by the reference's own code.
 
 Runs ``boxes_to_block_mask`` of ``sarbon/inference/video.py`` (video.py:26-34) of the
-reference checkout (path: first argument, default ``/root/reference``) on seeded random and
+reference checkout (its path is the first argument) on seeded random and
 hand-picked boxes and writes ``boxes/boxes_mask.npz`` next to this script.  The tests only
 read the ``.npz``; they never need the reference.
 
@@ -11,7 +11,7 @@ the reference's masks ``[N, hb, wb]``.  The boxes include the engine-pixel value
 loop produces (float32 track boxes divided by a float64 scale, video.py:145), coordinates
 on and next to block edges, outside the image, reversed, and huge.
 
-Usage: python tests/golden/make_boxes_golden.py [/path/to/reference]
+Usage: python tests/golden/make_boxes_golden.py /path/to/reference
 """
 import sys
 from pathlib import Path
@@ -19,7 +19,9 @@ from pathlib import Path
 import numpy as np
 
 OUT = Path(__file__).resolve().parent / "boxes"
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) < 2:
+    sys.exit("usage: make_boxes_golden.py /path/to/reference")
+REF = Path(sys.argv[1])
 sys.path.insert(0, str(REF))
 from sarbon.inference.video import boxes_to_block_mask  # noqa: E402
 

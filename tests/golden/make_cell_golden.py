@@ -1,7 +1,7 @@
 """Golden vectors for cell-level gating, made by the reference's own code.
 
-Runs ``sarbon/sparse/gating.py`` of the reference checkout (path: first argument, default
-``/root/reference``) on seeded random change masks and writes ``cells/cell_gating.npz`` next to
+Runs ``sarbon/sparse/gating.py`` of the reference checkout (its path is the first
+argument) on seeded random change masks and writes ``cells/cell_gating.npz`` next to
 this script.  The tests only read the ``.npz``; they never need the reference.
 
 For each case the fixture holds the change mask of c x c-pixel cells ``[N, Hc, Wc]`` and,
@@ -9,7 +9,7 @@ for every receptive radius of the Sarbon-S stem, the block mask of
 ``active_blocks_cell_level`` (cells dilated by ceil(R / c), then any-pooled into blocks,
 gating.py:42-43) and of ``active_blocks_block_level`` (gating.py:37-39).
 
-Usage: python tests/golden/make_cell_golden.py [/path/to/reference]
+Usage: python tests/golden/make_cell_golden.py /path/to/reference
 """
 import sys
 from pathlib import Path
@@ -18,7 +18,9 @@ import numpy as np
 import torch
 
 OUT = Path(__file__).resolve().parent / "cells"
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) < 2:
+    sys.exit("usage: make_cell_golden.py /path/to/reference")
+REF = Path(sys.argv[1])
 sys.path.insert(0, str(REF))
 from sarbon.sparse import gating  # noqa: E402
 
