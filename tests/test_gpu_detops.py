@@ -60,9 +60,11 @@ def test_dwconv_and_upsample(b, h, w, c):
     assert torch.equal(up, ref)
 
 
-# (2341, 2333, 16): ragged query and key counts (37 CTAs x 16 heads x 2 images, 37 key tiles)
+# (2341, 2333, 16): ragged query and key counts (37 CTAs x 16 heads x 2 images, 37 key tiles);
+# (5, 1, 8): one key, 63 masked slots of its tile; (70, 64, 8) one full key tile; (64, 129, 2)
+# a last tile with one key
 @pytest.mark.parametrize("tq,tk,heads", [(300, 300, 8), (240, 240, 8), (2040, 2040, 8), (1, 77, 8), (130, 65, 4),
-                                         (2341, 2333, 16)])
+                                         (2341, 2333, 16), (5, 1, 8), (70, 64, 8), (64, 129, 2)])
 def test_attention(tq, tk, heads):
     from sarbon_b200 import det_ops as ops
     g = gen(tq + tk)
