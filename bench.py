@@ -24,8 +24,8 @@ Arms:
 
 Multi-GPU (torchrun): streams are independent; each rank runs its own shard of the
 streams with no collective inside the timed region; the time is the max over ranks.
-Weak scaling (default): S streams per GPU.  Strong scaling (--total-streams T, e.g.
-64 streams of 1280x720 padded to 736 over 1/2/4/8 GPUs): the job's T
+Weak scaling (default): S streams per GPU.  Strong scaling (--total-streams T, e.g. a
+fixed job of 64 streams of 1280x720 padded to 736 rows over 1/2/4/8 GPUs): the job's T
 streams split contiguously over the ranks.
 """
 from __future__ import annotations
@@ -78,7 +78,8 @@ def parse():
     p.add_argument("--cell", type=int, default=0,
                    help="gate at cell level with this cell size (px; 0 = block level, the reference's rule)")
     p.add_argument("--fp8", nargs="?", const="s8", default=None, choices=["s8", "all"],
-                   help="e4m3 caches and weights (BASELINE config 5's weight format): in the stride-8 stage "
+                   help="e4m3 caches and per-output-channel e4m3 weights (the full-detection benchmark's weight "
+                        "format): in the stride-8 stage "
                         "(s8, SB_CREATE_FP8_S8) or in the stride-4 stage too (all)")
     p.add_argument("--cpu-seconds", type=float, default=20.0)
     p.add_argument("--no-reference-gpu", action="store_true",
@@ -88,7 +89,7 @@ def parse():
                    help="skip timing the detector after the stem (B200Detector vs the reference's own)")
     p.add_argument("--detector-iters", type=int, default=20)
     p.add_argument("--dec-layers", type=int, default=4,
-                   help="decoder layers of the detector (the 's' preset has 4; BASELINE config 5 asks for 6)")
+                   help="decoder layers of the detector (the 's' preset has 4; the full-detection benchmark uses 6)")
     return p.parse_args()
 
 

@@ -100,7 +100,7 @@ SB_API int sb_create(const sb_layer_desc* layers, int n_layers, int n_streams, i
  * per output channel (scale = max |w| / 448 of the channel, sb_layer_wscale), dequantised
  * in the fp32 epilogue (bias, residual, ReLU), then quantised to e4m3 again.  No reference
  * counterpart (the reference casts its tile weights to the engine dtype,
- * fused_engine.py:114): this is BASELINE config 5's weight format, applied where the layer's
+ * fused_engine.py:114): this is the full-detection benchmark's weight format, applied where the layer's
  * input is an e4m3 cache (it halves the tensor-core work and the weights). */
 #define SB_CREATE_FP8_S8 2
 /* SB_CREATE_FP8_S4: the same for the stride-4 stage (layers with out_stride == 4), except its

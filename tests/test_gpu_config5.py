@@ -1,8 +1,8 @@
-"""BASELINE config 5 on one GPU: the stem engine, then the DETR decoder (300 queries, 6 layers)
+"""The full-detection benchmark on one GPU: the stem engine, then the DETR decoder (300 queries, 6 layers)
 on its cached p8, against the fp16 reference.
 
 Reference: the reference's own detector, ``build("s", 6, halo_zero=False, dec_layers=6)``
-(sarbon/models/sarbon_det.py; the "s" preset has 4 decoder layers, config 5 asks for 6), with
+(sarbon/models/sarbon_det.py; the "s" preset has 4 decoder layers, the benchmark uses 6), with
 non-trivial BatchNorm statistics and heads, run as SarbonVideo runs it: the reference's own
 ``FusedSparseEngine`` (fp16, over ``stem_to_local(det.stem)``, video.py:58-64) steps the
 frames at the production threshold tau = 8 grey levels, then ``det(None, p8=p8)`` runs on
@@ -11,12 +11,12 @@ bench generator at ~3 % changed blocks; both engines step through the same 6 fra
 last frame is compared.
 
 * fp16 engine + B200Detector: p8 within 2e-3 relative RMS of the reference engine's, the
-  selected queries' scores (in selection order) within the north-star tolerance
+  selected queries' scores (in selection order) within
   |a - b| <= 1e-3 + 1e-2 |b| elementwise (the rows themselves may differ among equal fp16
   scores), and with the reference's query selection forced, boxes and class logits within
   the same tolerance.
 * e4m3 engine (``fp8="all"``: e4m3 activations and per-output-channel e4m3 weights in the
-  stride-4 and stride-8 stages; config 5's weight format) + B200Detector: e4m3 has no
+  stride-4 and stride-8 stages; the benchmark's weight format) + B200Detector: e4m3 has no
   reference implementation; measured against the fp16 reference (p8 relative RMS,
   selected-query overlap, box and score differences), the selected scores, boxes and class
   logits meet the same tolerance (measured here: p8 3.9 % RMS, boxes 6.8e-4 at most).
@@ -130,7 +130,8 @@ def test_config5_stem_and_decoder(ref_det, fp8):
     bad_box = (db > 1e-3 + 1e-2 * ref_out["pred_boxes"].float().abs()).float().mean().item()
     dl = (out["pred_logits"].float() - ref_out["pred_logits"].float()).abs()
     bad_log = (dl > 1e-3 + 1e-2 * ref_out["pred_logits"].float().abs()).float().mean().item()
-    print(f"\nconfig 5 ({'e4m3 stem' if fp8 else 'fp16 stem'}), changed blocks {sum(changed) / len(changed):.3f}: "
+    print(f"\nfull detection ({'e4m3 stem' if fp8 else 'fp16 stem'}), "
+          f"changed blocks {sum(changed) / len(changed):.3f}: "
           f"p8 rel RMS {p8_rms:.2e}; selected queries shared {shared:.3f}, their scores |d| max "
           f"{dv.max().item():.2e} (outside 1e-3 + 1e-2|b|: {bad_sel:.3f}); with the reference's selection: "
           f"|d box| max {db.max().item():.2e} p99 {db.flatten().quantile(0.99).item():.2e} median "

@@ -1,4 +1,4 @@
-"""GPU parity at the production gate setting and at BASELINE configs 2 and 4.
+"""GPU parity at the production gate setting and on a single 720p stream and on a shard of a 64-stream job.
 
 * gate band: on normalised fp16 camera frames at SarbonVideo's threshold
   (tau = 8/255 * 255 / mean(STD), video.py:63-64) the engine's change mask is compared
@@ -8,11 +8,11 @@
   The kernel decides by the exact sum; the two can only disagree for a block whose exact
   sum lies inside the fp32 rounding band of a 3072-term sum around the threshold.  Every
   disagreement is reported with its distance from the threshold and must lie in the band.
-* config 2: one 1280x720 stream padded to 1280x736 (920 blocks): change masks, dilated
+* one 1280x720 stream padded to 1280x736 (920 blocks): change masks, dilated
   masks, block lists and the image cache bit-exact against the oracle over a sequence;
   every layer elementwise (1e-2 rel / 1e-3 abs) against the oracle's conv of the engine's
   own input caches.
-* config 4: one shard of the 64-stream 1280x736 job (streams 16..31, the second of four
+* one shard of the 64-stream 1280x736 job (streams 16..31, the second of four
   GPUs) run as its own 16-stream engine equals the matching slice of one 64-stream engine
   bit for bit: caches, change masks, dilated masks and block lists.
 """

@@ -1,4 +1,4 @@
-"""Per-layer tile-conv numerics and the 1080p change-rate sweep (config 3).
+"""Per-layer tile-conv numerics and the 1080p change-rate sweep (16 x 1080p streams, 1-30 % changed blocks).
 
 * every layer of a dense pass equals a PyTorch fp32 conv (+bias, +residual, ReLU) of the
   engine's own input cache, within the fp16 tolerance (1e-2 rel / 1e-3 abs);

@@ -4,14 +4,14 @@ The reference is its own ``SarbonDetector`` (sarbon/models/sarbon_det.py, instal
 baseline/_ref), built as ``build("s", 6, halo_zero=False)`` with non-trivial BatchNorm
 statistics and affine parameters, randomised heads and sampling offsets, run as
 ``SarbonVideo._run_det`` runs it: ``det(None, p8=p8)`` under ``torch.autocast(float16)``
-(sarbon/inference/video.py:116-118).  Inputs: config 1's frame size (640x384 -> p8 48x80)
+(sarbon/inference/video.py:116-118).  Inputs: 640x384 frames (p8 48x80)
 and two images; 300 queries.
 
 * DenseCore's three output levels against ``det.core(p8)``;
 * the encoder's query selection against the reference's top-K (fraction of equal rows);
-* with the reference's selected rows forced (SURVEY's parity rule for the decoder: top-K
-  ties may order differently), the final boxes and class logits elementwise within
-  |a - b| <= 1e-3 + 1e-2 |b| (the north-star tolerance), and the identity embedding;
+* with the reference's selected rows forced (top-K ties may order differently, so the
+  decoder is compared on the same selection), the final boxes and class logits elementwise
+  within |a - b| <= 1e-3 + 1e-2 |b|, and the identity embedding;
 * the CUDA-graph replay equals the eager run bit for bit.
 """
 from pathlib import Path

@@ -7,8 +7,8 @@ interpreted Triton tile kernel for the active tiles) on normalised fp16 camera f
 SarbonVideo's threshold.  Each layer of the B200 engine is run alone
 (``FusedSparseEngine.dense_layers``) on the reference's input caches and compared,
 element by element, with the reference's output cache: 1e-2 relative / 1e-3 absolute,
-the north-star fp16 tolerance, with no allowance for depth (one fp32 accumulation and
-one fp16 rounding on each side).
+the fp16 tolerance, with no allowance for depth (one fp32 accumulation and one fp16
+rounding on each side).
 """
 import numpy as np
 import pytest
